@@ -1,0 +1,227 @@
+// Small kernels around the attention passes: field statistics, delta = rowsum(dO * O), the final combination of
+// the soft-min gradient of phi, and the batch/tile reduction of dbeta. All are deterministic (fixed summation order).
+#include "fpa_internal.h"
+
+namespace fpa {
+
+size_t stats_bytes(const Dims& d) {
+  size_t bh = size_t(d.BH());
+  return 4 * align256(bh * d.TP * sizeof(float)) + 2 * align256(bh * d.NB * sizeof(float));
+}
+
+size_t bwd_scratch_bytes(const Dims& d) {
+  size_t bh = size_t(d.BH());
+  return 4 * align256(bh * d.TP * sizeof(float)) + align256(bh * d.NB * d.NB * sizeof(float)) +
+         align256(bh * d.NB * sizeof(float));
+}
+
+static float* take(char*& p, size_t n_floats) {
+  float* r = reinterpret_cast<float*>(p);
+  p += align256(n_floats * sizeof(float));
+  return r;
+}
+
+Stats carve_stats(char* base, const Dims& d) {
+  size_t bh = size_t(d.BH());
+  Stats s;
+  s.pre = take(base, bh * d.TP);
+  s.suf = take(base, bh * d.TP);
+  s.prel = take(base, bh * d.TP);
+  s.sufl = take(base, bh * d.TP);
+  s.bmin = take(base, bh * d.NB);
+  s.bl = take(base, bh * d.NB);
+  return s;
+}
+
+BwdScratch carve_bwd(char* base, const Dims& d) {
+  size_t bh = size_t(d.BH());
+  BwdScratch s;
+  s.delta = take(base, bh * d.TP);
+  s.w = take(base, bh * d.TP);
+  s.dphi2 = take(base, bh * d.TP);
+  s.dphi4 = take(base, bh * d.TP);
+  s.tb = take(base, bh * d.NB * d.NB);
+  s.dbeta = take(base, bh * d.NB);
+  return s;
+}
+
+// One thread per (head, tile): sequential scans over the tile's BT positions (kernel.py:84-100).
+// It also clears the device status word of the call's workspace (the first launch of every call).
+__global__ void stats_kernel(const float* __restrict__ phi, int BH, int T, int BT, int NB, float il2, Stats st,
+                             int* status) {
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx == 0 && status) *status = 0;
+  if (idx >= BH * NB) return;
+  int z = idx / NB, j = idx % NB;
+  const float* ph = phi + size_t(z) * T;
+  size_t TP = size_t(NB) * BT;
+  size_t base = size_t(z) * TP + size_t(j) * BT;
+  int t0 = j * BT;
+  float mn = kInf, l = -kInf;
+  for (int k = 0; k < BT; ++k) {
+    int t = t0 + k;
+    float p = t < T ? ph[t] : kInf;
+    float a = t < T ? -p * il2 : -kInf;
+    mn = fminf(mn, p);
+    l = lse2(l, a);
+    st.pre[base + k] = mn;
+    st.prel[base + k] = l;
+  }
+  st.bmin[size_t(z) * NB + j] = mn;
+  st.bl[size_t(z) * NB + j] = l;
+  mn = kInf;
+  l = -kInf;
+  for (int k = BT - 1; k >= 0; --k) {
+    st.suf[base + k] = mn;  // over (t, tile end]
+    st.sufl[base + k] = l;
+    int t = t0 + k;
+    float p = t < T ? ph[t] : kInf;
+    float a = t < T ? -p * il2 : -kInf;
+    mn = fminf(mn, p);
+    l = lse2(l, a);
+  }
+}
+
+cudaError_t launch_stats(const float* phi, const Dims& d, float tau, const Stats& st, int* status, cudaStream_t s) {
+  int n = d.BH() * d.NB;
+  stats_kernel<<<(n + 127) / 128, 128, 0, s>>>(phi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, status);
+  return cudaGetLastError();
+}
+
+// delta_t = sum_d dO[t, d] * O[t, d] in float32 (kernel.py:166-174). One warp per row.
+template <typename TIn>
+__global__ void delta_kernel(const TIn* __restrict__ o, Str4 so, const TIn* __restrict__ dout, Str4 sdo, int H,
+                             int T, int D, int TP, int rows, float* __restrict__ delta) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  int z = warp / T, t = warp % T, b = z / H, h = z % H;
+  const TIn* op = o + b * so.b + h * so.h + int64_t(t) * so.t;
+  const TIn* dp = dout + b * sdo.b + h * sdo.h + int64_t(t) * sdo.t;
+  float acc = 0.f;
+  for (int c = lane; c < D; c += 32) acc += to_f32(op[c * so.d]) * to_f32(dp[c * sdo.d]);
+  acc = group_sum<32>(acc);
+  if (lane == 0) delta[size_t(z) * TP + t] = acc;
+}
+
+cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
+                         cudaStream_t s) {
+  int rows = d.BH() * d.T;
+  int blocks = (rows * 32 + 255) / 256;
+  if (dtype == FPA_DTYPE_F16)
+    delta_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)o, so, (const __half*)dout, sdo, d.H, d.T, d.D,
+                                                d.TP, rows, delta);
+  else
+    delta_kernel<float><<<blocks, 256, 0, s>>>((const float*)o, so, (const float*)dout, sdo, d.H, d.T, d.D, d.TP,
+                                               rows, delta);
+  return cudaGetLastError();
+}
+
+// Deterministic block sum of one value per thread (blockDim.x a multiple of 32, at most 1024). All threads must call.
+__device__ float block_sum(float v, float* red) {
+  v = group_sum<32>(v);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = 0.f;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < nw; ++w) r += red[w];
+  return r;  // valid in thread 0
+}
+
+// Final soft-min gradient of phi for tile U of head z (kernel.py:344-370 combines the same four parts):
+//   part1_u = sum_{s<u in U, SUF_s<inf} 2^{a2_u - c_s} W_s            (u in the key's tile)
+//   dphi2_u                                                            (u in the query's tile)
+//   dphi4_u                                                            (u in the diagonal tile with both)
+//   part3_u = 2^{a2_u - c_U} sum_{j<U<i} 2^{c_U - cmid_ij} TB[i][j]     (u in a tile strictly between)
+// dphi_u = beta * (part1 + dphi2 + dphi4 + part3). Block: BT threads (one per position of the tile).
+__global__ void dphi_kernel(const float* __restrict__ phi, const float* __restrict__ beta, int H, int T, int BT,
+                            int NB, float il2, Stats st, BwdScratch sc, float* __restrict__ dphi) {
+  extern __shared__ float sm[];
+  float* cb = sm;           // [NB] max of a2 per tile
+  float* A = cb + NB;       // [NB] A[j] = max cb over (j, U]
+  float* Bv = A + NB;       // [NB] B[i] = max cb over [U, i)
+  float* Ws = Bv + NB;      // [BT]
+  float* c2s = Ws + BT;     // [BT]
+  float* red = c2s + BT;    // [32]
+  const int U = blockIdx.x, z = blockIdx.y, h = z % H;
+  const int tid = threadIdx.x;
+  const size_t TP = size_t(NB) * BT;
+  for (int n = tid; n < NB; n += blockDim.x) cb[n] = -st.bmin[size_t(z) * NB + n] * il2;
+  const int u = U * BT + tid;
+  {
+    float w = 0.f, c2 = -kInf;
+    if (tid < BT) {
+      float suf = st.suf[size_t(z) * TP + u];
+      c2 = suf < kInf ? -suf * il2 : -kInf;
+      w = sc.w[size_t(z) * TP + u];
+      Ws[tid] = w;
+      c2s[tid] = c2;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = -kInf;
+    for (int j = U - 1; j >= 0; --j) {  // A[j] = max cb over tiles j+1 .. U
+      m = fmaxf(m, cb[j + 1]);
+      A[j] = m;
+    }
+    m = -kInf;
+    for (int i = U + 1; i < NB; ++i) {  // B[i] = max cb over tiles U .. i-1
+      m = fmaxf(m, cb[i - 1]);
+      Bv[i] = m;
+    }
+  }
+  __syncthreads();
+  // part3 partial sums: thread handles query tiles i = U+1+tid, U+1+tid+blockDim, ...
+  float s3 = 0.f;
+  if (U > 0 && U < NB - 1) {
+    const float cU = cb[U];
+    for (int i = U + 1 + tid; i < NB; i += blockDim.x) {
+      const float* row = sc.tb + (size_t(z) * NB + i) * NB;
+      for (int j = 0; j < U; ++j) s3 += exp2f(cU - fmaxf(A[j], Bv[i])) * row[j];
+    }
+  }
+  float S = block_sum(s3, red);
+  if (tid == 0) red[0] = S;
+  __syncthreads();
+  S = red[0];
+  if (tid < BT && u < T) {
+    float a2 = -phi[size_t(z) * T + u] * il2;
+    float part1 = 0.f;
+    for (int s = 0; s < tid; ++s)
+      if (c2s[s] > -kInf) part1 += exp2f(a2 - c2s[s]) * Ws[s];
+    float part3 = (U > 0 && U < NB - 1) ? exp2f(a2 - cb[U]) * S : 0.f;
+    size_t p = size_t(z) * TP + u;
+    dphi[size_t(z) * T + u] = beta[h] * (part1 + sc.dphi2[p] + sc.dphi4[p] + part3);
+  }
+}
+
+cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
+                        const BwdScratch& sc, float* dphi, cudaStream_t s) {
+  int threads = d.BT < 32 ? 32 : d.BT;
+  size_t smem = (3 * size_t(d.NB) + 2 * d.BT + 32) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+  }
+  dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc, dphi);
+  return cudaGetLastError();
+}
+
+// dbeta_h = sum over batch b and key tiles j of the per-tile partials, in a fixed order (kernel.py:450).
+__global__ void dbeta_kernel(int B, int H, int NB, const float* __restrict__ part, float* __restrict__ dbeta) {
+  int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  float acc = 0.f;
+  for (int b = 0; b < B; ++b)
+    for (int j = 0; j < NB; ++j) acc += part[(size_t(b) * H + h) * NB + j];
+  dbeta[h] = acc;
+}
+
+cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s) {
+  dbeta_kernel<<<(d.H + 63) / 64, 64, 0, s>>>(d.B, d.H, d.NB, sc.dbeta, dbeta);
+  return cudaGetLastError();
+}
+
+}  // namespace fpa

@@ -1,0 +1,72 @@
+// Shared device helpers and the workspace layout of the FPA kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/fpa.h"
+
+namespace fpa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kInf = __builtin_huge_valf();
+
+// Device status word at the head of every workspace (see fpa_workspace_status). The first 256 bytes of a
+// workspace are reserved for it so that the per-head arrays that follow stay 256-byte aligned.
+constexpr size_t kStatusBytes = 256;
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// log2(2^a + 2^b), with -inf + -inf = -inf (the stable base-2 log-add-exp of kernel.py:73-75).
+__device__ __forceinline__ float lse2(float a, float b) {
+  float m = fmaxf(a, b);
+  if (m == -kInf) return m;
+  return m + log2f(1.0f + exp2f(fminf(a, b) - m));
+}
+
+// Sum over the `W` consecutive lanes of a group (W a power of two <= 32, groups aligned). Every lane of the group
+// gets the bit-identical result: the butterfly pairs lanes symmetrically and float addition commutes.
+template <int W>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Per-tile statistics of the field phi, for tiles of BT positions (kernel.py:84-100 computes the same quantities):
+//   PRE_t  = min phi over [tile start, t]                      PREL_t = log2 sum 2^{a2} over [tile start, t]
+//   SUF_s  = min phi over (s, tile end] (inf if empty)         SUFL_s = log2 sum 2^{a2} over (s, tile end]
+//   BMIN_j = min phi over tile j                               BL_j   = log2 sum 2^{a2} over tile j
+// with a2 = -phi * log2(e) / tau. Positions >= T are excluded (phi = +inf, a2 = -inf there).
+struct Stats {
+  float* pre;   // [BH][TP]
+  float* suf;   // [BH][TP]
+  float* prel;  // [BH][TP]
+  float* sufl;  // [BH][TP]
+  float* bmin;  // [BH][NB]
+  float* bl;    // [BH][NB]
+};
+
+// Scratch of the backward pass (all float32, per head z = b*H + h).
+struct BwdScratch {
+  float* delta;  // [BH][TP]   rowsum(dO * O)
+  float* w;      // [BH][TP]   soft-min partial sums per key, normalised by 2^{c_s} (part "key tile")
+  float* dphi2;  // [BH][TP]   soft-min contribution of u in the query's tile
+  float* dphi4;  // [BH][TP]   soft-min contribution of u in the diagonal tile
+  float* tb;     // [BH][NB][NB] tile-pair totals, normalised by 2^{cmid}
+  float* dbeta;  // [BH][NB]   dbeta partial per key tile
+};
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Bounded-wait failure reporting: a kernel whose wait expires stores this code (first writer wins) and returns.
+__device__ __forceinline__ void report_timeout(int* status, int where) {
+  if (status) atomicCAS(status, 0, (FPA_ERR_TIMEOUT << 16) | (where & 0xffff));
+}
+
+}  // namespace fpa

@@ -1,0 +1,49 @@
+// Host-side launchers shared between the translation units of libfpa_b200 (not part of the public ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fpa_common.cuh"
+
+namespace fpa {
+
+struct Str4 {
+  int64_t b, h, t, d;
+};
+
+inline Str4 str4(const int64_t s[4]) { return Str4{s[0], s[1], s[2], s[3]}; }
+
+// Sizes shared by every kernel of one call. Tiles are BT positions; NB = ceil(T / BT); TP = NB * BT.
+struct Dims {
+  int B, H, T, D, BT, NB, TP;
+  int BH() const { return B * H; }
+};
+
+inline Dims make_dims(int B, int H, int T, int D, int BT) {
+  Dims d{B, H, T, D, BT, (T + BT - 1) / BT, 0};
+  d.TP = d.NB * BT;
+  return d;
+}
+
+// Workspace carving (all arrays 256-byte aligned, after the 256-byte status word).
+size_t stats_bytes(const Dims& d);
+size_t bwd_scratch_bytes(const Dims& d);
+Stats carve_stats(char* base, const Dims& d);
+BwdScratch carve_bwd(char* base, const Dims& d);
+
+// fpa_aux.cu
+cudaError_t launch_stats(const float* phi, const Dims& d, float tau, const Stats& st, int* status, cudaStream_t s);
+cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
+                         cudaStream_t s);
+cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
+                        const BwdScratch& sc, float* dphi, cudaStream_t s);
+cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s);
+
+// fpa_simt.cu (FFMA kernels, tiles of 64 positions, any supported D, fp16 or fp32 inputs)
+constexpr int kSimtBT = 64;
+cudaError_t simt_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s);
+cudaError_t simt_bwd_kv(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
+cudaError_t simt_bwd_q(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
+
+}  // namespace fpa

@@ -1,0 +1,134 @@
+/*
+ * fpa.h -- C ABI of the B200-native First Passage Attention (FPA) operator.
+ *
+ * FPA is causal softmax attention with the first-passage bias
+ *     b_ts = beta_h * min(0, min_{s<u<=t} phi_u - psi_s),   b_tt = 0,
+ * whose backward pass takes the gradient of phi through the soft minimum -tau*log sum_{s<u<=t} exp(-phi_u/tau).
+ *
+ * The library (libfpa_b200.so) is plain C at its boundary: device pointers, element strides, sizes and a
+ * cudaStream_t (passed as void*). It never allocates or frees device memory and never synchronises the stream;
+ * callers allocate the outputs and a workspace of the size the *_workspace_bytes queries return. All entry points
+ * are asynchronous on the given stream and reentrant.
+ *
+ * The entry points replace the reference implementation's device launches (yliu-fort/first-passage-attention):
+ *   fpa_fwd  <- kernel.py:398-412 (`_forward`: `_block_stats` -> `_stats`, then `_fwd`)
+ *   fpa_bwd  <- kernel.py:424-451 (`_FirstPassageAttention.backward`: `_bwd_delta`, `_bwd_kv`,
+ *               `_bwd_dphi_diag`, `_bwd_q`, `_bwd_dphi`, and the host-side `dbeta.sum((0, 2))`)
+ * The argument checks mirror kernel.py:469-488 (see fpa_status_string for the messages).
+ */
+#ifndef FPA_B200_H
+#define FPA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FPA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FPA_API __attribute__((visibility("default")))
+#else
+#define FPA_API
+#endif
+
+/* Element type of q, k, v, o, do, dq, dk, dv (kernel.py:471: all fp16 or all fp32). phi, psi, beta, lse, dphi,
+ * dpsi and dbeta are always float32. */
+enum FpaDtype { FPA_DTYPE_F16 = 0, FPA_DTYPE_F32 = 1 };
+
+/* Which kernels to run. AUTO picks the tensor-core (tcgen05) kernels for fp16 and the FFMA kernels for fp32. */
+enum FpaPath { FPA_PATH_AUTO = 0, FPA_PATH_SIMT = 1, FPA_PATH_TENSOR = 2 };
+
+enum FpaStatus {
+  FPA_OK = 0,
+  FPA_ERR_INVALID_ARGUMENT = 1, /* shapes, dtypes, null pointers, tau <= 0 (kernel.py:469-486) */
+  FPA_ERR_UNSUPPORTED = 2,      /* a valid request that the selected kernels do not cover (e.g. layout for TMA) */
+  FPA_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed (launch error, attribute, tensor map) */
+  FPA_ERR_TIMEOUT = 4,          /* a bounded device-side wait expired; reported through fpa_workspace_status */
+  FPA_ERR_WORKSPACE = 5         /* workspace pointer null, misaligned (256 B) or smaller than required */
+};
+
+/* Forward: o = softmax(q k^T / sqrt(D) + bias, causal) v, and lse_t = log2 sum_s exp2(scaled logits), the row
+ * statistic the backward pass needs. q, k, v, o: [B, H, T, D] with arbitrary element strides (stride[3] must be 1
+ * for the tensor-core path); phi, psi, lse: [B, H, T] contiguous float32; beta: [H] float32. */
+typedef struct FpaFwdArgs {
+  int32_t dtype;            /* FpaDtype */
+  int32_t path;             /* FpaPath */
+  int32_t B, H, T, D;       /* D in {16, 32, 64, 128, 256} (kernel.py:476: a power of two >= 16) */
+  float tau;                /* soft-min temperature, > 0 (enters only the backward pass) */
+  const void* q; int64_t q_stride[4];
+  const void* k; int64_t k_stride[4];
+  const void* v; int64_t v_stride[4];
+  const float* phi;         /* [B, H, T] */
+  const float* psi;         /* [B, H, T] */
+  const float* beta;        /* [H] */
+  void* o; int64_t o_stride[4];
+  float* lse;               /* [B, H, T], base-2 log-sum-exp of the log2e-scaled logits */
+  void* workspace;          /* fpa_fwd_workspace_bytes(...) bytes, 256-byte aligned */
+  size_t workspace_bytes;
+  int32_t kernels_launched; /* out: number of kernels this call launched */
+  int32_t path_taken;       /* out: FPA_PATH_SIMT or FPA_PATH_TENSOR */
+} FpaFwdArgs;
+
+/* Backward of sum(o * do): dq, dk, dv in the input dtype ([B, H, T, D], arbitrary strides), dphi and dpsi
+ * [B, H, T] float32 contiguous, dbeta [H] float32 summed over the batch (kernel.py:450). Deterministic: repeated
+ * calls on the same inputs give bit-identical results (no floating-point atomics). */
+typedef struct FpaBwdArgs {
+  int32_t dtype;
+  int32_t path;
+  int32_t B, H, T, D;
+  float tau;
+  const void* q; int64_t q_stride[4];
+  const void* k; int64_t k_stride[4];
+  const void* v; int64_t v_stride[4];
+  const void* o; int64_t o_stride[4];
+  const void* dout; int64_t dout_stride[4];
+  const float* lse;         /* as written by fpa_fwd */
+  const float* phi;
+  const float* psi;
+  const float* beta;
+  void* dq; int64_t dq_stride[4];
+  void* dk; int64_t dk_stride[4];
+  void* dv; int64_t dv_stride[4];
+  float* dphi;              /* [B, H, T] */
+  float* dpsi;              /* [B, H, T] */
+  float* dbeta;             /* [H] */
+  void* workspace;          /* fpa_bwd_workspace_bytes(...) bytes, 256-byte aligned */
+  size_t workspace_bytes;
+  int32_t kernels_launched; /* out */
+  int32_t path_taken;       /* out */
+} FpaBwdArgs;
+
+/* ABI version of the loaded library (FPA_ABI_VERSION). */
+FPA_API int fpa_abi_version(void);
+
+/* sizeof(FpaFwdArgs) for which == 0, sizeof(FpaBwdArgs) for which == 1; lets bindings check their struct mirror. */
+FPA_API size_t fpa_struct_size(int which);
+
+/* Workspace sizes in bytes for a call with these sizes (0 for invalid sizes). */
+FPA_API size_t fpa_fwd_workspace_bytes(int dtype, int B, int H, int T, int D, int path);
+FPA_API size_t fpa_bwd_workspace_bytes(int dtype, int B, int H, int T, int D, int path);
+
+/* Forward pass (replaces kernel.py:398-412). Returns an FpaStatus. */
+FPA_API int fpa_fwd(FpaFwdArgs* args, void* stream);
+
+/* Backward pass (replaces kernel.py:424-451). Returns an FpaStatus. */
+FPA_API int fpa_bwd(FpaBwdArgs* args, void* stream);
+
+/* Synchronises `stream`, then reads and clears the device status word at the head of a workspace that a previous
+ * fpa_fwd / fpa_bwd call used: FPA_OK, or FPA_ERR_TIMEOUT if a bounded device-side wait expired in that call. */
+FPA_API int fpa_workspace_status(void* workspace, void* stream);
+
+/* Human-readable text for an FpaStatus, or the message of the last argument error on this thread. */
+FPA_API const char* fpa_status_string(int status);
+
+/* The message of the last error raised on the calling thread (empty string when none). */
+FPA_API const char* fpa_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FPA_B200_H */

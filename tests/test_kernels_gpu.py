@@ -1,0 +1,224 @@
+"""Parity of the native CUDA kernels with the CPU oracle and with the reference's golden vectors.
+
+Tolerances are the reference's (test.py:19-20, README.md:49): max relative error (max|x - ref| / max|ref|)
+2e-3 in fp16 (1e-2 for dbeta) and 2e-4 in fp32, against the float64 definition."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from first_passage_attention_b200 import FirstPassageAttention, LaunchStats, first_passage_attention
+from first_passage_attention_b200 import _lib
+from oracle import fpa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+NAMES = ("o", "dq", "dk", "dv", "dphi", "dpsi", "dbeta")
+TOL = {torch.float16: 2e-3, torch.float32: 2e-4}
+TOL_DBETA_FP16 = 1e-2
+PATHS = {"auto": _lib.PATH_AUTO, "simt": _lib.PATH_SIMT}
+
+
+def need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+
+
+def make_inputs(B, H, T, D, phi_scale=1.0, ties=False, seed=0, dtype=torch.float16):
+    """test.py:108-117 (CPU tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(B, H, T, D, generator=g).to(dtype) for _ in range(3))
+    phi = torch.randn(B, H, T, generator=g).cumsum(-1) * phi_scale
+    if ties:
+        phi = torch.round(phi)
+    psi = phi + 0.5 * torch.randn(B, H, T, generator=g)
+    beta = torch.rand(H, generator=g) + 0.5
+    do = torch.randn(B, H, T, D, generator=g).to(dtype)
+    return q, k, v, phi, psi, beta, do
+
+
+def run_kernel(q, k, v, phi, psi, beta, do, tau=1.0, path="auto"):
+    os.environ["FPA_B200_PATH"] = path
+    try:
+        a = [t.cuda().clone().requires_grad_() for t in (q, k, v, phi, psi, beta)]
+        o = first_passage_attention(*a, tau=tau, impl="triton")
+        grads = torch.autograd.grad(o, a, do.cuda())
+        torch.cuda.synchronize()
+        return [o.detach().cpu()] + [x.cpu() for x in grads]
+    finally:
+        os.environ.pop("FPA_B200_PATH", None)
+
+
+def run_oracle(q, k, v, phi, psi, beta, do, tau=1.0):
+    n = [t.double().numpy() for t in (q, k, v, phi, psi, beta, do)]
+    o, _ = O.forward(*n[:6])
+    return [o] + list(O.backward(*n, tau=tau))
+
+
+def check(kern, ref, dtype, tol=None):
+    for name, x, r in zip(NAMES, kern, ref):
+        want = dtype if name in ("o", "dq", "dk", "dv") else torch.float32
+        assert x.dtype == want, name
+        assert torch.isfinite(x).all(), name
+        t = tol or (TOL_DBETA_FP16 if (name == "dbeta" and dtype == torch.float16) else TOL[dtype])
+        err = O.rel_err(x.double().numpy(), r)
+        assert err <= t, (name, err)
+
+
+# test.py:134-147, all sizes (the reference marks the last four GPU-only).
+CASES = [
+    (1, 2, 64, 64, 32, 1.0, False, torch.float16, 100),
+    (2, 3, 100, 64, 32, 1.0, False, torch.float16, 101),
+    (1, 2, 128, 64, 64, 1.0, False, torch.float16, 102),
+    (1, 2, 96, 64, 32, 40.0, False, torch.float16, 103),
+    (1, 2, 96, 64, 32, 1.0, True, torch.float16, 104),
+    (1, 2, 80, 32, 16, 1.0, False, torch.float16, 110),
+    (1, 2, 100, 64, 32, 1.0, False, torch.float32, 111),
+    (1, 2, 96, 16, 16, 40.0, False, torch.float32, 112),
+    (2, 4, 512, 64, 64, 1.0, False, torch.float16, 105),
+    (1, 2, 2048, 64, 64, 1.0, False, torch.float16, 106),
+    (1, 2, 2048, 64, 32, 1.0, False, torch.float32, 200),
+    (1, 2, 1000, 64, 32, 40.0, False, torch.float32, 201),
+]
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+@pytest.mark.parametrize("B,H,T,D,block,scale,ties,dtype,seed", CASES)
+def test_kernel_matches_the_oracle(B, H, T, D, block, scale, ties, dtype, seed, path):
+    need_gpu()
+    inp = make_inputs(B, H, T, D, scale, ties, seed=seed, dtype=dtype)
+    check(run_kernel(*inp, path=path), run_oracle(*inp), dtype)
+
+
+@pytest.mark.parametrize("name", sorted(f[:-4] for f in os.listdir(GOLDEN) if f.startswith(("t", "config1"))))
+def test_kernel_matches_the_reference_golden(name):
+    """Outputs of the reference implementation itself (tests/golden/make_golden.py)."""
+    need_gpu()
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    dtype = torch.float16 if str(z["dtype"]) == "f16" else torch.float32
+    inp = [torch.from_numpy(z[n]) for n in ("q", "k", "v", "phi", "psi", "beta", "do")]
+    inp = [x.to(dtype) if n in ("q", "k", "v", "do") else x for n, x in zip("qkvabcd", inp)]
+    kern = run_kernel(*inp, tau=float(z["tau"]))
+    check(kern, [z[n] for n in NAMES], dtype)
+
+
+def test_kernel_temperature():
+    """test.py:162-167."""
+    need_gpu()
+    inp = make_inputs(1, 2, 72, 32, seed=11, dtype=torch.float32)
+    check(run_kernel(*inp, tau=0.25), run_oracle(*inp, tau=0.25), torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_kernel_deterministic(dtype):
+    """test.py:170-174: two runs are bit-identical."""
+    need_gpu()
+    inp = make_inputs(2, 2, 300, 32, seed=12, dtype=dtype)
+    runs = [run_kernel(*inp) for _ in range(2)]
+    assert all(torch.equal(x, y) for x, y in zip(*runs))
+
+
+def config3_inputs(D, dtype, seed):
+    """Benchmark configuration 3: B2 H8 T1000; phi = cumsum N(-0.05, 1); psi = phi + N(0,1); beta = softplus(N)."""
+    g = torch.Generator().manual_seed(seed)
+    B, H, T = 2, 8, 1000
+    q, k, v = (torch.randn(B, H, T, D, generator=g).to(dtype) for _ in range(3))
+    phi = (torch.randn(B, H, T, generator=g) - 0.05).cumsum(-1)
+    psi = phi + torch.randn(B, H, T, generator=g)
+    beta = torch.nn.functional.softplus(torch.randn(H, generator=g))
+    do = torch.randn(B, H, T, D, generator=g).to(dtype)
+    return q, k, v, phi, psi, beta, do
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [16, 32, 128, 256])
+def test_config3_edge_coverage(D, dtype):
+    need_gpu()
+    inp = config3_inputs(D, dtype, seed=D)
+    kern = run_kernel(*inp)
+    check(kern, run_oracle(*inp), dtype)
+    again = run_kernel(*inp)
+    assert all(torch.equal(x, y) for x, y in zip(kern, again))
+
+
+@pytest.mark.parametrize("T", [1, 2, 63, 64, 65, 127, 129])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_ragged_and_tiny_lengths(T, dtype):
+    need_gpu()
+    inp = make_inputs(1, 3, T, 64, seed=300 + T, dtype=dtype)
+    check(run_kernel(*inp), run_oracle(*inp), dtype)
+
+
+def test_negative_and_scalar_beta():
+    """beta is a free parameter of the operator: a negative strength flips the bias sign (kernel.py:478-484)."""
+    need_gpu()
+    q, k, v, phi, psi, beta, do = make_inputs(1, 3, 200, 32, seed=41, dtype=torch.float32)
+    beta = torch.tensor([-0.7, 0.0, 1.3])
+    check(run_kernel(q, k, v, phi, psi, beta, do), run_oracle(q, k, v, phi, psi, beta, do), torch.float32)
+
+
+def test_strided_qkv_views():
+    """The layer's permuted views of the fused projection (kernel.py:527) are read in place."""
+    need_gpu()
+    B, T, H, D = 2, 130, 4, 32
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn(B, T, 3, H, D, generator=g).half()
+    q, k, v = qkv.permute(2, 0, 3, 1, 4)
+    _, _, _, phi, psi, beta, do = make_inputs(B, H, T, D, seed=6)
+    check(run_kernel(q, k, v, phi, psi, beta, do), run_oracle(q, k, v, phi, psi, beta, do), torch.float16)
+
+
+def test_long_context_prefix():
+    """Configuration 4 (B1 H16 T16383 D128 fp16) at full size. With do = 0 beyond T0 every output and gradient of
+    the first T0 positions equals that of the truncated problem (the operator is causal), so the full-size run is
+    checked against the oracle on the prefix; the rest of o is checked for finiteness."""
+    need_gpu()
+    B, H, T, D, T0 = 1, 16, 16383, 128, 640
+    g = torch.Generator().manual_seed(0)
+    q, k, v = ((0.5 * torch.randn(B, H, T, D, generator=g)).half() for _ in range(3))
+    phi = torch.randn(B, H, T, generator=g).cumsum(-1)
+    psi = phi + 2 * torch.randn(B, H, T, generator=g)
+    beta = 2 * torch.ones(H)
+    do = torch.randn(B, H, T, D, generator=g).half()
+    do[:, :, T0:] = 0
+    kern = run_kernel(q, k, v, phi, psi, beta, do)
+    assert torch.isfinite(kern[0]).all()
+    heads = [0, 7, 15]
+    pre = [x[:, heads, :T0] for x in (q, k, v, phi, psi)] + [beta[heads], do[:, heads, :T0]]
+    ref = run_oracle(*pre)
+    got = [kern[0][:, heads, :T0], kern[1][:, heads, :T0], kern[2][:, heads, :T0], kern[3][:, heads, :T0],
+           kern[4][:, heads, :T0], kern[5][:, heads, :T0], kern[6][heads]]
+    check(got, ref, torch.float16)
+    for x in kern[1:6]:  # dq, dk, dv, dphi, dpsi vanish exactly where do (and so dS) is zero
+        assert torch.count_nonzero(x[:, :, T0:]) == 0
+
+
+@pytest.mark.parametrize("amp", [False, True])
+def test_layer_kernel_matches_the_reference(amp):
+    """test.py:200-214: the layer on the native kernels against the layer on the PyTorch definition."""
+    need_gpu()
+    out = []
+    for impl in ("triton", "reference"):
+        torch.manual_seed(0)
+        layer = FirstPassageAttention(64, 4, impl=impl).cuda()
+        x = torch.randn(2, 50, 64, generator=torch.Generator().manual_seed(1)).cuda()
+        with torch.autocast("cuda", dtype=torch.float16, enabled=amp):
+            y = layer(x)
+        loss = y.float().square().mean()
+        out.append([y.detach().float()] + list(torch.autograd.grad(loss, list(layer.parameters()))))
+    tol = 5e-3 if amp else 1e-4
+    for a, b in zip(*out):
+        assert ((a - b).norm() / b.norm()).item() <= tol
+
+
+def test_native_library_is_what_ran():
+    """The CUDA path runs the in-tree libfpa_b200.so and counts its launches; nothing falls back."""
+    need_gpu()
+    LaunchStats.reset()
+    inp = make_inputs(1, 2, 256, 64, seed=9)
+    run_kernel(*inp)
+    assert LaunchStats.fwd_calls == 1 and LaunchStats.bwd_calls == 1 and LaunchStats.kernels >= 4
+    maps = open("/proc/self/maps").read()
+    assert _lib.LIB_PATH in maps
