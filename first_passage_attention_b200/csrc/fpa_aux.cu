@@ -45,10 +45,22 @@ BwdScratch carve_bwd(char* base, const Dims& d) {
   return s;
 }
 
+size_t keycols_bytes(const Dims& d) { return 3 * align256(size_t(d.BH()) * d.TP * sizeof(float)); }
+
+KeyCols carve_keycols(char* base, const Dims& d) {
+  size_t n = size_t(d.BH()) * d.TP;
+  KeyCols c;
+  c.a = take(base, n);
+  c.psi = take(base, n);
+  c.phi = take(base, n);
+  return c;
+}
+
 // One thread per (head, tile): sequential scans over the tile's BT positions (kernel.py:84-100).
-// It also clears the device status word of the call's workspace (the first launch of every call).
-__global__ void stats_kernel(const float* __restrict__ phi, int BH, int T, int BT, int NB, float il2, Stats st,
-                             int* status) {
+// It also clears the device status word of the call's workspace (the first launch of every call), and, when
+// `cols.a` is set, writes the per-key vectors of the tensor-core forward.
+__global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
+                             int NB, float il2, Stats st, KeyCols cols, int* status) {
   int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx == 0 && status) *status = 0;
   if (idx >= BH * NB) return;
@@ -71,20 +83,28 @@ __global__ void stats_kernel(const float* __restrict__ phi, int BH, int T, int B
   st.bl[size_t(z) * NB + j] = l;
   mn = kInf;
   l = -kInf;
+  const float* ps = psi + size_t(z) * T;
   for (int k = BT - 1; k >= 0; --k) {
     st.suf[base + k] = mn;  // over (t, tile end]
     st.sufl[base + k] = l;
     int t = t0 + k;
     float p = t < T ? ph[t] : kInf;
+    if (cols.a) {
+      float y = t < T ? ps[t] : 0.f;
+      cols.a[base + k] = fminf(mn - y, 0.f);
+      cols.psi[base + k] = y;
+      cols.phi[base + k] = p;
+    }
     float a = t < T ? -p * il2 : -kInf;
     mn = fminf(mn, p);
     l = lse2(l, a);
   }
 }
 
-cudaError_t launch_stats(const float* phi, const Dims& d, float tau, const Stats& st, int* status, cudaStream_t s) {
+cudaError_t launch_stats(const float* phi, const float* psi, const Dims& d, float tau, const Stats& st,
+                         const KeyCols& cols, int* status, cudaStream_t s) {
   int n = d.BH() * d.NB;
-  stats_kernel<<<(n + 127) / 128, 128, 0, s>>>(phi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, status);
+  stats_kernel<<<(n + 127) / 128, 128, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols, status);
   return cudaGetLastError();
 }
 

@@ -56,7 +56,7 @@ int bwd_path(int requested, int dtype, int D) {
 
 size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
-  return fpa::kStatusBytes + fpa::stats_bytes(d);
+  return fpa::kStatusBytes + fpa::stats_bytes(d) + (path == FPA_PATH_TENSOR ? fpa::keycols_bytes(d) : 0);
 }
 
 size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
@@ -102,12 +102,14 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
   char* ws = static_cast<char*>(a->workspace);
   int* status = reinterpret_cast<int*>(ws);
   fpa::Stats st = fpa::carve_stats(ws + fpa::kStatusBytes, d);
-  cudaError_t e = fpa::launch_stats(a->phi, d, a->tau, st, status, s);
+  fpa::KeyCols cols{nullptr, nullptr, nullptr};
+  if (path == FPA_PATH_TENSOR) cols = fpa::carve_keycols(ws + fpa::kStatusBytes + fpa::stats_bytes(d), d);
+  cudaError_t e = fpa::launch_stats(a->phi, a->psi, d, a->tau, st, cols, status, s);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   a->kernels_launched = 1;
   if (path == FPA_PATH_TENSOR) {
     int n = 0;
-    rc = fpa::tc_fwd(*a, d, st, status, s, &n, &g_last_error);
+    rc = fpa::tc_fwd(*a, d, st, cols, status, s, &n, &g_last_error);
     a->kernels_launched += n;
     if (rc) return rc;
   } else {
@@ -138,7 +140,7 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   fpa::Stats st = fpa::carve_stats(ws, d);
   fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d);
   int n = 0;
-  cudaError_t e = fpa::launch_stats(a->phi, d, a->tau, st, status, s);
+  cudaError_t e = fpa::launch_stats(a->phi, a->psi, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr}, status, s);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   ++n;
   e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta, s);

@@ -52,6 +52,15 @@ struct Stats {
   float* bl;    // [BH][NB]
 };
 
+// Per-key vectors the tensor-core forward streams next to each key tile (float32, [BH][TP]):
+//   a_s   = min(SUF_s - psi_s, 0)   (the part of min(0, x_ts) that does not depend on the query)
+//   psi_s, phi_s                     (psi and phi themselves; phi = +inf and psi = 0 beyond T)
+struct KeyCols {
+  float* a;
+  float* psi;
+  float* phi;
+};
+
 // Scratch of the backward pass (all float32, per head z = b*H + h).
 struct BwdScratch {
   float* delta;  // [BH][TP]   rowsum(dO * O)

@@ -33,7 +33,10 @@ Stats carve_stats(char* base, const Dims& d);
 BwdScratch carve_bwd(char* base, const Dims& d);
 
 // fpa_aux.cu
-cudaError_t launch_stats(const float* phi, const Dims& d, float tau, const Stats& st, int* status, cudaStream_t s);
+size_t keycols_bytes(const Dims& d);
+KeyCols carve_keycols(char* base, const Dims& d);
+cudaError_t launch_stats(const float* phi, const float* psi, const Dims& d, float tau, const Stats& st,
+                         const KeyCols& cols, int* status, cudaStream_t s);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,

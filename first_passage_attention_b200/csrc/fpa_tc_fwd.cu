@@ -1,14 +1,493 @@
+// Tensor-core forward pass of FPA for sm_100a (fp16 q, k, v; fp32 accumulation).
+//
+// One CTA computes two query tiles of 128 rows (i0 = 2m, i1 = 2m + 1) of one head and walks their key tiles from
+// the diagonal backwards (the order of kernel.py:104-162), so that the minimum of phi over the key tiles already
+// passed, `mid`, is a running minimum. Warp roles (384 threads; warps 10-11 only hand their registers to the softmax groups):
+//   warps 0-3  softmax group 0 (query tile i0; thread = row = TMEM lane)
+//   warps 4-7  softmax group 1 (query tile i1)
+//   warp  8    TMA producer: Q tiles once, then K, V tiles and the per-key vectors through an NS-stage ring
+//   warp  9    MMA issuer (one thread): S_x = Q_x K^T into TMEM, O_x += P_x V with P_x read from TMEM
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D); P_x (fp16, packed two per
+// column) overwrites the first 64 columns of S_x after the softmax has read S_x.
+//
+// The bias of query t (tile i) and key s (tile j) in log2 units is beta*log2e * min(0, x_ts) with
+//   off-diagonal (j < i):  min(0, x_ts) = min(a_s, min(mid_ij, PRE_t) - psi_s),  a_s = min(SUF_s - psi_s, 0)
+//   diagonal (j == i):     x_ts = min_{s<u<=t} phi_u - psi_s, a running minimum along the row (keys descending).
+// The online softmax rescales O lazily: the running maximum only moves when it grows by more than 8 (log2), so P
+// stays below 2^8 and most tiles need no O correction.
+//
+// Synchronisation (all mbarriers, every wait bounded by fpa::sm100::mbar_wait):
+//   q_full              producer -> MMA       (TMA bytes)
+//   k_full[s], v_full[s] producer -> MMA, softmax (TMA / bulk bytes)
+//   kv_empty[s]         MMA commit -> producer (stage s free again)
+//   s_full[x]           MMA commit -> softmax x (S_x ready; also implies the previous O_x += P_x V completed)
+//   p_full[x]           softmax x (128 arrivals) -> MMA (P_x in TMEM, O_x corrected)
+//   o_done[x]           MMA commit -> softmax x (final O_x complete)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fpa_sm100.cuh"
 #include "fpa_tc.h"
 
 namespace fpa {
+using namespace sm100;
 
-bool tc_supports(int D) { return false; }
+namespace {
 
-int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, int* status, cudaStream_t s, int* launched,
+constexpr int kBT = kTcBT;
+constexpr int kThreads = 384;
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
+constexpr float kRescaleThreshold = 8.0f;
+
+template <int D>
+struct TcFwdCfg {
+  static constexpr int BOXC = D >= 64 ? 64 : D;   // head-dim columns per TMA box (one swizzle row)
+  static constexpr int NBOX = D / BOXC;           // boxes per [128 x D] tile
+  static constexpr int SWB = BOXC * 2;            // bytes per row inside a box = swizzle width
+  static constexpr int BOXB = kBT * SWB;          // bytes per box
+  static constexpr int TILEB = NBOX * BOXB;       // bytes per [128 x D] tile
+  static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
+  static constexpr int NS = D >= 128 ? 2 : 3;     // K/V ring stages
+  static constexpr int COLB = kBT * 4;            // bytes of one per-key vector
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * TILEB;
+  static constexpr int OFF_V = OFF_K + NS * TILEB;
+  static constexpr int OFF_COL = OFF_V + NS * TILEB;  // per stage: a, psi, phi
+  static constexpr int OFF_BAR = OFF_COL + NS * 3 * COLB;
+  static constexpr int NBAR = 1 + 3 * NS + 2 + 2 + 2 + 1;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot + alignment slack
+  static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
+  static constexpr uint32_t IDESC_O = idesc_f16(kBT, D, 1);
+  static constexpr int COL_O = 2 * kBT;
+};
+
+struct TcFwdParams {
+  const float* cola;   // [BH][TP]
+  const float* colpsi;
+  const float* colphi;
+  const float* pre;    // [BH][TP]
+  const float* bmin;   // [BH][NB]
+  const float* beta;   // [H]
+  __half* o;
+  int64_t o_sb, o_sh, o_st;
+  float* lse;          // [BH][T]
+  int* status;
+  int H, T, NB, TP;
+  float scale2;        // D^-1/2 * log2(e)
+};
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+              const __grid_constant__ CUtensorMap tv, const TcFwdParams p) {
+  using C = TcFwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + C::NS;
+  uint64_t* kv_empty = v_full + C::NS;
+  uint64_t* s_full = kv_empty + C::NS;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npair = gridDim.x;
+  const int m = npair - 1 - blockIdx.x;  // longest pairs first
+  const int z = blockIdx.y, b = z / p.H, h = z % p.H;
+  const int i0 = 2 * m, i1 = 2 * m + 1;
+  const bool has1 = i1 < p.NB;
+  const int jtop = has1 ? i1 : i0;
+  const int nsteps = jtop + 1;
+  const int k0 = has1 ? 1 : 0;  // first step in which query tile i0 takes part
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, 128);
+      mbar_init(o_done + x, 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA group keeps 56 and each
+  // softmax group takes 224 (128*56 + 256*224 = 384*168).
+  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  if (warp == kWarpProducer) {
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      uint8_t* sq = smem + C::OFF_Q;
+      mbar_expect_tx(q_full, (has1 ? 2 : 1) * C::TILEB);
+      for (int bx = 0; bx < C::NBOX; ++bx) {
+        tma_load_4d(sq + bx * C::BOXB, &tq, bx * C::BOXC, i0 * kBT, h, b, q_full);
+        if (has1) tma_load_4d(sq + C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i1 * kBT, h, b, q_full);
+      }
+      bool ok = true;
+      const size_t colbase = size_t(z) * p.TP;
+      for (int k = 0; k < nsteps && ok; ++k) {
+        const int st = k % C::NS, j = jtop - k;
+        if (k >= C::NS) ok = mbar_wait(kv_empty + st, ((k / C::NS) - 1) & 1, p.status, 1);
+        if (!ok) break;
+        uint8_t* sk = smem + C::OFF_K + st * C::TILEB;
+        uint8_t* sv = smem + C::OFF_V + st * C::TILEB;
+        uint8_t* sc = smem + C::OFF_COL + st * 3 * C::COLB;
+        mbar_expect_tx(k_full + st, C::TILEB + 3 * C::COLB);
+        for (int bx = 0; bx < C::NBOX; ++bx) tma_load_4d(sk + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, k_full + st);
+        bulk_load(sc, p.cola + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        bulk_load(sc + C::COLB, p.colpsi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        bulk_load(sc + 2 * C::COLB, p.colphi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        mbar_expect_tx(v_full + st, C::TILEB);
+        for (int bx = 0; bx < C::NBOX; ++bx) tma_load_4d(sv + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, v_full + st);
+      }
+      // Drain: wait (bounded) until the copies this thread issued have landed before the CTA may exit.
+      mbar_wait(q_full, 0, p.status, 2);
+      for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k) {
+        mbar_wait(k_full + k % C::NS, (k / C::NS) & 1, p.status, 3);
+        mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 4);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      const uint32_t q0 = smem_u32(smem + C::OFF_Q), q1 = q0 + C::TILEB;
+      auto issue_s = [&](int x, int st) {
+        const uint32_t qa = x == 0 ? q0 : q1;
+        const uint32_t ka = smem_u32(smem + C::OFF_K + st * C::TILEB);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
+          mma_ss(tmem + x * kBT, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
+                 C::IDESC_S, kk > 0);
+        }
+      };
+      auto issue_pv = [&](int x, int st, bool acc) {
+        const uint32_t va = smem_u32(smem + C::OFF_V + st * C::TILEB);
+#pragma unroll
+        for (int kk = 0; kk < kBT / 16; ++kk) {
+          mma_ts(tmem + C::COL_O + x * D, tmem + x * kBT + kk * 8,
+                 smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_O, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, p.status, 10);
+      if (ok) ok = mbar_wait(k_full + 0, 0, p.status, 11);
+      tc_fence_after();
+      if (ok) {
+        if (k0 == 0) {
+          issue_s(0, 0);
+          mma_commit(s_full + 0);
+        }
+        if (has1) {
+          issue_s(1, 0);
+          mma_commit(s_full + 1);
+        }
+      }
+      int cnt0 = 0, cnt1 = 0;
+      for (int k = 0; k < nsteps && ok; ++k) {
+        const int st = k % C::NS;
+        ok = mbar_wait(v_full + st, (k / C::NS) & 1, p.status, 12);
+        if (!ok) break;
+        const bool more = k + 1 < nsteps;
+        const int st1 = (k + 1) % C::NS;
+        if (k >= k0) {  // query tile i0
+          ok = mbar_wait(p_full + 0, cnt0 & 1, p.status, 13);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(0, st, cnt0 > 0);
+          ++cnt0;
+        }
+        if (more) {
+          ok = mbar_wait(k_full + st1, ((k + 1) / C::NS) & 1, p.status, 14);
+          if (!ok) break;
+          tc_fence_after();
+          if (k + 1 >= k0) {
+            issue_s(0, st1);
+            mma_commit(s_full + 0);
+          }
+        }
+        if (has1) {  // query tile i1 takes part in every step
+          ok = mbar_wait(p_full + 1, cnt1 & 1, p.status, 15);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(1, st, cnt1 > 0);
+          ++cnt1;
+        }
+        mma_commit(kv_empty + st);
+        if (more && has1) {
+          issue_s(1, st1);
+          mma_commit(s_full + 1);
+        }
+      }
+      mma_commit(o_done + 0);
+      mma_commit(o_done + 1);
+      // Drain: every MMA issued by this thread has completed before TMEM can be released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.status, 16);
+    }
+  } else if (warp < 8) {
+    // ----------------------------------------------------------------------------------- softmax groups ----
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    const int x = warp >> 2, wr = warp & 3;
+    const int r = wr * 32 + lane;
+    const int i = x == 0 ? i0 : i1;
+    const bool active_wg = (x == 0) || has1;
+    const int t = i * kBT + r;
+    const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
+    const uint32_t col_s = x * kBT, col_o = C::COL_O + x * D;
+    const float betal = p.beta[h] * kLog2e;
+    const float pre_t = p.pre[size_t(z) * p.TP + t];
+    const float* bmin = p.bmin + size_t(z) * p.NB;
+    float mrow = -kInf, lrow = 0.f, mid = kInf;
+    int cnt = 0;
+    bool ok = active_wg;
+    const int kfirst = x == 0 ? k0 : 0;
+    for (int k = kfirst; k < nsteps && ok; ++k) {
+      const int j = jtop - k, st = k % C::NS;
+      ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 20);
+      if (ok) ok = mbar_wait(s_full + x, cnt & 1, p.status, 21);
+      if (!ok) break;
+      tc_fence_after();
+      float s[kBT];
+#pragma unroll
+      for (int c = 0; c < kBT / 32; ++c) tmem_ld32(tl + col_s + c * 32, s + c * 32);
+      tmem_ld_wait();
+      const float* ca = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB);
+      const float* cpsi = ca + kBT;
+      const float* cphi = ca + 2 * kBT;
+      if (j == i) {
+        // Diagonal tile: keys from the row down, carrying rmin = min_{s<u<=t} phi_u.
+        float rmin = kInf;
+        const int lim = min(r, p.T - 1 - j * kBT);  // last valid key of this row
+#pragma unroll
+        for (int c = kBT - 1; c >= 0; --c) {
+          const float xm = fminf(rmin - cpsi[c], 0.f);
+          const float v = fmaf(betal, xm, s[c] * p.scale2);
+          s[c] = c <= lim ? v : -kInf;
+          if (c <= r) rmin = fminf(rmin, cphi[c]);
+        }
+      } else {
+        const float cap = fminf(mid, pre_t);
+#pragma unroll
+        for (int c = 0; c < kBT; ++c) {
+          const float xm = fminf(ca[c], cap - cpsi[c]);
+          s[c] = fmaf(betal, xm, s[c] * p.scale2);
+        }
+        mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
+      }
+      float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int c = 4; c < kBT; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+      const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      // Lazy rescaling of the running maximum.
+      const float mnew = fmaxf(mrow, mt);
+      bool need = false;
+      float alpha = 1.f;
+      if (cnt == 0) {
+        mrow = mnew;
+      } else if (mnew > mrow + kRescaleThreshold) {
+        need = true;
+        alpha = exp2f(mrow - mnew);
+        mrow = mnew;
+      }
+      if (__any_sync(0xffffffffu, need)) {
+        lrow *= alpha;
+#pragma unroll
+        for (int c = 0; c < D; c += 16) {
+          float o[16];
+          tmem_ld16(tl + col_o + c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] *= alpha;
+          tmem_st16(tl + col_o + c, reinterpret_cast<const uint32_t*>(o));
+        }
+      }
+      float ls[2] = {0.f, 0.f};
+#pragma unroll
+      for (int c0 = 0; c0 < kBT; c0 += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = exp2f(s[c0 + e] - mrow), p1 = exp2f(s[c0 + e + 1] - mrow);
+          ls[0] += p0;
+          ls[1] += p1;
+          pk[e / 2] = pack_half2(p0, p1);
+        }
+        tmem_st16(tl + col_s + c0 / 2, pk);
+      }
+      lrow += ls[0] + ls[1];
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full + x);
+      ++cnt;
+    }
+    if (ok && active_wg) ok = mbar_wait(o_done + x, 0, p.status, 22);
+    if (ok && active_wg) {
+      tc_fence_after();
+      const float inv = 1.f / lrow;
+      const bool store = t < p.T;
+      __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(store ? t : 0) * p.o_st;
+#pragma unroll
+      for (int c = 0; c < D; c += 16) {
+        float o[16];
+        tmem_ld16(tl + col_o + c, o);
+        tmem_ld_wait();
+        if (store) {
+          uint4 w0, w1;
+          w0.x = pack_half2(o[0] * inv, o[1] * inv);
+          w0.y = pack_half2(o[2] * inv, o[3] * inv);
+          w0.z = pack_half2(o[4] * inv, o[5] * inv);
+          w0.w = pack_half2(o[6] * inv, o[7] * inv);
+          w1.x = pack_half2(o[8] * inv, o[9] * inv);
+          w1.y = pack_half2(o[10] * inv, o[11] * inv);
+          w1.z = pack_half2(o[12] * inv, o[13] * inv);
+          w1.w = pack_half2(o[14] * inv, o[15] * inv);
+          reinterpret_cast<uint4*>(orow + c)[0] = w0;
+          reinterpret_cast<uint4*>(orow + c)[1] = w1;
+        }
+      }
+      if (store) p.lse[size_t(z) * p.T + t] = mrow + log2f(lrow);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Tensor map of a [B, H, T, D] fp16 operand (innermost stride 1) with boxes of [128 rows x BOXC columns].
+template <int D>
+bool make_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T) {
+  using C = TcFwdCfg<D>;
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(T), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t strides[3] = {cuuint64_t(st[2]) * 2, cuuint64_t(st[1]) * 2, cuuint64_t(st[0]) * 2};
+  cuuint32_t box[4] = {cuuint32_t(C::BOXC), cuuint32_t(kBT), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMapSwizzle sw = C::SWB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : C::SWB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                         : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool tma_layout_ok(const void* p, const int64_t st[4]) {
+  if (reinterpret_cast<uintptr_t>(p) % 16) return false;
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((st[i] * 2) % 16 || st[i] <= 0) return false;
+  return true;
+}
+
+template <int D>
+int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
            std::string* err) {
+  using C = TcFwdCfg<D>;
+  CUtensorMap mq, mk, mv;
+  if (!make_map<D>(&mq, a.q, a.q_stride, d.B, d.H, d.T) || !make_map<D>(&mk, a.k, a.k_stride, d.B, d.H, d.T) ||
+      !make_map<D>(&mv, a.v, a.v_stride, d.B, d.H, d.T)) {
+    *err = "cuTensorMapEncodeTiled failed for q, k or v";
+    return FPA_ERR_CUDA;
+  }
+  auto fn = tc_fwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  TcFwdParams p;
+  p.cola = cols.a;
+  p.colpsi = cols.psi;
+  p.colphi = cols.phi;
+  p.pre = st.pre;
+  p.bmin = st.bmin;
+  p.beta = a.beta;
+  p.o = static_cast<__half*>(a.o);
+  p.o_sb = a.o_stride[0];
+  p.o_sh = a.o_stride[1];
+  p.o_st = a.o_stride[2];
+  p.lse = a.lse;
+  p.status = status;
+  p.H = d.H;
+  p.T = d.T;
+  p.NB = d.NB;
+  p.TP = d.TP;
+  p.scale2 = float(1.0 / sqrt(double(D))) * kLog2e;
+  dim3 grid((d.NB + 1) / 2, d.BH());
+  fn<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  return FPA_OK;
+}
+
+}  // namespace
+
+bool tc_supports(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
+
+int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
+           int* launched, std::string* err) {
   *launched = 0;
-  *err = "tensor-core forward not built";
-  return FPA_ERR_UNSUPPORTED;
+  if (!tma_layout_ok(a.q, a.q_stride) || !tma_layout_ok(a.k, a.k_stride) || !tma_layout_ok(a.v, a.v_stride)) {
+    *err = "the tensor-core path needs q, k, v with unit innermost stride and 16-byte aligned rows";
+    return FPA_ERR_UNSUPPORTED;
+  }
+  if (a.o_stride[3] != 1 || (a.o_stride[2] * 2) % 16 || reinterpret_cast<uintptr_t>(a.o) % 16) {
+    *err = "the tensor-core path needs o with unit innermost stride and 16-byte aligned rows";
+    return FPA_ERR_UNSUPPORTED;
+  }
+  int rc;
+  switch (d.D) {
+    case 16: rc = launch<16>(a, d, st, cols, status, s, err); break;
+    case 32: rc = launch<32>(a, d, st, cols, status, s, err); break;
+    case 64: rc = launch<64>(a, d, st, cols, status, s, err); break;
+    case 128: rc = launch<128>(a, d, st, cols, status, s, err); break;
+    default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
+  }
+  if (rc == FPA_OK) *launched = 1;
+  return rc;
 }
 
 }  // namespace fpa
