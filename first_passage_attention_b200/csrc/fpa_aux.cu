@@ -56,55 +56,83 @@ KeyCols carve_keycols(char* base, const Dims& d) {
   return c;
 }
 
-// One thread per (head, tile): sequential scans over the tile's BT positions (kernel.py:84-100).
-// It also clears the device status word of the call's workspace (the first launch of every call), and, when
-// `cols.a` is set, writes the per-key vectors of the tensor-core forward.
+// Block per (tile j, head z), one thread per position: warp-shuffle scans joined across warps through shared
+// memory (kernel.py:84-100 computes the same per-tile statistics). It also clears the device status word of the
+// call's workspace (the first launch of every call), and, when `cols.a` is set, writes the per-key vectors of the
+// tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int* status) {
-  int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx == 0 && status) *status = 0;
-  if (idx >= BH * NB) return;
-  int z = idx / NB, j = idx % NB;
-  const float* ph = phi + size_t(z) * T;
-  size_t TP = size_t(NB) * BT;
-  size_t base = size_t(z) * TP + size_t(j) * BT;
-  int t0 = j * BT;
-  float mn = kInf, l = -kInf;
-  for (int k = 0; k < BT; ++k) {
-    int t = t0 + k;
-    float p = t < T ? ph[t] : kInf;
-    float a = t < T ? -p * il2 : -kInf;
-    mn = fminf(mn, p);
-    l = lse2(l, a);
-    st.pre[base + k] = mn;
-    st.prel[base + k] = l;
-  }
-  st.bmin[size_t(z) * NB + j] = mn;
-  st.bl[size_t(z) * NB + j] = l;
-  mn = kInf;
-  l = -kInf;
-  const float* ps = psi + size_t(z) * T;
-  for (int k = BT - 1; k >= 0; --k) {
-    st.suf[base + k] = mn;  // over (t, tile end]
-    st.sufl[base + k] = l;
-    int t = t0 + k;
-    float p = t < T ? ph[t] : kInf;
-    if (cols.a) {
-      float y = t < T ? ps[t] : 0.f;
-      cols.a[base + k] = fminf(mn - y, 0.f);
-      cols.psi[base + k] = y;
-      cols.phi[base + k] = p;
+  __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
+  const int j = blockIdx.x, z = blockIdx.y;
+  if (j == 0 && z == 0 && tid == 0 && status) *status = 0;
+  const int t = j * BT + tid;
+  const size_t base = (size_t(z) * NB + j) * BT;
+  const float p = t < T ? phi[size_t(z) * T + t] : kInf;
+  const float a = t < T ? -p * il2 : -kInf;
+  // inclusive prefix: PRE, PREL
+  float pm = p, pl = a;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float qm = __shfl_up_sync(0xffffffffu, pm, o), ql = __shfl_up_sync(0xffffffffu, pl, o);
+    if (lane >= o) {
+      pm = fminf(pm, qm);
+      pl = lse2(pl, ql);
     }
-    float a = t < T ? -p * il2 : -kInf;
-    mn = fminf(mn, p);
-    l = lse2(l, a);
+  }
+  if (lane == 31) {
+    wmin[w] = pm;
+    wlse[w] = pl;
+  }
+  __syncthreads();
+  for (int v = 0; v < w; ++v) {
+    pm = fminf(pm, wmin[v]);
+    pl = lse2(pl, wlse[v]);
+  }
+  st.pre[base + tid] = pm;
+  st.prel[base + tid] = pl;
+  if (tid == BT - 1) {
+    st.bmin[size_t(z) * NB + j] = pm;
+    st.bl[size_t(z) * NB + j] = pl;
+  }
+  __syncthreads();
+  // inclusive suffix, then shifted by one: SUF_t, SUFL_t over (t, tile end]
+  float sm = p, sl = a;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float qm = __shfl_down_sync(0xffffffffu, sm, o), ql = __shfl_down_sync(0xffffffffu, sl, o);
+    if (lane + o < 32) {
+      sm = fminf(sm, qm);
+      sl = lse2(sl, ql);
+    }
+  }
+  if (lane == 0) {
+    wmin[w] = sm;
+    wlse[w] = sl;
+  }
+  __syncthreads();
+  for (int v = nw - 1; v > w; --v) {
+    sm = fminf(sm, wmin[v]);
+    sl = lse2(sl, wlse[v]);
+  }
+  smin[tid] = sm;
+  slse[tid] = sl;
+  __syncthreads();
+  const float suf = tid + 1 < BT ? smin[tid + 1] : kInf;
+  const float sufl = tid + 1 < BT ? slse[tid + 1] : -kInf;
+  st.suf[base + tid] = suf;
+  st.sufl[base + tid] = sufl;
+  if (cols.a) {
+    const float y = t < T ? psi[size_t(z) * T + t] : 0.f;
+    cols.a[base + tid] = fminf(suf - y, 0.f);
+    cols.psi[base + tid] = y;
+    cols.phi[base + tid] = p;
   }
 }
 
 cudaError_t launch_stats(const float* phi, const float* psi, const Dims& d, float tau, const Stats& st,
                          const KeyCols& cols, int* status, cudaStream_t s) {
-  int n = d.BH() * d.NB;
-  stats_kernel<<<(n + 127) / 128, 128, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols, status);
+  stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols, status);
   return cudaGetLastError();
 }
 
@@ -199,7 +227,7 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     const float cU = cb[U];
     for (int i = U + 1 + tid; i < NB; i += blockDim.x) {
       const float* row = sc.tb + (size_t(z) * NB + i) * NB;
-      for (int j = 0; j < U; ++j) s3 += exp2f(cU - fmaxf(A[j], Bv[i])) * row[j];
+      for (int j = 0; j < U; ++j) s3 += ex2(cU - fmaxf(A[j], Bv[i])) * row[j];
     }
   }
   float S = block_sum(s3, red);
@@ -210,8 +238,8 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     float a2 = -phi[size_t(z) * T + u] * il2;
     float part1 = 0.f;
     for (int s = 0; s < tid; ++s)
-      if (c2s[s] > -kInf) part1 += exp2f(a2 - c2s[s]) * Ws[s];
-    float part3 = (U > 0 && U < NB - 1) ? exp2f(a2 - cb[U]) * S : 0.f;
+      if (c2s[s] > -kInf) part1 += ex2(a2 - c2s[s]) * Ws[s];
+    float part3 = (U > 0 && U < NB - 1) ? ex2(a2 - cb[U]) * S : 0.f;
     size_t p = size_t(z) * TP + u;
     dphi[size_t(z) * T + u] = beta[h] * (part1 + sc.dphi2[p] + sc.dphi4[p] + part3);
   }

@@ -22,11 +22,24 @@ template <typename T> __device__ __forceinline__ T from_f32(float x);
 template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
 template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
+// 2^x and log2(x) with the hardware approximations (PTX ex2.approx.ftz.f32 / lg2.approx.ftz.f32: about 2^-22
+// relative error; subnormal results flush to zero; ex2(-inf) = +0, lg2(0) = -inf). One MUFU operation each.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // log2(2^a + 2^b), with -inf + -inf = -inf (the stable base-2 log-add-exp of kernel.py:73-75).
 __device__ __forceinline__ float lse2(float a, float b) {
   float m = fmaxf(a, b);
   if (m == -kInf) return m;
-  return m + log2f(1.0f + exp2f(fminf(a, b) - m));
+  return m + lg2(1.0f + ex2(fminf(a, b) - m));
 }
 
 // Sum over the `W` consecutive lanes of a group (W a power of two <= 32, groups aligned). Every lane of the group

@@ -73,13 +73,13 @@ simt_fwd_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k, S
 #pragma unroll
     for (int e = 0; e < CH; ++e) mx = fmaxf(mx, sc[e]);
     if (mx == -kInf) return;
-    float corr = exp2f(m - mx);
+    float corr = ex2(m - mx);
     l *= corr;
 #pragma unroll
     for (int c = 0; c < CPT; ++c) acc[c] *= corr;
 #pragma unroll
     for (int e = 0; e < CH; ++e) {
-      float p = exp2f(sc[e] - mx);
+      float p = ex2(sc[e] - mx);
       l += p;
       const float* vr = Vs + (s0 + e) * D + c0;
 #pragma unroll
@@ -149,7 +149,7 @@ simt_fwd_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k, S
     TIn* orow = o + b * so.b + h * so.h + int64_t(t) * so.t;
 #pragma unroll
     for (int c = 0; c < CPT; ++c) orow[int64_t(c0 + c) * so.d] = from_f32<TIn>(acc[c] * inv);
-    if (sub == 0) lse[size_t(z) * T + t] = m + log2f(l);
+    if (sub == 0) lse[size_t(z) * T + t] = m + lg2(l);
   }
 }
 
@@ -234,7 +234,7 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
         const float x = rmin - psi_s;  // +inf on and above the diagonal
         const float xm = fminf(x, 0.f);
         const bool valid = (tl >= sl) && (t < T) && s_ok;
-        const float p = valid ? exp2f(dot + betal * xm - lses[tl]) : 0.f;
+        const float p = valid ? ex2(dot + betal * xm - lses[tl]) : 0.f;
         const float ds = p * (dpd - dels[tl]);
 #pragma unroll
         for (int c = 0; c < CPT; ++c) {
@@ -260,9 +260,9 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
         }
         float Hh = 0.f;
         for (int tl = tend - 1; tl > sl; --tl) {
-          if (tl < tend - 1) Hh *= exp2f(Ls[sl * LD + tl] - Ls[sl * LD + tl + 1]);
+          if (tl < tend - 1) Hh *= ex2(Ls[sl * LD + tl] - Ls[sl * LD + tl + 1]);
           Hh += Gd[sl * LD + tl];
-          Gd[sl * LD + tl] = exp2f(-phis[tl] * il2 - Ls[sl * LD + tl]) * Hh;
+          Gd[sl * LD + tl] = ex2(-phis[tl] * il2 - Ls[sl * LD + tl]) * Hh;
         }
       }
       __syncthreads();
@@ -276,7 +276,7 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
       float rs = fmaxf(c2_s, cmid2);
       const bool vrs = rs > -kInf;
       rs = vrs ? rs : 0.f;
-      const float sv_ = exp2f(sufl_s - rs) + exp2f(midl - rs);
+      const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
       const float cap = fminf(suf_s, mid);
       float fsum = 0.f;
       for (int tl = 0; tl < BT; ++tl) {
@@ -294,7 +294,7 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
         const float x = fminf(cap, pres[tl]) - psi_s;
         const float xm = fminf(x, 0.f);
         const bool valid = (t < T) && s_ok;
-        const float p = valid ? exp2f(dot + betal * xm - lses[tl]) : 0.f;
+        const float p = valid ? ex2(dot + betal * xm - lses[tl]) : 0.f;
         const float ds = p * (dpd - dels[tl]);
 #pragma unroll
         for (int c = 0; c < CPT; ++c) {
@@ -304,11 +304,11 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
         const float g = (valid && x <= 0.f) ? ds : 0.f;
         gsum += g;
         dbsum += valid ? ds * xm : 0.f;
-        fsum += g / (sv_ + exp2f(prels[tl] - rs));
+        fsum += g / (sv_ + ex2(prels[tl] - rs));
       }
-      if (vrs) wsum += exp2f(c2_s - rs) * fsum;
+      if (vrs) wsum += ex2(c2_s - rs) * fsum;
       if (i > j + 1) {
-        float tp = (vrs && sub == 0) ? exp2f(cmid2 - rs) * fsum : 0.f;
+        float tp = (vrs && sub == 0) ? ex2(cmid2 - rs) * fsum : 0.f;
         tp = group_sum<32>(tp);
         const int warp = threadIdx.x >> 5, nw = S::THREADS >> 5;
         if ((threadIdx.x & 31) == 0) red[warp] = tp;
@@ -392,7 +392,7 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
   const float pre_t = st.pre[size_t(z) * TP + t];
   const float prel_t = st.prel[size_t(z) * TP + t];
   const float c2_t = t_ok ? -pre_t * il2 : 0.f;
-  const float bpre = t_ok ? exp2f(prel_t - c2_t) : 1.f;
+  const float bpre = t_ok ? ex2(prel_t - c2_t) : 1.f;
   float racc = 0.f;
 
   auto tile_in = [&](int j) {
@@ -423,7 +423,7 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
     dpd = group_sum<TPR>(dpd);
     const bool ok = (sl <= tl) && (i * BT + sl < T) && t_ok;
     const float x = rmin - psis[sl];
-    const float p = ok ? exp2f(dot + betal * fminf(x, 0.f) - lse_t) : 0.f;
+    const float p = ok ? ex2(dot + betal * fminf(x, 0.f) - lse_t) : 0.f;
     const float ds = p * (dpd - del_t);
 #pragma unroll
     for (int c = 0; c < CPT; ++c) dqr[c] = fmaf(ds, krow[c], dqr[c]);
@@ -434,7 +434,7 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
     __syncthreads();
     tile_in(j);
     __syncthreads();
-    const float mterm = exp2f(midl - c2_t) + bpre;
+    const float mterm = ex2(midl - c2_t) + bpre;
     const float cap = fminf(mid, pre_t);
     for (int sl = 0; sl < BT; ++sl) {
       const float* krow = Ks + sl * D + c0;
@@ -448,12 +448,12 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
       dot = group_sum<TPR>(dot);
       dpd = group_sum<TPR>(dpd);
       const float x = fminf(sufs[sl], cap) - psis[sl];
-      const float p = t_ok ? exp2f(dot + betal * fminf(x, 0.f) - lse_t) : 0.f;
+      const float p = t_ok ? ex2(dot + betal * fminf(x, 0.f) - lse_t) : 0.f;
       const float ds = p * (dpd - del_t);
 #pragma unroll
       for (int c = 0; c < CPT; ++c) dqr[c] = fmaf(ds, krow[c], dqr[c]);
       const float g = (t_ok && x <= 0.f) ? ds : 0.f;
-      racc += g / (exp2f(sufls[sl] - c2_t) + mterm);
+      racc += g / (ex2(sufls[sl] - c2_t) + mterm);
     }
     mid = fminf(mid, st.bmin[size_t(z) * NB + j]);
     midl = lse2(midl, st.bl[size_t(z) * NB + j]);
@@ -474,7 +474,7 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
     const int tend = min(BT, T - i * BT);
     const float a2 = -phis[tl] * il2;
     float p2 = 0.f;
-    for (int t2 = tl; t2 < tend; ++t2) p2 += exp2f(a2 - c2t[t2]) * rr[t2];
+    for (int t2 = tl; t2 < tend; ++t2) p2 += ex2(a2 - c2t[t2]) * rr[t2];
     sc.dphi2[size_t(z) * TP + t] = p2;
   }
 }

@@ -48,6 +48,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or about `hint_ns` passes, so a
+// waiting warp issues almost nothing while it waits.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -55,15 +69,17 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Every wait is bounded: after `kWaitLimitNs` without the phase completing, the wait records FPA_ERR_TIMEOUT with
-// the call-site id in the workspace status word and returns false; the caller then unwinds.
+// the call-site id in the workspace status word and returns false; the caller then unwinds. The clock is read only
+// once per suspended try_wait, so a waiting warp costs next to nothing.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSuspendHintNs = 100000;       // 0.1 ms
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait_sleep(addr, parity, kSuspendHintNs)) return true;
     if (global_ns() - t0 > kWaitLimitNs) {
       report_timeout(status, site);
       return false;

@@ -90,7 +90,9 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
               const __grid_constant__ CUtensorMap tv, const TcFwdParams p) {
   using C = TcFwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base (the swizzle atoms of the UMMA operands), kept as an offset from smem_raw so the
+  // compiler still sees shared-memory pointers.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
@@ -309,7 +311,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         mrow = mnew;
       } else if (mnew > mrow + kRescaleThreshold) {
         need = true;
-        alpha = exp2f(mrow - mnew);
+        alpha = ex2(mrow - mnew);
         mrow = mnew;
       }
       if (__any_sync(0xffffffffu, need)) {
@@ -330,7 +332,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = exp2f(s[c0 + e] - mrow), p1 = exp2f(s[c0 + e + 1] - mrow);
+          const float p0 = ex2(s[c0 + e] - mrow), p1 = ex2(s[c0 + e + 1] - mrow);
           ls[0] += p0;
           ls[1] += p1;
           pk[e / 2] = pack_half2(p0, p1);
@@ -368,7 +370,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           reinterpret_cast<uint4*>(orow + c)[1] = w1;
         }
       }
-      if (store) p.lse[size_t(z) * p.T + t] = mrow + log2f(lrow);
+      if (store) p.lse[size_t(z) * p.T + t] = mrow + lg2(lrow);
     }
   }
   tc_fence_before();

@@ -148,12 +148,18 @@ def test_config3_edge_coverage(D, dtype):
     assert all(torch.equal(x, y) for x, y in zip(kern, again))
 
 
-@pytest.mark.parametrize("T", [1, 2, 63, 64, 65, 127, 129])
+@pytest.mark.parametrize("T", [1, 2, 3, 63, 64, 65, 127, 129])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_ragged_and_tiny_lengths(T, dtype):
+    """Lengths around the tile sizes (64 for the FFMA kernels, 128 for the tensor-core forward) and the degenerate
+    T = 1, 2. For T <= 2 the gradients through dS = P (dP - delta) are pure cancellation: with fp16 inputs, delta
+    is formed from the fp16-rounded output o (as kernel.py:174 forms it), so only rounding is left and those
+    cases are held to 1e-2 instead of 2e-3."""
     need_gpu()
     inp = make_inputs(1, 3, T, 64, seed=300 + T, dtype=dtype)
-    check(run_kernel(*inp), run_oracle(*inp), dtype, floor=1e-2 if T <= 2 else 0.0)
+    tiny = T <= 2
+    tol = 1e-2 if (tiny and dtype == torch.float16) else None
+    check(run_kernel(*inp), run_oracle(*inp), dtype, tol=tol, floor=1e-2 if tiny else 0.0)
 
 
 def test_negative_and_scalar_beta():
