@@ -17,7 +17,8 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE = range(6
 
 # Exported symbols, in the order include/fpa.h declares them.
 EXPORTS = ("fpa_abi_version", "fpa_struct_size", "fpa_fwd_workspace_bytes", "fpa_bwd_workspace_bytes", "fpa_fwd",
-           "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error")
+           "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_fwd_noalloc")
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _c_i64x4 = ctypes.c_int64 * 4
 
@@ -87,6 +88,8 @@ def load():
         lib.fpa_status_string.restype = ctypes.c_char_p
         lib.fpa_status_string.argtypes = [ctypes.c_int]
         lib.fpa_last_error.restype = ctypes.c_char_p
+        lib.fpa_fwd_noalloc.restype = ctypes.c_int
+        lib.fpa_fwd_noalloc.argtypes = [ctypes.POINTER(FpaFwdArgs), ctypes.c_void_p]
         if lib.fpa_abi_version() != ABI_VERSION:
             raise RuntimeError(f"libfpa_b200 ABI version {lib.fpa_abi_version()} != {ABI_VERSION}; rebuild it")
         if lib.fpa_struct_size(0) != ctypes.sizeof(FpaFwdArgs) or lib.fpa_struct_size(1) != ctypes.sizeof(FpaBwdArgs):

@@ -66,6 +66,8 @@ size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
 
 }  // namespace
 
+void fpa::set_last_error(const std::string& msg) { g_last_error = msg; }
+
 extern "C" {
 
 int fpa_abi_version(void) { return FPA_ABI_VERSION; }

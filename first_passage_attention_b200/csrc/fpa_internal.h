@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "fpa_common.cuh"
 
 namespace fpa {
@@ -25,6 +27,9 @@ inline Dims make_dims(int B, int H, int T, int D, int BT) {
   d.TP = d.NB * BT;
   return d;
 }
+
+// Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
+void set_last_error(const std::string& msg);
 
 // Workspace carving (all arrays 256-byte aligned, after the 256-byte status word).
 size_t stats_bytes(const Dims& d);

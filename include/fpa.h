@@ -127,6 +127,21 @@ FPA_API const char* fpa_status_string(int status);
 /* The message of the last error raised on the calling thread (empty string when none). */
 FPA_API const char* fpa_last_error(void);
 
+/* Size of the scratch array built into the library for fpa_fwd_noalloc (8 MiB per GPU that loads the library). */
+#define FPA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/* Forward pass for callers that cannot allocate device memory (a plugin host that hands over only the input and
+ * output buffers, a runtime whose device memory is fully reserved, code that must not allocate after start-up).
+ * This entry point has no counterpart in the reference. It runs the same kernels as fpa_fwd, but their scratch
+ * lives in a device array that is part of the library image (FPA_NOALLOC_SCRATCH_BYTES, held by every GPU that
+ * loads the library until the process exits) instead of a caller workspace: args->workspace and
+ * args->workspace_bytes are ignored and overwritten. It allocates nothing. A call whose scratch need
+ * (fpa_fwd_workspace_bytes) exceeds FPA_NOALLOC_SCRATCH_BYTES returns FPA_ERR_WORKSPACE with a message and
+ * launches nothing. The first call on each device looks up the array's device address (make that first call
+ * before any stream capture). All calls share the one array: calls whose kernels overlap on the GPU race and
+ * must be serialised by the caller. */
+FPA_API int fpa_fwd_noalloc(FpaFwdArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
