@@ -49,6 +49,24 @@ def flops(B, H, T, D, which):
     return f if which == "fwd" else 3.5 * f
 
 
+def head_shard(B, H, rank, world):
+    """Contiguous block of the flattened (b, h) heads owned by `rank` when B*H heads are split over `world` ranks:
+    returns (z0, z1). Heads are independent in the forward and the backward, so the shards need no exchange."""
+    n = B * H
+    if n % world:
+        raise ValueError(f"{n} heads cannot be split evenly over {world} ranks")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def take_heads(x, z0, z1, H):
+    """The heads z0..z1 of a [B, H, ...] tensor as a [1, z1 - z0, ...] tensor; beta (H,) maps to beta[z % H]."""
+    if x.dim() == 1:
+        return x[torch.arange(z0, z1, device=x.device) % H]
+    flat = x.reshape(-1, *x.shape[2:])
+    return flat[z0:z1].unsqueeze(0)
+
+
 def load_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -212,14 +230,17 @@ def main():
 
     from first_passage_attention_b200 import LaunchStats, first_passage_attention
 
-    # Shard of this rank: weak scaling runs the full per-GPU batch; strong splits the B*H heads across ranks.
+    # Shard of this rank: weak scaling runs a full per-GPU batch of its own; strong splits the B*H heads of one
+    # batch across the ranks (every rank draws the same batch and keeps its heads).
     if args.scaling == "strong":
-        heads = B * H
-        assert heads % world == 0, "strong scaling needs B*H divisible by the number of GPUs"
-        Br, Hr = 1, heads // world
+        z0, z1 = head_shard(B, H, rank, world)
+        full = make_inputs(B, H, T, D, seed=1000, device=device)
+        q, k, v, phi, psi, beta, do = (take_heads(t, z0, z1, H).contiguous() for t in full)
+        del full
+        Br, Hr = 1, z1 - z0
     else:
         Br, Hr = B, H
-    q, k, v, phi, psi, beta, do = make_inputs(Br, Hr, T, D, seed=1000 + rank, device=device)
+        q, k, v, phi, psi, beta, do = make_inputs(Br, Hr, T, D, seed=1000 + rank, device=device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
     def fwd():
