@@ -61,7 +61,8 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // call's workspace (the first launch of every call), and, when `cols.a` is set, writes the per-key vectors of the
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
-                             int NB, float il2, Stats st, KeyCols cols, int* status) {
+                             int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
+                             const float* __restrict__ beta, int H, int* status) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.y;
@@ -123,23 +124,35 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   st.suf[base + tid] = suf;
   st.sufl[base + tid] = sufl;
   if (cols.a) {
-    const float y = t < T ? psi[size_t(z) * T + t] : 0.f;
-    cols.a[base + tid] = fminf(suf - y, 0.f);
-    cols.psi[base + tid] = y;
-    cols.phi[base + tid] = p;
+    const bool ok = t < T;
+    const float y = ok ? psi[size_t(z) * T + t] : 0.f;
+    if (cols_scaled) {
+      const float bl = beta[z % H] * kLog2e;
+      cols.a[base + tid] = ok ? bl * fminf(suf - y, 0.f) : 0.f;
+      cols.psi[base + tid] = ok ? -bl * y : 0.f;
+      cols.phi[base + tid] = ok ? bl * p : 0.f;
+    } else {
+      cols.a[base + tid] = ok ? suf - y : kInf;
+      cols.psi[base + tid] = y;
+      cols.phi[base + tid] = ok ? p : kInf;
+    }
   }
 }
 
-cudaError_t launch_stats(const float* phi, const float* psi, const Dims& d, float tau, const Stats& st,
-                         const KeyCols& cols, int* status, cudaStream_t s) {
-  stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols, status);
+cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
+                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s) {
+  stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
+                                                   cols_scaled, beta, d.H, status);
   return cudaGetLastError();
 }
 
 // delta_t = sum_d dO[t, d] * O[t, d] in float32 (kernel.py:166-174). One warp per row.
+// When `lse` and `lsep` are set it also copies lse [BH][T] into the padded layout lsep [BH][TP], so the tensor-core
+// backward can fetch whole tiles of it with bulk copies.
 template <typename TIn>
 __global__ void delta_kernel(const TIn* __restrict__ o, Str4 so, const TIn* __restrict__ dout, Str4 sdo, int H,
-                             int T, int D, int TP, int rows, float* __restrict__ delta) {
+                             int T, int D, int TP, int rows, float* __restrict__ delta, const float* __restrict__ lse,
+                             float* __restrict__ lsep) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   int z = warp / T, t = warp % T, b = z / H, h = z % H;
@@ -148,19 +161,22 @@ __global__ void delta_kernel(const TIn* __restrict__ o, Str4 so, const TIn* __re
   float acc = 0.f;
   for (int c = lane; c < D; c += 32) acc += to_f32(op[c * so.d]) * to_f32(dp[c * sdo.d]);
   acc = group_sum<32>(acc);
-  if (lane == 0) delta[size_t(z) * TP + t] = acc;
+  if (lane == 0) {
+    delta[size_t(z) * TP + t] = acc;
+    if (lsep) lsep[size_t(z) * TP + t] = lse[size_t(z) * T + t];
+  }
 }
 
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
-                         cudaStream_t s) {
+                         const float* lse, float* lsep, cudaStream_t s) {
   int rows = d.BH() * d.T;
   int blocks = (rows * 32 + 255) / 256;
   if (dtype == FPA_DTYPE_F16)
     delta_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)o, so, (const __half*)dout, sdo, d.H, d.T, d.D,
-                                                d.TP, rows, delta);
+                                                d.TP, rows, delta, lse, lsep);
   else
     delta_kernel<float><<<blocks, 256, 0, s>>>((const float*)o, so, (const float*)dout, sdo, d.H, d.T, d.D, d.TP,
-                                               rows, delta);
+                                               rows, delta, lse, lsep);
   return cudaGetLastError();
 }
 
@@ -254,6 +270,53 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
     if (e != cudaSuccess) return e;
   }
   dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc, dphi);
+  return cudaGetLastError();
+}
+
+// In-tile soft-min gradient of the diagonal tiles from their stored g (the tensor-core backward writes
+// g_ts = dS_ts [x_ts <= 0] of each diagonal tile to `gd` [BH][NB][BT][BT], indexed [key s][query t]). For key s:
+//   H(t) = g_ts + (Z_{s,t} / Z_{s,t+1}) H(t+1),  contribution to u = t: (2^{a2_t} / Z_{s,t}) H(t),
+// Z_{s,t} = sum_{s<u<=t} 2^{a2_u} carried as its log2 (kernel.py:269-283 evaluates the same sums with scans).
+// Block: one thread per key; the contributions are summed per u in a fixed order.
+__global__ void diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, int T, int BT, int NB,
+                                 float il2, float* __restrict__ dphi4) {
+  extern __shared__ float sm[];
+  const int LD = BT + 1;
+  float* G = sm;             // [BT][BT+1]
+  float* L = G + BT * LD;    // [BT][BT+1]
+  float* a2 = L + BT * LD;   // [BT]
+  const int j = blockIdx.x, z = blockIdx.y, tid = threadIdx.x;
+  const size_t TP = size_t(NB) * BT;
+  const float* g = gd + (size_t(z) * NB + j) * BT * BT;
+  for (int e = tid; e < BT * BT; e += blockDim.x) G[(e / BT) * LD + (e % BT)] = g[e];
+  const int p0 = j * BT;
+  a2[tid] = p0 + tid < T ? -phi[size_t(z) * T + p0 + tid] * il2 : -kInf;
+  __syncthreads();
+  const int tend = min(BT, T - p0), sl = tid;
+  float Lr = -kInf;
+  for (int t = sl + 1; t < tend; ++t) {
+    Lr = lse2(Lr, a2[t]);
+    L[sl * LD + t] = Lr;
+  }
+  float Hh = 0.f;
+  for (int t = tend - 1; t > sl; --t) {
+    if (t < tend - 1) Hh *= ex2(L[sl * LD + t] - L[sl * LD + t + 1]);
+    Hh += G[sl * LD + t];
+    G[sl * LD + t] = ex2(a2[t] - L[sl * LD + t]) * Hh;
+  }
+  __syncthreads();
+  if (sl < tend) {
+    float acc = 0.f;
+    for (int s2 = 0; s2 < sl; ++s2) acc += G[s2 * LD + sl];
+    dphi4[size_t(z) * TP + p0 + sl] = acc;
+  }
+}
+
+cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s) {
+  const size_t smem = (2 * size_t(d.BT) * (d.BT + 1) + d.BT) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(diag_dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  diag_dphi_kernel<<<dim3(d.NB, d.BH()), d.BT, smem, s>>>(phi, gd, d.T, d.BT, d.NB, kLog2e / tau, dphi4);
   return cudaGetLastError();
 }
 

@@ -106,7 +106,7 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
   fpa::Stats st = fpa::carve_stats(ws + fpa::kStatusBytes, d);
   fpa::KeyCols cols{nullptr, nullptr, nullptr};
   if (path == FPA_PATH_TENSOR) cols = fpa::carve_keycols(ws + fpa::kStatusBytes + fpa::stats_bytes(d), d);
-  cudaError_t e = fpa::launch_stats(a->phi, a->psi, d, a->tau, st, cols, status, s);
+  cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, cols, 1, status, s);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   a->kernels_launched = 1;
   if (path == FPA_PATH_TENSOR) {
@@ -142,10 +142,12 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   fpa::Stats st = fpa::carve_stats(ws, d);
   fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d);
   int n = 0;
-  cudaError_t e = fpa::launch_stats(a->phi, a->psi, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr}, status, s);
+  cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr},
+                                    0, status, s);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   ++n;
-  e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta, s);
+  e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta,
+                        nullptr, nullptr, s);
   if (e != cudaSuccess) return cuda_fail(e, "delta kernel");
   ++n;
   e = fpa::simt_bwd_kv(*a, d, st, sc, s);

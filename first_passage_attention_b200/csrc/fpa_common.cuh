@@ -65,9 +65,12 @@ struct Stats {
   float* bl;    // [BH][NB]
 };
 
-// Per-key vectors the tensor-core forward streams next to each key tile (float32, [BH][TP]):
-//   a_s   = min(SUF_s - psi_s, 0)   (the part of min(0, x_ts) that does not depend on the query)
-//   psi_s, phi_s                     (psi and phi themselves; phi = +inf and psi = 0 beyond T)
+// Per-key vectors the tensor-core forward streams next to each key tile (float32, [BH][TP]), in the units of the
+// log2-scaled logits (b' = beta * log2 e of the key's head):
+//   a_s   = b' * min(SUF_s - psi_s, 0)   (the part of the bias that does not depend on the query)
+//   psi_s = -b' * psi_s                   (negated, so the bias needs an add rather than a subtract)
+//   phi_s = b' * phi_s                    (for the running extremum inside the diagonal tile)
+// All three are 0 beyond T.
 struct KeyCols {
   float* a;
   float* psi;

@@ -40,10 +40,12 @@ BwdScratch carve_bwd(char* base, const Dims& d);
 // fpa_aux.cu
 size_t keycols_bytes(const Dims& d);
 KeyCols carve_keycols(char* base, const Dims& d);
-cudaError_t launch_stats(const float* phi, const float* psi, const Dims& d, float tau, const Stats& st,
-                         const KeyCols& cols, int* status, cudaStream_t s);
+// cols_scaled = 1: the forward's b'-scaled key vectors; 0: raw (a = SUF - psi, psi, phi) for the backward.
+cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
+                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
-                         cudaStream_t s);
+                         const float* lse, float* lsep, cudaStream_t s);
+cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
                         const BwdScratch& sc, float* dphi, cudaStream_t s);
 cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s);

@@ -1,6 +1,8 @@
 // Tensor-core (tcgen05 / TMEM / TMA) kernels for sm_100a.
 #pragma once
 
+#include <cuda.h>
+
 #include <string>
 
 #include "fpa_internal.h"
@@ -10,6 +12,14 @@ namespace fpa {
 constexpr int kTcBT = 128;  // positions per tile of the tensor-core kernels (the MMA M and N)
 
 bool tc_supports(int D);
+
+// True if a [B, H, T, D] fp16 operand with these element strides can be read by TMA as it is (innermost stride 1,
+// 16-byte aligned base and strides).
+bool tma_layout_ok(const void* p, const int64_t st[4]);
+
+// Tensor map of a [B, H, T, D] fp16 operand: boxes of [128 rows x min(64, D) columns] with the swizzle whose width
+// is one box row (128 B for D >= 64, 64 B for D = 32, 32 B for D = 16); rows >= T read as zero.
+bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T, int D);
 
 // Forward pass on the tensor cores; `status` is the device status word of the workspace. Sets *launched to the
 // number of kernels launched. Returns an FpaStatus; on failure writes a message into *err.

@@ -10,9 +10,10 @@
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D); P_x (fp16, packed two per
 // column) overwrites the first 64 columns of S_x after the softmax has read S_x.
 //
-// The bias of query t (tile i) and key s (tile j) in log2 units is beta*log2e * min(0, x_ts) with
-//   off-diagonal (j < i):  min(0, x_ts) = min(a_s, min(mid_ij, PRE_t) - psi_s),  a_s = min(SUF_s - psi_s, 0)
-//   diagonal (j == i):     x_ts = min_{s<u<=t} phi_u - psi_s, a running minimum along the row (keys descending).
+// The bias of query t (tile i) and key s (tile j) in log2 units is b' * min(0, x_ts), b' = beta * log2 e, with
+//   off-diagonal (j < i):  b' min(0, x_ts) = min(b' a_s, b' min(mid_ij, PRE_t) - b' psi_s),  a_s = min(SUF_s - psi_s, 0)
+//   diagonal (j == i):     x_ts = min_{s<u<=t} phi_u - psi_s, a running minimum along the row (keys descending);
+// the per-key terms come pre-scaled by b' (stats_kernel), and for b' < 0 every minimum becomes a maximum.
 // The online softmax rescales O lazily: the running maximum only moves when it grows by more than 8 (log2), so P
 // stays below 2^8 and most tiles need no O correction.
 //
@@ -24,9 +25,9 @@
 //   p_full[x]           softmax x (128 arrivals) -> MMA (P_x in TMEM, O_x corrected)
 //   o_done[x]           MMA commit -> softmax x (final O_x complete)
 #include <cuda.h>
-#include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "fpa_sm100.cuh"
 #include "fpa_tc.h"
@@ -75,9 +76,36 @@ struct TcFwdParams {
   int64_t o_sb, o_sh, o_st;
   float* lse;          // [BH][T]
   int* status;
-  int H, T, NB, TP;
+  int B, H, T, NB, TP, NPAIR;
   float scale2;        // D^-1/2 * log2(e)
 };
+
+// With kEmuEvery > 0, every kEmuEvery-th pair of columns takes its exponentials on the FMA pipe instead of the
+// MUFU unit (16 exp2 per clock per SM against 128 FMA lanes). Off by default: measured on B200 at configuration 2
+// the forward is not MUFU-bound yet (no gain at 1/5 or 1/3 of the pairs) and the polynomial adds 1e-4 to lse.
+#ifndef FPA_EMU_EVERY
+#define FPA_EMU_EVERY 0
+#endif
+constexpr int kEmuEvery = FPA_EMU_EVERY;
+
+// 2^x for a pair, on the FMA/ALU pipes: x = n + f with n = rint(x) (the 1.5 * 2^23 rounding trick), f in
+// [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted for this file by a reweighted least-squares minimax on
+// [-0.5, 0.5] (max relative error 7.5e-5, below the fp16 rounding of P); 2^n is added to the exponent field.
+// x is clamped at -125 so the exponent field of the result stays >= 1 for every f (2^-125 rounds to 0 in fp16).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 nf = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(nf, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.055171627551317215f, 0.055171627551317215f), f,
+                        make_float2(0.2426111400127411f, 0.2426111400127411f));
+  q = __ffma2_rn(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = __ffma2_rn(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  // Unsigned arithmetic: the shift drops the high bits of t, leaving n << 23 modulo 2^32.
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
@@ -105,9 +133,11 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int npair = gridDim.x;
-  const int m = npair - 1 - blockIdx.x;  // longest pairs first
-  const int z = blockIdx.y, b = z / p.H, h = z % p.H;
+  // 1-d grid in longest-first order: all heads' pair NPAIR-1 (the most key tiles), then NPAIR-2, ... so the block
+  // scheduler performs a longest-processing-time-first list schedule over the SMs.
+  const int nbh = p.B * p.H;
+  const int m = p.NPAIR - 1 - int(blockIdx.x) / nbh;
+  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
   const int i0 = 2 * m, i1 = 2 * m + 1;
   const bool has1 = i1 < p.NB;
   const int jtop = has1 ? i1 : i0;
@@ -139,42 +169,52 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   // softmax group takes 224 (128*56 + 256*224 = 384*168).
   if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
   if (warp == kWarpProducer) {
-    if (lane == 0) {
+    // The whole warp runs the loop (converged, uniform operands); one elected lane issues each copy.
+    if (elect_one()) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
-      uint8_t* sq = smem + C::OFF_Q;
+    }
+    __syncwarp();
+    uint8_t* sq = smem + C::OFF_Q;
+    if (elect_one()) {
       mbar_expect_tx(q_full, (has1 ? 2 : 1) * C::TILEB);
       for (int bx = 0; bx < C::NBOX; ++bx) {
         tma_load_4d(sq + bx * C::BOXB, &tq, bx * C::BOXC, i0 * kBT, h, b, q_full);
         if (has1) tma_load_4d(sq + C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i1 * kBT, h, b, q_full);
       }
-      bool ok = true;
-      const size_t colbase = size_t(z) * p.TP;
-      for (int k = 0; k < nsteps && ok; ++k) {
-        const int st = k % C::NS, j = jtop - k;
-        if (k >= C::NS) ok = mbar_wait(kv_empty + st, ((k / C::NS) - 1) & 1, p.status, 1);
-        if (!ok) break;
-        uint8_t* sk = smem + C::OFF_K + st * C::TILEB;
-        uint8_t* sv = smem + C::OFF_V + st * C::TILEB;
-        uint8_t* sc = smem + C::OFF_COL + st * 3 * C::COLB;
+    }
+    __syncwarp();
+    bool ok = true;
+    const size_t colbase = size_t(z) * p.TP;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, j = jtop - k;
+      if (k >= C::NS) ok = mbar_wait(kv_empty + st, ((k / C::NS) - 1) & 1, p.status, 1);
+      if (!ok) break;
+      uint8_t* sk = smem + C::OFF_K + st * C::TILEB;
+      uint8_t* sv = smem + C::OFF_V + st * C::TILEB;
+      uint8_t* sc = smem + C::OFF_COL + st * 3 * C::COLB;
+      if (elect_one()) {
         mbar_expect_tx(k_full + st, C::TILEB + 3 * C::COLB);
-        for (int bx = 0; bx < C::NBOX; ++bx) tma_load_4d(sk + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, k_full + st);
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_4d(sk + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, k_full + st);
         bulk_load(sc, p.cola + colbase + size_t(j) * kBT, C::COLB, k_full + st);
         bulk_load(sc + C::COLB, p.colpsi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
         bulk_load(sc + 2 * C::COLB, p.colphi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
         mbar_expect_tx(v_full + st, C::TILEB);
-        for (int bx = 0; bx < C::NBOX; ++bx) tma_load_4d(sv + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, v_full + st);
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_4d(sv + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, v_full + st);
       }
-      // Drain: wait (bounded) until the copies this thread issued have landed before the CTA may exit.
-      mbar_wait(q_full, 0, p.status, 2);
-      for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k) {
-        mbar_wait(k_full + k % C::NS, (k / C::NS) & 1, p.status, 3);
-        mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 4);
-      }
+      __syncwarp();
+    }
+    // Drain: wait (bounded) until the copies this warp issued have landed before the CTA may exit.
+    mbar_wait(q_full, 0, p.status, 2);
+    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k) {
+      mbar_wait(k_full + k % C::NS, (k / C::NS) & 1, p.status, 3);
+      mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 4);
     }
   } else if (warp == kWarpMma) {
-    if (lane == 0) {
+    {  // whole warp, converged: operands stay warp-uniform; one elected lane issues each MMA
       const uint32_t q0 = smem_u32(smem + C::OFF_Q), q1 = q0 + C::TILEB;
       auto issue_s = [&](int x, int st) {
         const uint32_t qa = x == 0 ? q0 : q1;
@@ -182,7 +222,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
-          mma_ss(tmem + x * kBT, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
+          mma_ss_w(tmem + x * kBT, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
                  C::IDESC_S, kk > 0);
         }
       };
@@ -190,7 +230,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         const uint32_t va = smem_u32(smem + C::OFF_V + st * C::TILEB);
 #pragma unroll
         for (int kk = 0; kk < kBT / 16; ++kk) {
-          mma_ts(tmem + C::COL_O + x * D, tmem + x * kBT + kk * 8,
+          mma_ts_w(tmem + C::COL_O + x * D, tmem + x * kBT + kk * 8,
                  smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_O, (acc || kk > 0) ? 1u : 0u);
         }
       };
@@ -200,11 +240,11 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       if (ok) {
         if (k0 == 0) {
           issue_s(0, 0);
-          mma_commit(s_full + 0);
+          mma_commit_w(s_full + 0);
         }
         if (has1) {
           issue_s(1, 0);
-          mma_commit(s_full + 1);
+          mma_commit_w(s_full + 1);
         }
       }
       int cnt0 = 0, cnt1 = 0;
@@ -227,7 +267,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           tc_fence_after();
           if (k + 1 >= k0) {
             issue_s(0, st1);
-            mma_commit(s_full + 0);
+            mma_commit_w(s_full + 0);
           }
         }
         if (has1) {  // query tile i1 takes part in every step
@@ -237,16 +277,16 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           issue_pv(1, st, cnt1 > 0);
           ++cnt1;
         }
-        mma_commit(kv_empty + st);
+        mma_commit_w(kv_empty + st);
         if (more && has1) {
           issue_s(1, st1);
-          mma_commit(s_full + 1);
+          mma_commit_w(s_full + 1);
         }
       }
-      mma_commit(o_done + 0);
-      mma_commit(o_done + 1);
-      // Drain: every MMA issued by this thread has completed before TMEM can be released.
-      mma_commit(drain);
+      mma_commit_w(o_done + 0);
+      mma_commit_w(o_done + 1);
+      // Drain: every MMA issued by this warp has completed before TMEM can be released.
+      mma_commit_w(drain);
       mbar_wait(drain, 0, p.status, 16);
     }
   } else if (warp < 8) {
@@ -266,85 +306,110 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     int cnt = 0;
     bool ok = active_wg;
     const int kfirst = x == 0 ? k0 : 0;
-    for (int k = kfirst; k < nsteps && ok; ++k) {
-      const int j = jtop - k, st = k % C::NS;
-      ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 20);
-      if (ok) ok = mbar_wait(s_full + x, cnt & 1, p.status, 21);
-      if (!ok) break;
-      tc_fence_after();
-      float s[kBT];
+    // The bias in log2 units is b' * min(0, x) with b' = beta * log2 e. For b' >= 0 that is a minimum of the
+    // pre-scaled per-key terms; for b' < 0 every minimum becomes a maximum (NEG).
+    auto run = [&](auto neg_tag) {
+      constexpr bool NEG = decltype(neg_tag)::value;
+      auto ext = [](float a, float b2) { return NEG ? fmaxf(a, b2) : fminf(a, b2); };
+      const float2 sc2 = make_float2(p.scale2, p.scale2);
+      for (int k = kfirst; k < nsteps && ok; ++k) {
+        const int j = jtop - k, st = k % C::NS;
+        ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 20);
+        if (ok) ok = mbar_wait(s_full + x, cnt & 1, p.status, 21);
+        if (!ok) break;
+        tc_fence_after();
+        float s[kBT];
 #pragma unroll
-      for (int c = 0; c < kBT / 32; ++c) tmem_ld32(tl + col_s + c * 32, s + c * 32);
-      tmem_ld_wait();
-      const float* ca = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB);
-      const float* cpsi = ca + kBT;
-      const float* cphi = ca + 2 * kBT;
-      if (j == i) {
-        // Diagonal tile: keys from the row down, carrying rmin = min_{s<u<=t} phi_u.
-        float rmin = kInf;
-        const int lim = min(r, p.T - 1 - j * kBT);  // last valid key of this row
+        for (int c = 0; c < kBT / 32; ++c) tmem_ld32(tl + col_s + c * 32, s + c * 32);
+        tmem_ld_wait();
+        const float* cA = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB);  // b'*min(SUF-psi,0)
+        const float* cE = cA + kBT;                                                               // -b'*psi
+        const float* cF = cA + 2 * kBT;                                                           // b'*phi
+        if (j == i) {
+          // Diagonal tile: keys from the row down; rr = extremum of b'*phi over (key, row] (+-inf when empty).
+          float rr = NEG ? -kInf : kInf;
+          const int lim = min(r, p.T - 1 - j * kBT);  // last valid key of this row
 #pragma unroll
-        for (int c = kBT - 1; c >= 0; --c) {
-          const float xm = fminf(rmin - cpsi[c], 0.f);
-          const float v = fmaf(betal, xm, s[c] * p.scale2);
-          s[c] = c <= lim ? v : -kInf;
-          if (c <= r) rmin = fminf(rmin, cphi[c]);
+          for (int c = kBT - 1; c >= 0; --c) {
+            const float bias = ext(0.f, rr + cE[c]);
+            const float v = fmaf(s[c], p.scale2, bias);
+            s[c] = c <= lim ? v : -kInf;
+            if (c <= r) rr = ext(rr, cF[c]);
+          }
+        } else {
+          // Off the diagonal: bias = ext(a_s, b' * min(mid, PRE_t) - b' * psi_s), two keys per packed op.
+          const float R = betal * fminf(mid, pre_t);
+          const float2 R2 = make_float2(R, R);
+#pragma unroll
+          for (int c = 0; c < kBT; c += 2) {
+            const float2 e2 = *reinterpret_cast<const float2*>(cE + c);
+            const float2 a2 = *reinterpret_cast<const float2*>(cA + c);
+            const float2 tt = __fadd2_rn(R2, e2);
+            const float2 bias = make_float2(ext(a2.x, tt.x), ext(a2.y, tt.y));
+            const float2 v = __ffma2_rn(make_float2(s[c], s[c + 1]), sc2, bias);
+            s[c] = v.x;
+            s[c + 1] = v.y;
+          }
+          mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
         }
-      } else {
-        const float cap = fminf(mid, pre_t);
+        float m4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-        for (int c = 0; c < kBT; ++c) {
-          const float xm = fminf(ca[c], cap - cpsi[c]);
-          s[c] = fmaf(betal, xm, s[c] * p.scale2);
+        for (int c = 4; c < kBT; c += 4) {
+          m4[0] = fmaxf(m4[0], s[c]);
+          m4[1] = fmaxf(m4[1], s[c + 1]);
+          m4[2] = fmaxf(m4[2], s[c + 2]);
+          m4[3] = fmaxf(m4[3], s[c + 3]);
         }
-        mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
-      }
-      float m4[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-      for (int c = 4; c < kBT; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
-      const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      // Lazy rescaling of the running maximum.
-      const float mnew = fmaxf(mrow, mt);
-      bool need = false;
-      float alpha = 1.f;
-      if (cnt == 0) {
-        mrow = mnew;
-      } else if (mnew > mrow + kRescaleThreshold) {
-        need = true;
-        alpha = ex2(mrow - mnew);
-        mrow = mnew;
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        lrow *= alpha;
-#pragma unroll
-        for (int c = 0; c < D; c += 16) {
-          float o[16];
-          tmem_ld16(tl + col_o + c, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] *= alpha;
-          tmem_st16(tl + col_o + c, reinterpret_cast<const uint32_t*>(o));
+        const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        // Lazy rescaling of the running maximum.
+        const float mnew = fmaxf(mrow, mt);
+        bool need = false;
+        float alpha = 1.f;
+        if (cnt == 0) {
+          mrow = mnew;
+        } else if (mnew > mrow + kRescaleThreshold) {
+          need = true;
+          alpha = ex2(mrow - mnew);
+          mrow = mnew;
         }
-      }
-      float ls[2] = {0.f, 0.f};
+        if (__any_sync(0xffffffffu, need)) {
+          lrow *= alpha;
 #pragma unroll
-      for (int c0 = 0; c0 < kBT; c0 += 32) {
-        uint32_t pk[16];
+          for (int c = 0; c < D; c += 16) {
+            float o[16];
+            tmem_ld16(tl + col_o + c, o);
+            tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2(s[c0 + e] - mrow), p1 = ex2(s[c0 + e + 1] - mrow);
-          ls[0] += p0;
-          ls[1] += p1;
-          pk[e / 2] = pack_half2(p0, p1);
+            for (int e = 0; e < 16; ++e) o[e] *= alpha;
+            tmem_st16(tl + col_o + c, reinterpret_cast<const uint32_t*>(o));
+          }
         }
-        tmem_st16(tl + col_s + c0 / 2, pk);
+        const float2 nm2 = make_float2(-mrow, -mrow);
+        float2 ls = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c0 = 0; c0 < kBT; c0 += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 xx = __fadd2_rn(make_float2(s[c0 + e], s[c0 + e + 1]), nm2);
+            const bool emu = kEmuEvery > 0 && ((c0 + e) / 2) % (kEmuEvery > 0 ? kEmuEvery : 1) == 0;
+            const float2 pp = emu ? ex2_poly2(xx) : make_float2(ex2(xx.x), ex2(xx.y));
+            ls = __fadd2_rn(ls, pp);
+            pk[e / 2] = pack_half2(pp.x, pp.y);
+          }
+          tmem_st16(tl + col_s + c0 / 2, pk);
+        }
+        lrow += ls.x + ls.y;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full + x);
+        ++cnt;
       }
-      lrow += ls[0] + ls[1];
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full + x);
-      ++cnt;
-    }
+    };
+    if (betal < 0.f)
+      run(std::true_type{});
+    else
+      run(std::false_type{});
     if (ok && active_wg) ok = mbar_wait(o_done + x, 0, p.status, 22);
     if (ok && active_wg) {
       tc_fence_after();
@@ -381,53 +446,13 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-// Tensor map of a [B, H, T, D] fp16 operand (innermost stride 1) with boxes of [128 rows x BOXC columns].
-template <int D>
-bool make_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T) {
-  using C = TcFwdCfg<D>;
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(T), cuuint64_t(H), cuuint64_t(B)};
-  cuuint64_t strides[3] = {cuuint64_t(st[2]) * 2, cuuint64_t(st[1]) * 2, cuuint64_t(st[0]) * 2};
-  cuuint32_t box[4] = {cuuint32_t(C::BOXC), cuuint32_t(kBT), 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUtensorMapSwizzle sw = C::SWB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                          : C::SWB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                         : CU_TENSOR_MAP_SWIZZLE_32B;
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-bool tma_layout_ok(const void* p, const int64_t st[4]) {
-  if (reinterpret_cast<uintptr_t>(p) % 16) return false;
-  if (st[3] != 1) return false;
-  for (int i = 0; i < 3; ++i)
-    if ((st[i] * 2) % 16 || st[i] <= 0) return false;
-  return true;
-}
-
 template <int D>
 int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
            std::string* err) {
   using C = TcFwdCfg<D>;
   CUtensorMap mq, mk, mv;
-  if (!make_map<D>(&mq, a.q, a.q_stride, d.B, d.H, d.T) || !make_map<D>(&mk, a.k, a.k_stride, d.B, d.H, d.T) ||
-      !make_map<D>(&mv, a.v, a.v_stride, d.B, d.H, d.T)) {
+  if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
+      !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D)) {
     *err = "cuTensorMapEncodeTiled failed for q, k or v";
     return FPA_ERR_CUDA;
   }
@@ -450,13 +475,14 @@ int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
   p.o_st = a.o_stride[2];
   p.lse = a.lse;
   p.status = status;
+  p.B = d.B;
   p.H = d.H;
   p.T = d.T;
   p.NB = d.NB;
   p.TP = d.TP;
+  p.NPAIR = (d.NB + 1) / 2;
   p.scale2 = float(1.0 / sqrt(double(D))) * kLog2e;
-  dim3 grid((d.NB + 1) / 2, d.BH());
-  fn<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, p);
+  fn<<<p.NPAIR * d.BH(), kThreads, C::SMEM, s>>>(mq, mk, mv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);

@@ -1,0 +1,51 @@
+// Host-side TMA tensor maps for the tensor-core kernels.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fpa_tc.h"
+
+namespace fpa {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool tma_layout_ok(const void* p, const int64_t st[4]) {
+  if (reinterpret_cast<uintptr_t>(p) % 16) return false;
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((st[i] * 2) % 16 || st[i] <= 0) return false;
+  return true;
+}
+
+bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T, int D) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int boxc = D >= 64 ? 64 : D;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(T), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t strides[3] = {cuuint64_t(st[2]) * 2, cuuint64_t(st[1]) * 2, cuuint64_t(st[0]) * 2};
+  cuuint32_t box[4] = {cuuint32_t(boxc), cuuint32_t(kTcBT), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMapSwizzle sw = boxc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : boxc == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                       : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace fpa
