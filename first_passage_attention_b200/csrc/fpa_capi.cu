@@ -49,10 +49,8 @@ int pick_path(int requested, int dtype, int D) {
 
 int tile_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcBT : fpa::kSimtBT; }
 
-// The backward kernels of this build are the FFMA kernels for every dtype; the path choice affects the forward.
-int bwd_path(int requested, int dtype, int D) {
-  return pick_path(requested, dtype, D) < 0 ? -1 : FPA_PATH_SIMT;
-}
+// The backward follows the same choice as the forward: tensor cores for fp16 with a supported D, FFMA otherwise.
+int bwd_path(int requested, int dtype, int D) { return pick_path(requested, dtype, D); }
 
 size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
@@ -61,7 +59,8 @@ size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
 
 size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
-  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d);
+  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d) +
+         (path == FPA_PATH_TENSOR ? fpa::tc_bwd_extra_bytes(d) : 0);
 }
 
 }  // namespace
@@ -142,20 +141,32 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   fpa::Stats st = fpa::carve_stats(ws, d);
   fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d);
   int n = 0;
-  cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr},
-                                    0, status, s);
-  if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
-  ++n;
-  e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta,
-                        nullptr, nullptr, s);
-  if (e != cudaSuccess) return cuda_fail(e, "delta kernel");
-  ++n;
-  e = fpa::simt_bwd_kv(*a, d, st, sc, s);
-  if (e != cudaSuccess) return cuda_fail(e, "kv-pass kernel");
-  ++n;
-  e = fpa::simt_bwd_q(*a, d, st, sc, s);
-  if (e != cudaSuccess) return cuda_fail(e, "q-pass kernel");
-  ++n;
+  cudaError_t e;
+  if (path == FPA_PATH_TENSOR) {
+    char* extra = ws + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d);
+    int m = 0;
+    rc = fpa::tc_bwd(*a, d, st, sc, extra, status, s, &m, &g_last_error);
+    n += m;
+    if (rc) {
+      a->kernels_launched = n;
+      return rc;
+    }
+  } else {
+    e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr}, 0, status,
+                          s);
+    if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
+    ++n;
+    e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta,
+                          nullptr, nullptr, s);
+    if (e != cudaSuccess) return cuda_fail(e, "delta kernel");
+    ++n;
+    e = fpa::simt_bwd_kv(*a, d, st, sc, s);
+    if (e != cudaSuccess) return cuda_fail(e, "kv-pass kernel");
+    ++n;
+    e = fpa::simt_bwd_q(*a, d, st, sc, s);
+    if (e != cudaSuccess) return cuda_fail(e, "q-pass kernel");
+    ++n;
+  }
   e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, s);
   if (e != cudaSuccess) return cuda_fail(e, "dphi kernel");
   ++n;

@@ -26,4 +26,11 @@ bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int 
 int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
            int* launched, std::string* err);
 
+// Backward pass on the tensor cores (fp16). `extra` is tc_bwd_extra_bytes(d) bytes of workspace (raw key vectors,
+// the stored g of the diagonal tiles, a padded copy of lse). Launches the field statistics, delta, the kv-pass,
+// the diagonal soft-min and the q-pass; the caller then runs the dphi combination and the dbeta reduction.
+size_t tc_bwd_extra_bytes(const Dims& d);
+int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
+           cudaStream_t s, int* launched, std::string* err);
+
 }  // namespace fpa

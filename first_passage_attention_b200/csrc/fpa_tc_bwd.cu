@@ -1,0 +1,730 @@
+// Tensor-core backward pass of FPA for sm_100a (fp16 operands, fp32 accumulation), in two deterministic passes
+// with the decomposition of the reference's backward (kernel.py:178-265 kv-pass, 287-340 q-pass):
+//
+//   tc_bwd_kv_kernel  one CTA per key tile j (128 keys) of one head, query tiles i = j .. NB-1:
+//                     S^T = K Q^T and dP^T = V dO^T into TMEM; thread = key computes P^T, dS^T (fp16, back into
+//                     TMEM over S^T and dP^T), then dV += P^T dO and dK += dS^T Q on the tensor cores. Also dpsi,
+//                     the dbeta partial, the soft-min sums W (u in the key's tile) and TB (u strictly between the
+//                     tiles), and g of the diagonal tile (stored for diag_dphi_kernel).
+//   tc_bwd_q_kernel   one CTA per query tile i, key tiles j = i .. 0: S = Q K^T, dP = dO V^T; thread = query
+//                     computes dS (fp16, into its own TMEM columns) and dQ += dS K; also r_t and from it the
+//                     soft-min part with u in the query's tile (DPHI2).
+//
+// Warp roles (192 threads): warps 0-3 the row group (thread = TMEM lane), warp 4 the TMA producer (stationary
+// tiles once, streamed tiles and their per-row vectors through a 2-stage ring), warp 5 the MMA issuer (whole warp,
+// one elected lane issues). Every mbarrier wait is bounded (fpa::sm100::mbar_wait).
+#include <cuda.h>
+
+#include "fpa_sm100.cuh"
+#include "fpa_tc.h"
+
+namespace fpa {
+using namespace sm100;
+
+namespace {
+
+constexpr int kBT = kTcBT;
+constexpr int kThreads = 192;
+constexpr int kWarpProducer = 4;
+constexpr int kWarpMma = 5;
+constexpr int kNamedBarRows = 1;  // bar.sync id used by the 128 row threads
+
+template <int D>
+struct TcBwdCfg {
+  static constexpr int BOXC = D >= 64 ? 64 : D;
+  static constexpr int NBOX = D / BOXC;
+  static constexpr int SWB = BOXC * 2;
+  static constexpr int BOXB = kBT * SWB;
+  static constexpr int TILEB = NBOX * BOXB;
+  static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
+  static constexpr int NS = 2;
+  static constexpr int NVEC = 5;
+  static constexpr int VECB = kBT * 4;
+  static constexpr int OFF_A = 0;                        // stationary operand 1
+  static constexpr int OFF_B = TILEB;                    // stationary operand 2
+  static constexpr int OFF_S1 = 2 * TILEB;               // streamed operand 1 [NS]
+  static constexpr int OFF_S2 = OFF_S1 + NS * TILEB;     // streamed operand 2 [NS]
+  static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][NVEC][128] floats
+  static constexpr int OFF_RED = OFF_VEC + NS * NVEC * VECB;  // 3 * 128 floats of row-group scratch
+  static constexpr int OFF_BAR = OFF_RED + 3 * kBT * 4;
+  static constexpr int NBAR = 1 + 2 * NS + 4;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
+  static constexpr uint32_t IDESC_ACC = idesc_f16(kBT, D, 1);
+  static constexpr int COL_S = 0, COL_P = kBT, COL_A1 = 2 * kBT, COL_A2 = 2 * kBT + D;
+};
+
+struct TcBwdParams {
+  // per-head [BH][TP] arrays (padded, tiles of 128)
+  const float* lsep;
+  const float* delta;
+  const float* pre;
+  const float* prel;
+  const float* suf;
+  const float* sufl;
+  const float* bmin;   // [BH][NB]
+  const float* bl;     // [BH][NB]
+  const float* xs;     // SUF - psi (raw key vectors)
+  const float* psi;    // psi
+  const float* phi;    // phi (+inf beyond T)
+  const float* beta;   // [H]
+  // outputs
+  __half* dq;
+  __half* dk;
+  __half* dv;
+  int64_t dq_s[3], dk_s[3], dv_s[3];  // b, h, t strides (d stride 1)
+  float* dpsi;         // [BH][T]
+  float* w;            // [BH][TP]
+  float* tb;           // [BH][NB][NB]
+  float* dbeta;        // [BH][NB]
+  float* gd;           // [BH][NB][128][128]
+  float* dphi2;        // [BH][TP]
+  int* status;
+  int B, H, T, NB, TP;
+  float scale, scale2, il2;
+};
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void rows_sync() { asm volatile("bar.sync %0, 128;" ::"r"(kNamedBarRows) : "memory"); }
+
+// Deterministic sum over the 128 row threads (fixed shuffle tree, then the 4 warp partials in order). All 128
+// threads call it; the result is returned to every thread.
+__device__ __forceinline__ float rows_sum(float v, float* red) {
+  v = group_sum<32>(v);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  rows_sync();
+  const float r = (red[0] + red[1]) + (red[2] + red[3]);
+  rows_sync();
+  return r;
+}
+
+template <int D>
+__device__ __forceinline__ void issue_ss(uint32_t d, uint32_t a, uint32_t b) {
+  using C = TcBwdCfg<D>;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
+    mma_ss_w(d, smem_desc(a + off, 16, 8 * C::SWB, C::SW), smem_desc(b + off, 16, 8 * C::SWB, C::SW), C::IDESC_S,
+             kk > 0);
+  }
+}
+
+// D[128 x D] (+)= A[128 x 128 from TMEM, fp16 packed] * B[128 x D from smem, N-contiguous].
+template <int D>
+__device__ __forceinline__ void issue_ts(uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
+  using C = TcBwdCfg<D>;
+#pragma unroll
+  for (int kk = 0; kk < kBT / 16; ++kk)
+    mma_ts_w(d, a_tmem + kk * 8, smem_desc(b + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_ACC,
+             (acc || kk > 0) ? 1u : 0u);
+}
+
+// ------------------------------------------------------------------------------------------------ kv-pass ----
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                 const TcBwdParams p) {
+  using C = TcBwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* a_full = bars;
+  uint64_t* st_full = bars + 1;
+  uint64_t* st_empty = st_full + C::NS;
+  uint64_t* s_full = st_empty + C::NS;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* acc_done = p_full + 1;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbh = p.B * p.H;
+  const int j = int(blockIdx.x) / nbh;  // key tile 0 has the most query tiles: first in launch order
+  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
+  const int nsteps = p.NB - j;
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(st_full + s, 1);
+      mbar_init(st_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const size_t zb = size_t(z) * p.TP;
+
+  if (warp == kWarpProducer) {
+    if (elect_one()) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      prefetch_tmap(&tdo);
+      mbar_expect_tx(a_full, 2 * C::TILEB);
+      for (int bx = 0; bx < C::NBOX; ++bx) {
+        tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
+        tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
+      }
+    }
+    __syncwarp();
+    bool ok = true;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, i = j + k;
+      if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 101);
+      if (!ok) break;
+      if (elect_one()) {
+        uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
+        mbar_expect_tx(st_full + st, 2 * C::TILEB + C::NVEC * C::VECB);
+        for (int bx = 0; bx < C::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, st_full + st);
+          tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b,
+                      st_full + st);
+        }
+        const size_t off = zb + size_t(i) * kBT;
+        bulk_load(vec + 0 * C::VECB, p.lsep + off, C::VECB, st_full + st);
+        bulk_load(vec + 1 * C::VECB, p.delta + off, C::VECB, st_full + st);
+        bulk_load(vec + 2 * C::VECB, p.pre + off, C::VECB, st_full + st);
+        bulk_load(vec + 3 * C::VECB, p.prel + off, C::VECB, st_full + st);
+        bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
+      }
+      __syncwarp();
+    }
+    mbar_wait(a_full, 0, p.status, 102);
+    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
+      mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 103);
+  } else if (warp == kWarpMma) {
+    const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
+    const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
+    bool ok = mbar_wait(a_full, 0, p.status, 110);
+    if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 111);
+    tc_fence_after();
+    if (ok) {
+      issue_ss<D>(tmem + C::COL_S, sa, s1);  // S^T  = K Q^T
+      issue_ss<D>(tmem + C::COL_P, sb, s2);  // dP^T = V dO^T
+      mma_commit_w(s_full);
+    }
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS;
+      ok = mbar_wait(p_full, k & 1, p.status, 112);
+      if (!ok) break;
+      tc_fence_after();
+      issue_ts<D>(tmem + C::COL_A1, tmem + C::COL_S, s2 + st * C::TILEB, k > 0);  // dV += P^T dO
+      issue_ts<D>(tmem + C::COL_A2, tmem + C::COL_P, s1 + st * C::TILEB, k > 0);  // dK += dS^T Q
+      mma_commit_w(st_empty + st);
+      if (k + 1 < nsteps) {
+        const int st1 = (k + 1) % C::NS;
+        ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 113);
+        if (!ok) break;
+        tc_fence_after();
+        issue_ss<D>(tmem + C::COL_S, sa, s1 + st1 * C::TILEB);
+        issue_ss<D>(tmem + C::COL_P, sb, s2 + st1 * C::TILEB);
+        mma_commit_w(s_full);
+      }
+    }
+    mma_commit_w(acc_done);
+    mma_commit_w(drain);
+    mbar_wait(drain, 0, p.status, 114);
+  } else if (warp < 4) {
+    const int r = threadIdx.x;  // key within the tile = TMEM lane
+    const int s = j * kBT + r;
+    const bool s_ok = s < p.T;
+    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const float bh = p.beta[h], betal = bh * kLog2e;
+    const float psi_s = p.psi[zb + s];
+    const float xs_s = p.xs[zb + s];    // SUF_s - psi_s (+inf for the last key of the tile)
+    const float suf_s = p.suf[zb + s];
+    const float sufl_s = p.sufl[zb + s];
+    const float c2_s = suf_s < kInf ? -suf_s * p.il2 : -kInf;
+    const float* bmin = p.bmin + size_t(z) * p.NB;
+    const float* bl = p.bl + size_t(z) * p.NB;
+    float gsum = 0.f, dbsum = 0.f, wsum = 0.f;
+    float mid = kInf, midl = -kInf;
+    bool ok = true;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, i = j + k;
+      ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 120);
+      if (ok) ok = mbar_wait(s_full, k & 1, p.status, 121);
+      if (!ok) break;
+      tc_fence_after();
+      const float* vec = reinterpret_cast<const float*>(smem + C::OFF_VEC + st * C::NVEC * C::VECB);
+      const float* vlse = vec;
+      const float* vdel = vec + kBT;
+      const float* vpre = vec + 2 * kBT;
+      const float* vprel = vec + 3 * kBT;
+      const float* vphi = vec + 4 * kBT;
+      const bool diag = k == 0;
+      const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
+      float rs = fmaxf(c2_s, cmid2);
+      const bool vrs = !diag && rs > -kInf;
+      rs = vrs ? rs : 0.f;
+      const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
+      const int tvalid = p.T - i * kBT;  // queries c < tvalid exist
+      float rr = kInf, fsum = 0.f;
+      float* grow = p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBT; c0 += 32) {
+        float sS[32], sP[32];
+        tmem_ld32(tl + C::COL_S + c0, sS);
+        tmem_ld32(tl + C::COL_P + c0, sP);
+        tmem_ld_wait();
+        uint32_t ppk[16], dpk[16];
+        float gbuf[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int c = c0 + e;
+          const bool valid = s_ok && c < tvalid && (!diag || c >= r);
+          float x;
+          if (diag) {
+            if (c > r) rr = fminf(rr, vphi[c]);
+            x = rr - psi_s;  // +inf for c <= r
+          } else {
+            x = fminf(xs_s, fminf(mid, vpre[c]) - psi_s);
+          }
+          const float xm = fminf(x, 0.f);
+          const float sv = fmaf(sS[e], p.scale2, betal * xm);
+          const float pp = valid ? ex2(sv - vlse[c]) : 0.f;
+          const float ds = valid ? pp * (sP[e] - vdel[c]) : 0.f;
+          const float g = (valid && x <= 0.f) ? ds : 0.f;
+          gsum += g;
+          dbsum += ds * xm;
+          if (vrs) fsum += g * rcp_approx(sv_ + ex2(vprel[c] - rs));
+          gbuf[e] = g;
+          sS[e] = pp;
+          sP[e] = ds;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
+          dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+        }
+        tmem_st16(tl + C::COL_S + c0 / 2, ppk);
+        tmem_st16(tl + C::COL_P + c0 / 2, dpk);
+        if (diag) {
+          float4* dst = reinterpret_cast<float4*>(grow + c0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dst[e] = make_float4(gbuf[4 * e], gbuf[4 * e + 1], gbuf[4 * e + 2], gbuf[4 * e + 3]);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (!diag) {
+        if (vrs) wsum += ex2(c2_s - rs) * fsum;
+        if (i > j + 1) {
+          const float tot = rows_sum(vrs ? ex2(cmid2 - rs) * fsum : 0.f, red);
+          if (r == 0) p.tb[(size_t(z) * p.NB + i) * p.NB + j] = tot;
+        }
+        mid = fminf(mid, bmin[i]);
+        midl = lse2(midl, bl[i]);
+      }
+    }
+    if (ok) ok = mbar_wait(acc_done, 0, p.status, 122);
+    if (ok) {
+      tc_fence_after();
+      __half* dvrow = p.dv + b * p.dv_s[0] + h * p.dv_s[1] + int64_t(s_ok ? s : 0) * p.dv_s[2];
+      __half* dkrow = p.dk + b * p.dk_s[0] + h * p.dk_s[1] + int64_t(s_ok ? s : 0) * p.dk_s[2];
+#pragma unroll
+      for (int c = 0; c < D; c += 16) {
+        float a1[16], a2[16];
+        tmem_ld16(tl + C::COL_A1 + c, a1);
+        tmem_ld16(tl + C::COL_A2 + c, a2);
+        tmem_ld_wait();
+        if (s_ok) {
+          uint32_t u1[8], u2[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            u1[e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
+            u2[e] = pack_half2(a2[2 * e] * p.scale, a2[2 * e + 1] * p.scale);
+          }
+          reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(u1[0], u1[1], u1[2], u1[3]);
+          reinterpret_cast<uint4*>(dvrow + c)[1] = make_uint4(u1[4], u1[5], u1[6], u1[7]);
+          reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(u2[0], u2[1], u2[2], u2[3]);
+          reinterpret_cast<uint4*>(dkrow + c)[1] = make_uint4(u2[4], u2[5], u2[6], u2[7]);
+        }
+      }
+      if (s_ok) {
+        p.dpsi[size_t(z) * p.T + s] = -bh * gsum;
+        p.w[zb + s] = wsum;
+      }
+    }
+    const float db = rows_sum(dbsum, red);
+    if (r == 0) p.dbeta[size_t(z) * p.NB + j] = db;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------- q-pass ----
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                const TcBwdParams p) {
+  using C = TcBwdCfg<D>;
+  constexpr int COL_DS = C::COL_A1 + D;  // dS (fp16, 64 columns) in its own columns
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* a_full = bars;
+  uint64_t* st_full = bars + 1;
+  uint64_t* st_empty = st_full + C::NS;
+  uint64_t* s_full = st_empty + C::NS;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* acc_done = p_full + 1;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+
+  const int warp = threadIdx.x >> 5;
+  const int nbh = p.B * p.H;
+  const int i = p.NB - 1 - int(blockIdx.x) / nbh;  // longest query tiles first
+  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
+  const int nsteps = i + 1;                         // key tiles j = i, i-1, ..., 0
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(st_full + s, 1);
+      mbar_init(st_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const size_t zb = size_t(z) * p.TP;
+
+  if (warp == kWarpProducer) {
+    if (elect_one()) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      prefetch_tmap(&tdo);
+      mbar_expect_tx(a_full, 2 * C::TILEB);
+      for (int bx = 0; bx < C::NBOX; ++bx) {
+        tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, a_full);
+        tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b, a_full);
+      }
+    }
+    __syncwarp();
+    bool ok = true;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, j = i - k;
+      if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 201);
+      if (!ok) break;
+      if (elect_one()) {
+        uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
+        mbar_expect_tx(st_full + st, 2 * C::TILEB + 4 * C::VECB);
+        for (int bx = 0; bx < C::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, st_full + st);
+          tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, st_full + st);
+        }
+        const size_t off = zb + size_t(j) * kBT;
+        bulk_load(vec + 0 * C::VECB, p.xs + off, C::VECB, st_full + st);
+        bulk_load(vec + 1 * C::VECB, p.psi + off, C::VECB, st_full + st);
+        bulk_load(vec + 2 * C::VECB, p.sufl + off, C::VECB, st_full + st);
+        bulk_load(vec + 3 * C::VECB, p.phi + off, C::VECB, st_full + st);
+      }
+      __syncwarp();
+    }
+    mbar_wait(a_full, 0, p.status, 202);
+    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
+      mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 203);
+  } else if (warp == kWarpMma) {
+    const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
+    const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
+    bool ok = mbar_wait(a_full, 0, p.status, 210);
+    if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 211);
+    tc_fence_after();
+    if (ok) {
+      issue_ss<D>(tmem + C::COL_S, sa, s1);  // S  = Q K^T
+      issue_ss<D>(tmem + C::COL_P, sb, s2);  // dP = dO V^T
+      mma_commit_w(s_full);
+    }
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS;
+      ok = mbar_wait(p_full, k & 1, p.status, 212);
+      if (!ok) break;
+      tc_fence_after();
+      issue_ts<D>(tmem + C::COL_A1, tmem + COL_DS, s1 + st * C::TILEB, k > 0);  // dQ += dS K
+      mma_commit_w(st_empty + st);
+      if (k + 1 < nsteps) {
+        const int st1 = (k + 1) % C::NS;
+        ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 213);
+        if (!ok) break;
+        tc_fence_after();
+        issue_ss<D>(tmem + C::COL_S, sa, s1 + st1 * C::TILEB);
+        issue_ss<D>(tmem + C::COL_P, sb, s2 + st1 * C::TILEB);
+        mma_commit_w(s_full);
+      }
+    }
+    mma_commit_w(acc_done);
+    mma_commit_w(drain);
+    mbar_wait(drain, 0, p.status, 214);
+  } else if (warp < 4) {
+    const int r = threadIdx.x;  // query within the tile = TMEM lane
+    const int t = i * kBT + r;
+    const bool t_ok = t < p.T;
+    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const float betal = p.beta[h] * kLog2e;
+    const float lse_t = p.lsep[zb + t];
+    const float del_t = t_ok ? p.delta[zb + t] : 0.f;
+    const float pre_t = p.pre[zb + t];
+    const float prel_t = p.prel[zb + t];
+    const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
+    const float bpre = t_ok ? ex2(prel_t - c2_t) : 1.f;
+    const float* bmin = p.bmin + size_t(z) * p.NB;
+    const float* bl = p.bl + size_t(z) * p.NB;
+    float racc = 0.f, mid = kInf, midl = -kInf;
+    bool ok = true;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, j = i - k;
+      ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 220);
+      if (ok) ok = mbar_wait(s_full, k & 1, p.status, 221);
+      if (!ok) break;
+      tc_fence_after();
+      const float* vec = reinterpret_cast<const float*>(smem + C::OFF_VEC + st * C::NVEC * C::VECB);
+      const float* vxs = vec;
+      const float* vpsi = vec + kBT;
+      const float* vsufl = vec + 2 * kBT;
+      const float* vphi = vec + 3 * kBT;
+      const bool diag = k == 0;
+      const float cap = fminf(mid, pre_t);
+      const float mterm = ex2(midl - c2_t) + bpre;
+      const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
+      float rr = kInf;
+      // Keys in descending order so the diagonal tile can carry rr = min_{key<u<=t} phi_u.
+#pragma unroll 1
+      for (int c0 = kBT - 32; c0 >= 0; c0 -= 32) {
+        float sS[32], sP[32];
+        tmem_ld32(tl + C::COL_S + c0, sS);
+        tmem_ld32(tl + C::COL_P + c0, sP);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 31; e >= 0; --e) {
+          const int c = c0 + e;
+          const bool valid = t_ok && c < kvalid && (!diag || c <= r);
+          float x;
+          if (diag) {
+            x = rr - vpsi[c];  // +inf at c == r
+            if (c <= r) rr = fminf(rr, vphi[c]);
+          } else {
+            x = fminf(vxs[c], cap - vpsi[c]);
+          }
+          const float xm = fminf(x, 0.f);
+          const float sv = fmaf(sS[e], p.scale2, betal * xm);
+          const float pp = valid ? ex2(sv - lse_t) : 0.f;
+          const float ds = valid ? pp * (sP[e] - del_t) : 0.f;
+          if (!diag) {
+            const float g = (valid && x <= 0.f) ? ds : 0.f;
+            racc += g * rcp_approx(ex2(vsufl[c] - c2_t) + mterm);
+          }
+          sP[e] = ds;
+        }
+        uint32_t dpk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+        tmem_st16(tl + COL_DS + c0 / 2, dpk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (!diag) {
+        mid = fminf(mid, bmin[j]);
+        midl = lse2(midl, bl[j]);
+      }
+    }
+    if (ok) ok = mbar_wait(acc_done, 0, p.status, 222);
+    if (ok) {
+      tc_fence_after();
+      __half* dqrow = p.dq + b * p.dq_s[0] + h * p.dq_s[1] + int64_t(t_ok ? t : 0) * p.dq_s[2];
+#pragma unroll
+      for (int c = 0; c < D; c += 16) {
+        float a1[16];
+        tmem_ld16(tl + C::COL_A1 + c, a1);
+        tmem_ld_wait();
+        if (t_ok) {
+          uint32_t u[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) u[e] = pack_half2(a1[2 * e] * p.scale, a1[2 * e + 1] * p.scale);
+          reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(u[0], u[1], u[2], u[3]);
+          reinterpret_cast<uint4*>(dqrow + c)[1] = make_uint4(u[4], u[5], u[6], u[7]);
+        }
+      }
+    }
+    // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile).
+    float* rsh = red + kBT;
+    float* csh = red + 2 * kBT;
+    rsh[r] = racc;
+    csh[r] = c2_t;
+    rows_sync();
+    if (t_ok) {
+      const int tend = min(kBT, p.T - i * kBT);
+      const float a2 = -p.phi[zb + t] * p.il2;
+      float p2 = 0.f;
+      for (int t2 = r; t2 < tend; ++t2) p2 += ex2(a2 - csh[t2]) * rsh[t2];
+      p.dphi2[zb + t] = p2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
+               float* gd, float* lsep, int* status, cudaStream_t s, std::string* err) {
+  using C = TcBwdCfg<D>;
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
+      !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D) ||
+      !make_tile_map(&mdo, a.dout, a.dout_stride, d.B, d.H, d.T, D)) {
+    *err = "cuTensorMapEncodeTiled failed for q, k, v or do";
+    return FPA_ERR_CUDA;
+  }
+  TcBwdParams p;
+  p.lsep = lsep;
+  p.delta = sc.delta;
+  p.pre = st.pre;
+  p.prel = st.prel;
+  p.suf = st.suf;
+  p.sufl = st.sufl;
+  p.bmin = st.bmin;
+  p.bl = st.bl;
+  p.xs = cols.a;
+  p.psi = cols.psi;
+  p.phi = cols.phi;
+  p.beta = a.beta;
+  p.dq = static_cast<__half*>(a.dq);
+  p.dk = static_cast<__half*>(a.dk);
+  p.dv = static_cast<__half*>(a.dv);
+  for (int q = 0; q < 3; ++q) {
+    p.dq_s[q] = a.dq_stride[q];
+    p.dk_s[q] = a.dk_stride[q];
+    p.dv_s[q] = a.dv_stride[q];
+  }
+  p.dpsi = a.dpsi;
+  p.w = sc.w;
+  p.tb = sc.tb;
+  p.dbeta = sc.dbeta;
+  p.gd = gd;
+  p.dphi2 = sc.dphi2;
+  p.status = status;
+  p.B = d.B;
+  p.H = d.H;
+  p.T = d.T;
+  p.NB = d.NB;
+  p.TP = d.TP;
+  p.scale = float(1.0 / sqrt(double(D)));
+  p.scale2 = p.scale * kLog2e;
+  p.il2 = kLog2e / a.tau;
+  auto kv = tc_bwd_kv_kernel<D>;
+  auto qk = tc_bwd_q_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core backward: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  const int grid = d.NB * d.BH();
+  kv<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    e = launch_diag_dphi(a.phi, gd, d, a.tau, sc.dphi4, s);
+  }
+  if (e == cudaSuccess) {
+    qk<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core backward launch: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  return FPA_OK;
+}
+
+}  // namespace
+
+size_t tc_bwd_extra_bytes(const Dims& d) {
+  const size_t bh = size_t(d.BH());
+  return keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * sizeof(float)) +
+         align256(bh * d.TP * sizeof(float));
+}
+
+int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
+           cudaStream_t s, int* launched, std::string* err) {
+  *launched = 0;
+  if (!tma_layout_ok(a.q, a.q_stride) || !tma_layout_ok(a.k, a.k_stride) || !tma_layout_ok(a.v, a.v_stride) ||
+      !tma_layout_ok(a.dout, a.dout_stride)) {
+    *err = "the tensor-core path needs q, k, v, do with unit innermost stride and 16-byte aligned rows";
+    return FPA_ERR_UNSUPPORTED;
+  }
+  for (const void* ptr : {a.dq, a.dk, a.dv})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) {
+      *err = "the tensor-core path needs 16-byte aligned dq, dk, dv";
+      return FPA_ERR_UNSUPPORTED;
+    }
+  if (a.dq_stride[3] != 1 || a.dk_stride[3] != 1 || a.dv_stride[3] != 1 || (a.dq_stride[2] * 2) % 16 ||
+      (a.dk_stride[2] * 2) % 16 || (a.dv_stride[2] * 2) % 16) {
+    *err = "the tensor-core path needs dq, dk, dv with unit innermost stride and 16-byte aligned rows";
+    return FPA_ERR_UNSUPPORTED;
+  }
+  const size_t bh = size_t(d.BH());
+  KeyCols cols = carve_keycols(extra, d);
+  float* gd = reinterpret_cast<float*>(extra + keycols_bytes(d));
+  float* lsep = reinterpret_cast<float*>(extra + keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * 4));
+  // Raw key vectors and the padded lse copy (filled by the stats and delta kernels of this call).
+  cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s);
+  if (e == cudaSuccess)
+    e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, a.lse, lsep, s);
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core backward prologue: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  int rc;
+  switch (d.D) {
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
+    default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
+  }
+  if (rc == FPA_OK) *launched = 5;  // stats, delta, kv-pass, diagonal dphi, q-pass
+  return rc;
+}
+
+}  // namespace fpa
