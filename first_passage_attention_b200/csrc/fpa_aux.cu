@@ -167,9 +167,60 @@ __global__ void delta_kernel(const TIn* __restrict__ o, Str4 so, const TIn* __re
   }
 }
 
+// fp16 with unit innermost stride and 16-byte aligned rows: G = D / 8 lanes per row, 16-byte loads.
+template <int G>
+__global__ void delta_f16_vec_kernel(const __half* __restrict__ o, Str4 so, const __half* __restrict__ dout, Str4 sdo,
+                                     int H, int T, int TP, int rows, float* __restrict__ delta,
+                                     const float* __restrict__ lse, float* __restrict__ lsep) {
+  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = gid / G, part = gid % G;
+  const bool ok = row < rows;
+  float acc = 0.f;
+  int z = 0, t = 0;
+  if (ok) {
+    z = row / T;
+    t = row % T;
+    const int b = z / H, h = z % H;
+    const uint4 a = *reinterpret_cast<const uint4*>(o + b * so.b + h * so.h + int64_t(t) * so.t + part * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(dout + b * sdo.b + h * sdo.h + int64_t(t) * sdo.t + part * 8);
+    const __half2* ah = reinterpret_cast<const __half2*>(&a);
+    const __half2* ch = reinterpret_cast<const __half2*>(&c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 x = __half22float2(ah[q]), y = __half22float2(ch[q]);
+      acc = fmaf(x.x, y.x, acc);
+      acc = fmaf(x.y, y.y, acc);
+    }
+  }
+  acc = group_sum<G>(acc);
+  if (ok && part == 0) {
+    delta[size_t(z) * TP + t] = acc;
+    if (lsep) lsep[size_t(z) * TP + t] = lse[size_t(z) * T + t];
+  }
+}
+
+static bool vec16_ok(const void* p, Str4 s) {
+  return reinterpret_cast<uintptr_t>(p) % 16 == 0 && s.d == 1 && (s.t * 2) % 16 == 0 && (s.h * 2) % 16 == 0 &&
+         (s.b * 2) % 16 == 0;
+}
+
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          const float* lse, float* lsep, cudaStream_t s) {
   int rows = d.BH() * d.T;
+  if (dtype == FPA_DTYPE_F16 && d.D >= 16 && d.D <= 256 && vec16_ok(o, so) && vec16_ok(dout, sdo)) {
+    const int G = d.D / 8;
+    const int blocks = int((int64_t(rows) * G + 255) / 256);
+    auto a = static_cast<const __half*>(o);
+    auto c = static_cast<const __half*>(dout);
+    switch (G) {
+      case 2: delta_f16_vec_kernel<2><<<blocks, 256, 0, s>>>(a, so, c, sdo, d.H, d.T, d.TP, rows, delta, lse, lsep); break;
+      case 4: delta_f16_vec_kernel<4><<<blocks, 256, 0, s>>>(a, so, c, sdo, d.H, d.T, d.TP, rows, delta, lse, lsep); break;
+      case 8: delta_f16_vec_kernel<8><<<blocks, 256, 0, s>>>(a, so, c, sdo, d.H, d.T, d.TP, rows, delta, lse, lsep); break;
+      case 16: delta_f16_vec_kernel<16><<<blocks, 256, 0, s>>>(a, so, c, sdo, d.H, d.T, d.TP, rows, delta, lse, lsep); break;
+      default: delta_f16_vec_kernel<32><<<blocks, 256, 0, s>>>(a, so, c, sdo, d.H, d.T, d.TP, rows, delta, lse, lsep); break;
+    }
+    return cudaGetLastError();
+  }
   int blocks = (rows * 32 + 255) / 256;
   if (dtype == FPA_DTYPE_F16)
     delta_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)o, so, (const __half*)dout, sdo, d.H, d.T, d.D,
@@ -274,35 +325,56 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
 }
 
 // In-tile soft-min gradient of the diagonal tiles from their stored g (the tensor-core backward writes
-// g_ts = dS_ts [x_ts <= 0] of each diagonal tile to `gd` [BH][NB][BT][BT], indexed [key s][query t]). For key s:
+// g_ts = dS_ts [x_ts <= 0] of each diagonal tile to `gd` [BH][NB][128][128], indexed [key s][query t]). For key s:
 //   H(t) = g_ts + (Z_{s,t} / Z_{s,t+1}) H(t+1),  contribution to u = t: (2^{a2_t} / Z_{s,t}) H(t),
-// Z_{s,t} = sum_{s<u<=t} 2^{a2_u} carried as its log2 (kernel.py:269-283 evaluates the same sums with scans).
-// Block: one thread per key; the contributions are summed per u in a fixed order.
-__global__ void diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, int T, int BT, int NB,
-                                 float il2, float* __restrict__ dphi4) {
-  extern __shared__ float sm[];
-  const int LD = BT + 1;
-  float* G = sm;             // [BT][BT+1]
-  float* L = G + BT * LD;    // [BT][BT+1]
-  float* a2 = L + BT * LD;   // [BT]
-  const int j = blockIdx.x, z = blockIdx.y, tid = threadIdx.x;
+// Z_{s,t} = sum_{s<u<=t} 2^{a2_u} (kernel.py:269-283 evaluates the same sums with scans). Every factor lies in
+// [0, 1]. Thread = key: log2 Z_{s,t} for all t is kept in registers (the forward running sum carries its maximum
+// separately, so its chain is one exp2 and one FMA per step); the contributions are summed per u in a fixed order.
+constexpr int kDiagBT = 128;
+
+__global__ void __launch_bounds__(kDiagBT)
+diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, int T, int NB, float il2,
+                 float* __restrict__ dphi4) {
+  constexpr int BT = kDiagBT, LD = BT + 1;
+  extern __shared__ float dsm[];
+  float* G = dsm;          // [BT][BT+1]
+  float* a2 = G + BT * LD;  // [BT]
+  const int j = blockIdx.x, z = blockIdx.y, sl = threadIdx.x;
   const size_t TP = size_t(NB) * BT;
-  const float* g = gd + (size_t(z) * NB + j) * BT * BT;
-  for (int e = tid; e < BT * BT; e += blockDim.x) G[(e / BT) * LD + (e % BT)] = g[e];
+  const float4* g4 = reinterpret_cast<const float4*>(gd + (size_t(z) * NB + j) * BT * BT);
+  for (int e = sl; e < BT * BT / 4; e += BT) {
+    const float4 v = g4[e];
+    const int row = (4 * e) / BT, col = (4 * e) % BT;
+    G[row * LD + col] = v.x;
+    G[row * LD + col + 1] = v.y;
+    G[row * LD + col + 2] = v.z;
+    G[row * LD + col + 3] = v.w;
+  }
   const int p0 = j * BT;
-  a2[tid] = p0 + tid < T ? -phi[size_t(z) * T + p0 + tid] * il2 : -kInf;
+  a2[sl] = p0 + sl < T ? -phi[size_t(z) * T + p0 + sl] * il2 : -kInf;
   __syncthreads();
-  const int tend = min(BT, T - p0), sl = tid;
-  float Lr = -kInf;
-  for (int t = sl + 1; t < tend; ++t) {
-    Lr = lse2(Lr, a2[t]);
-    L[sl * LD + t] = Lr;
+  const int tend = min(BT, T - p0);
+  float L[BT];
+  float mz = -kInf, zz = 0.f;
+#pragma unroll
+  for (int t = 0; t < BT; ++t) {
+    const float at = a2[t];
+    const float d = at - mz;
+    const bool up = d > 0.f;
+    const float e = ex2(-fabsf(d));
+    const float znew = up ? fmaf(zz, e, 1.f) : zz + e;
+    const bool on = t > sl && t < tend;
+    zz = on ? znew : zz;
+    mz = on ? (up ? at : mz) : mz;
+    L[t] = mz + lg2(zz);
   }
   float Hh = 0.f;
-  for (int t = tend - 1; t > sl; --t) {
-    if (t < tend - 1) Hh *= ex2(L[sl * LD + t] - L[sl * LD + t + 1]);
-    Hh += G[sl * LD + t];
-    G[sl * LD + t] = ex2(a2[t] - L[sl * LD + t]) * Hh;
+#pragma unroll
+  for (int t = BT - 1; t >= 0; --t) {
+    const bool on = t > sl && t < tend;
+    const float rho = (t + 1 < BT && t + 1 < tend) ? ex2(L[t] - L[t + 1 < BT ? t + 1 : t]) : 0.f;
+    Hh = on ? fmaf(Hh, rho, G[sl * LD + t]) : 0.f;
+    if (on) G[sl * LD + t] = ex2(a2[t] - L[t]) * Hh;
   }
   __syncthreads();
   if (sl < tend) {
@@ -313,10 +385,11 @@ __global__ void diag_dphi_kernel(const float* __restrict__ phi, const float* __r
 }
 
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s) {
-  const size_t smem = (2 * size_t(d.BT) * (d.BT + 1) + d.BT) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(diag_dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (d.BT != kDiagBT) return cudaErrorInvalidValue;
+  const int smem = (kDiagBT * (kDiagBT + 1) + kDiagBT) * int(sizeof(float));
+  cudaError_t e = cudaFuncSetAttribute(diag_dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  diag_dphi_kernel<<<dim3(d.NB, d.BH()), d.BT, smem, s>>>(phi, gd, d.T, d.BT, d.NB, kLog2e / tau, dphi4);
+  diag_dphi_kernel<<<dim3(d.NB, d.BH()), kDiagBT, smem, s>>>(phi, gd, d.T, d.NB, kLog2e / tau, dphi4);
   return cudaGetLastError();
 }
 
