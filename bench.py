@@ -297,6 +297,18 @@ def main():
     sync_all()
     e2e_total = max_over_ranks(timed(e2e, args.steps, args.warmup, flush))
     sync_all()
+    # Per-kernel device times of the library's launches (CUDA events around each launch, on the call's stream),
+    # in a separate pass so the event records stay out of the timed regions above.
+    from first_passage_attention_b200 import _lib
+    lib = _lib.load()
+    _lib.profile_report()
+    lib.fpa_profile(1)
+    for _ in range(args.steps):
+        flush.zero_()
+        fwd_bwd()
+    torch.cuda.synchronize()
+    lib.fpa_profile(0)
+    kernels = _lib.profile_report()
 
     K = args.steps
     fwd_ms, step_ms, e2e_ms = fwd_total / K, step_total / K, e2e_total / K
@@ -306,6 +318,25 @@ def main():
     job_fwd = f_fwd * world / (fwd_ms * 1e-3) / 1e12
     per_gpu_fwd = f_fwd / (fwd_ms * 1e-3) / 1e12
     per_gpu_step = f_step / (step_ms * 1e-3) / 1e12
+
+    # Algorithmic FLOPs per launch (causal FlashAttention convention, unit G = B*H*T^2*D): the forward kernel does
+    # the forward's 2G; the kv-pass does 4 of the backward's 5 G-sized products (S^T, dP^T, dV, dK); the q-pass does
+    # dQ (its S and dP are the recomputation the convention does not count).
+    G = float(Br) * Hr * T * T * D
+    algo = {"fwd_tc": 2 * G, "fwd_simt": 2 * G, "bwd_kv_tc": 4 * G, "bwd_kv_simt": 4 * G, "bwd_q_tc": G,
+            "bwd_q_simt": G}
+    per_launch_us = {k: 1e3 * ms / n for k, (n, ms) in kernels.items()}
+    dom = max(kernels, key=lambda k: kernels[k][1]) if kernels else None
+    step_kernel_ms = sum(ms for (n, ms) in kernels.values()) / max(1, args.steps)
+    if dom in algo:
+        ach = algo[dom] / (per_launch_us[dom] * 1e-6) / 1e12
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                "frac": ach / peak, "peak_source": peak_src, "traffic": None,
+                "share_of_step": kernels[dom][1] / max(1e-9, sum(ms for (n, ms) in kernels.values()))}
+    else:
+        roof = {"bound": "tensor", "kernel": "forward pass (field statistics + attention forward)",
+                "achieved": per_gpu_fwd, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu_fwd / peak,
+                "peak_source": peak_src, "traffic": None}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -326,9 +357,8 @@ def main():
                        "l2": "flushed before every timed step (256 MiB write, outside the events)"},
             "fwd_ms": fwd_ms, "fwd_tflops": job_fwd, "fwd_pct_peak": 100 * per_gpu_fwd / peak,
             "fwd_bwd_ms": step_ms, "fwd_bwd_tflops": job_step, "fwd_bwd_pct_peak": 100 * per_gpu_step / peak,
-            "roofline": {"bound": "tensor", "kernel": "forward pass (field statistics + attention forward)",
-                         "achieved": per_gpu_fwd, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu_fwd / peak,
-                         "peak_source": peak_src, "traffic": None},
+            "roofline": roof,
+            "kernels_us_per_launch": {k: round(v, 2) for k, v in sorted(per_launch_us.items())},
             "e2e": {"value": f_step * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,

@@ -17,7 +17,8 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE = range(6
 
 # Exported symbols, in the order include/fpa.h declares them.
 EXPORTS = ("fpa_abi_version", "fpa_struct_size", "fpa_fwd_workspace_bytes", "fpa_bwd_workspace_bytes", "fpa_fwd",
-           "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_fwd_noalloc")
+           "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_profile",
+           "fpa_profile_report", "fpa_fwd_noalloc")
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _c_i64x4 = ctypes.c_int64 * 4
@@ -88,6 +89,10 @@ def load():
         lib.fpa_status_string.restype = ctypes.c_char_p
         lib.fpa_status_string.argtypes = [ctypes.c_int]
         lib.fpa_last_error.restype = ctypes.c_char_p
+        lib.fpa_profile.restype = ctypes.c_int
+        lib.fpa_profile.argtypes = [ctypes.c_int]
+        lib.fpa_profile_report.restype = ctypes.c_int
+        lib.fpa_profile_report.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
         lib.fpa_fwd_noalloc.restype = ctypes.c_int
         lib.fpa_fwd_noalloc.argtypes = [ctypes.POINTER(FpaFwdArgs), ctypes.c_void_p]
         if lib.fpa_abi_version() != ABI_VERSION:
@@ -96,6 +101,20 @@ def load():
             raise RuntimeError("libfpa_b200 argument structs do not match the Python mirror; rebuild it")
         _lib = lib
         return lib
+
+
+def profile_report():
+    """{kernel: (launches, total ms)} of the launches recorded since profiling was enabled (clears them)."""
+    lib = load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    n = lib.fpa_profile_report(buf, len(buf))
+    if n < 0:
+        raise RuntimeError("fpa_profile_report failed")
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, cnt, ms = line.split()
+        out[name] = (int(cnt), float(ms))
+    return out
 
 
 def check(rc):

@@ -62,7 +62,7 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
-                             const float* __restrict__ beta, int H, int* status) {
+                             const float* __restrict__ beta, int H, Fact fact, int* status) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.y;
@@ -123,6 +123,19 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   const float sufl = tid + 1 < BT ? slse[tid + 1] : -kInf;
   st.suf[base + tid] = suf;
   st.sufl[base + tid] = sufl;
+  if (fact.prey) {
+    // slse holds the inclusive suffix LSE: slse[0] = BL_j; the prefix LSE of the first position is a2 there;
+    // the smallest finite exclusive suffix is at the second-to-last valid position (= a2 of the last one).
+    const int lv = min(BT, T - j * BT) - 1;
+    const float blj = slse[0];
+    const float sufl0 = BT > 1 ? slse[1] : -kInf;
+    fact.prey[base + tid] = t < T ? ex2(pl - blj) : 1.f;
+    fact.sufy[base + tid] = ex2(sufl - sufl0);
+    if (tid == 0) {
+      fact.prer[size_t(z) * NB + j] = blj - pl;  // pl = PREL_first in thread 0
+      fact.sufr[size_t(z) * NB + j] = lv >= 1 ? sufl0 - slse[lv] : 0.f;
+    }
+  }
   if (cols.a) {
     const bool ok = t < T;
     const float y = ok ? psi[size_t(z) * T + t] : 0.f;
@@ -140,9 +153,11 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 }
 
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
-                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s) {
+                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
+                         const Fact* fact) {
+  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr};
   stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
-                                                   cols_scaled, beta, d.H, status);
+                                                   cols_scaled, beta, d.H, f, status);
   return cudaGetLastError();
 }
 

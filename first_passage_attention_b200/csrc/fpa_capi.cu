@@ -105,19 +105,23 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
   fpa::Stats st = fpa::carve_stats(ws + fpa::kStatusBytes, d);
   fpa::KeyCols cols{nullptr, nullptr, nullptr};
   if (path == FPA_PATH_TENSOR) cols = fpa::carve_keycols(ws + fpa::kStatusBytes + fpa::stats_bytes(d), d);
+  fpa::prof_mark(s, "stats");
   cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, cols, 1, status, s);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   a->kernels_launched = 1;
   if (path == FPA_PATH_TENSOR) {
     int n = 0;
+    fpa::prof_mark(s, "fwd_tc");
     rc = fpa::tc_fwd(*a, d, st, cols, status, s, &n, &g_last_error);
     a->kernels_launched += n;
     if (rc) return rc;
   } else {
+    fpa::prof_mark(s, "fwd_simt");
     e = fpa::simt_fwd(*a, d, st, s);
     if (e != cudaSuccess) return cuda_fail(e, "forward kernel");
     a->kernels_launched += 1;
   }
+  fpa::prof_mark(s, nullptr);
   a->path_taken = path;
   return FPA_OK;
 }
@@ -152,27 +156,34 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
       return rc;
     }
   } else {
+    fpa::prof_mark(s, "stats");
     e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, fpa::KeyCols{nullptr, nullptr, nullptr}, 0, status,
                           s);
     if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
     ++n;
+    fpa::prof_mark(s, "delta");
     e = fpa::launch_delta(a->dtype, a->o, fpa::str4(a->o_stride), a->dout, fpa::str4(a->dout_stride), d, sc.delta,
                           nullptr, nullptr, s);
     if (e != cudaSuccess) return cuda_fail(e, "delta kernel");
     ++n;
+    fpa::prof_mark(s, "bwd_kv_simt");
     e = fpa::simt_bwd_kv(*a, d, st, sc, s);
     if (e != cudaSuccess) return cuda_fail(e, "kv-pass kernel");
     ++n;
+    fpa::prof_mark(s, "bwd_q_simt");
     e = fpa::simt_bwd_q(*a, d, st, sc, s);
     if (e != cudaSuccess) return cuda_fail(e, "q-pass kernel");
     ++n;
   }
+  fpa::prof_mark(s, "dphi");
   e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, s);
   if (e != cudaSuccess) return cuda_fail(e, "dphi kernel");
   ++n;
+  fpa::prof_mark(s, "dbeta");
   e = fpa::launch_dbeta(d, sc, a->dbeta, s);
   if (e != cudaSuccess) return cuda_fail(e, "dbeta kernel");
   ++n;
+  fpa::prof_mark(s, nullptr);
   a->kernels_launched = n;
   a->path_taken = path;
   return FPA_OK;

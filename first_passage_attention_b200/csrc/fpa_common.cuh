@@ -77,6 +77,17 @@ struct KeyCols {
   float* phi;
 };
 
+// Factors that let the tensor-core backward form the soft-min denominators without a per-element exp2
+// (float32; written by stats_kernel when `prey` is set):
+//   prey_t = 2^{PREL_t - BL_j} for t in tile j, prer_j = BL_j - PREL_{first of j}
+//   sufy_s = 2^{SUFL_s - SUFL_{first of j}} for s in tile j, sufr_j = SUFL_{first} - min_{SUFL_s > -inf} SUFL_s
+struct Fact {
+  float* prey;  // [BH][TP]
+  float* sufy;  // [BH][TP]
+  float* prer;  // [BH][NB]
+  float* sufr;  // [BH][NB]
+};
+
 // Scratch of the backward pass (all float32, per head z = b*H + h).
 struct BwdScratch {
   float* delta;  // [BH][TP]   rowsum(dO * O)

@@ -28,6 +28,10 @@ inline Dims make_dims(int B, int H, int T, int D, int BT) {
   return d;
 }
 
+// Profiling mark (fpa_profile.cu): when profiling is on, records an event on `s` that starts the timing of the
+// kernel `name` launched next; name = nullptr ends the last kernel of a call. A no-op otherwise.
+void prof_mark(cudaStream_t s, const char* name);
+
 // Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
 void set_last_error(const std::string& msg);
 
@@ -42,7 +46,8 @@ size_t keycols_bytes(const Dims& d);
 KeyCols carve_keycols(char* base, const Dims& d);
 // cols_scaled = 1: the forward's b'-scaled key vectors; 0: raw (a = SUF - psi, psi, phi) for the backward.
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
-                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s);
+                         const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
+                         const Fact* fact = nullptr);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          const float* lse, float* lsep, cudaStream_t s);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);

@@ -10,10 +10,14 @@
 //                     computes dS (fp16, into its own TMEM columns) and dQ += dS K; also r_t and from it the
 //                     soft-min part with u in the query's tile (DPHI2).
 //
-// Warp roles (192 threads): warps 0-3 the row group (thread = TMEM lane), warp 4 the TMA producer (stationary
-// tiles once, streamed tiles and their per-row vectors through a 2-stage ring), warp 5 the MMA issuer (whole warp,
-// one elected lane issues). Every mbarrier wait is bounded (fpa::sm100::mbar_wait).
+// Warp roles (384 threads): warps 0-3 and 4-7 are two row groups (thread = TMEM lane) that split the 128 columns
+// of each S / dP tile between them (64 each); warp 8 is the TMA producer (stationary tiles once, streamed tiles and
+// their per-row vectors through a 2-stage ring), warp 9 the MMA issuer (whole warp, one elected lane issues);
+// warps 10-11 only hand their registers to the row groups (setmaxnreg). Every mbarrier wait is bounded
+// (fpa::sm100::mbar_wait).
 #include <cuda.h>
+
+#include <type_traits>
 
 #include "fpa_sm100.cuh"
 #include "fpa_tc.h"
@@ -24,10 +28,11 @@ using namespace sm100;
 namespace {
 
 constexpr int kBT = kTcBT;
-constexpr int kThreads = 192;
-constexpr int kWarpProducer = 4;
-constexpr int kWarpMma = 5;
-constexpr int kNamedBarRows = 1;  // bar.sync id used by the 128 row threads
+constexpr int kThreads = 384;
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
+constexpr int kRowThreads = 256;  // two row groups of 128
+constexpr int kNamedBarRows = 1;  // bar.sync id used by the 256 row threads
 
 template <int D>
 struct TcBwdCfg {
@@ -38,15 +43,15 @@ struct TcBwdCfg {
   static constexpr int TILEB = NBOX * BOXB;
   static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
   static constexpr int NS = 2;
-  static constexpr int NVEC = 5;
+  static constexpr int NVEC = 6;
   static constexpr int VECB = kBT * 4;
   static constexpr int OFF_A = 0;                        // stationary operand 1
   static constexpr int OFF_B = TILEB;                    // stationary operand 2
   static constexpr int OFF_S1 = 2 * TILEB;               // streamed operand 1 [NS]
   static constexpr int OFF_S2 = OFF_S1 + NS * TILEB;     // streamed operand 2 [NS]
   static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][NVEC][128] floats
-  static constexpr int OFF_RED = OFF_VEC + NS * NVEC * VECB;  // 3 * 128 floats of row-group scratch
-  static constexpr int OFF_BAR = OFF_RED + 3 * kBT * 4;
+  static constexpr int OFF_RED = OFF_VEC + NS * NVEC * VECB;  // 32 + 4 * 128 floats of row-group scratch
+  static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
   static constexpr int NBAR = 1 + 2 * NS + 4;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
@@ -68,6 +73,10 @@ struct TcBwdParams {
   const float* psi;    // psi
   const float* phi;    // phi (+inf beyond T)
   const float* beta;   // [H]
+  const float* prey;   // 2^{PREL_t - BL_tile}
+  const float* sufy;   // 2^{SUFL_s - SUFL_first of tile}
+  const float* prer;   // [BH][NB] BL - PREL_first
+  const float* sufr;   // [BH][NB] SUFL_first - min finite SUFL
   // outputs
   __half* dq;
   __half* dk;
@@ -95,19 +104,22 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ void rows_sync() { asm volatile("bar.sync %0, 128;" ::"r"(kNamedBarRows) : "memory"); }
+__device__ __forceinline__ void rows_sync() { asm volatile("bar.sync %0, 256;" ::"r"(kNamedBarRows) : "memory"); }
 
-// Deterministic sum over the 128 row threads (fixed shuffle tree, then the 4 warp partials in order). All 128
-// threads call it; the result is returned to every thread.
+// Deterministic sum over the 256 row threads (fixed shuffle tree, then the 8 warp partials in a fixed order). All
+// 256 threads call it; the result is returned to every thread.
 __device__ __forceinline__ float rows_sum(float v, float* red) {
   v = group_sum<32>(v);
   const int w = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) red[w] = v;
   rows_sync();
-  const float r = (red[0] + red[1]) + (red[2] + red[3]);
+  const float r = ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
   rows_sync();
   return r;
 }
+
+__device__ __forceinline__ void regs_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory"); }
+__device__ __forceinline__ void regs_rows() { asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory"); }
 
 template <int D>
 __device__ __forceinline__ void issue_ss(uint32_t d, uint32_t a, uint32_t b) {
@@ -120,13 +132,15 @@ __device__ __forceinline__ void issue_ss(uint32_t d, uint32_t a, uint32_t b) {
   }
 }
 
-// D[128 x D] (+)= A[128 x 128 from TMEM, fp16 packed] * B[128 x D from smem, N-contiguous].
+// D[128 x D] (+)= A[128 x 128 from TMEM, fp16 packed] * B[128 x D from smem, N-contiguous]. The K-step kk of A
+// (16 values, 8 packed columns) sits at column a_tmem + 16 kk: the row groups write it over the first half of the
+// 16 fp32 columns they read it from, so no column is overwritten before it is read.
 template <int D>
 __device__ __forceinline__ void issue_ts(uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
   using C = TcBwdCfg<D>;
 #pragma unroll
   for (int kk = 0; kk < kBT / 16; ++kk)
-    mma_ts_w(d, a_tmem + kk * 8, smem_desc(b + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_ACC,
+    mma_ts_w(d, a_tmem + kk * 16, smem_desc(b + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_ACC,
              (acc || kk > 0) ? 1u : 0u);
 }
 
@@ -163,7 +177,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       mbar_init(st_empty + s, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kRowThreads);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -174,6 +188,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const size_t zb = size_t(z) * p.TP;
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 56 and the
+  // two row groups take 224 each (128*56 + 256*224 = 384*168).
+  if (warp >= 8) regs_producer();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -195,7 +212,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       if (!ok) break;
       if (elect_one()) {
         uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
-        mbar_expect_tx(st_full + st, 2 * C::TILEB + C::NVEC * C::VECB);
+        mbar_expect_tx(st_full + st, 2 * C::TILEB + 6 * C::VECB);
         for (int bx = 0; bx < C::NBOX; ++bx) {
           tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, st_full + st);
           tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b,
@@ -207,6 +224,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         bulk_load(vec + 2 * C::VECB, p.pre + off, C::VECB, st_full + st);
         bulk_load(vec + 3 * C::VECB, p.prel + off, C::VECB, st_full + st);
         bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
+        bulk_load(vec + 5 * C::VECB, p.prey + off, C::VECB, st_full + st);
       }
       __syncwarp();
     }
@@ -245,11 +263,14 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 114);
-  } else if (warp < 4) {
-    const int r = threadIdx.x;  // key within the tile = TMEM lane
+  } else if (warp < 8) {
+    regs_rows();
+    const int grp = warp >> 2, wr = warp & 3;
+    const int r = wr * 32 + (threadIdx.x & 31);  // key within the tile = TMEM lane
+    const int cb = grp * 64;                     // this group's query columns [cb, cb + 64)
     const int s = j * kBT + r;
     const bool s_ok = s < p.T;
-    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
     const float bh = p.beta[h], betal = bh * kLog2e;
     const float psi_s = p.psi[zb + s];
     const float xs_s = p.xs[zb + s];    // SUF_s - psi_s (+inf for the last key of the tile)
@@ -273,25 +294,38 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       const float* vpre = vec + 2 * kBT;
       const float* vprel = vec + 3 * kBT;
       const float* vphi = vec + 4 * kBT;
+      const float* vprey = vec + 5 * kBT;
       const bool diag = k == 0;
       const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
       float rs = fmaxf(c2_s, cmid2);
       const bool vrs = !diag && rs > -kInf;
       rs = vrs ? rs : 0.f;
       const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
+      // 2^{PREL_t - rs} = prey_t * 2^{BL_i - rs} when both factors stay in range (no exp2 per element).
+      const float bli = bl[i];
+      // Warp-uniform: the chunk body holds warp-collective TMEM loads and stores, so the whole warp takes the
+      // factorised path or none of it does.
+      const bool fact = __all_sync(0xffffffffu, vrs && p.prer[size_t(z) * p.NB + i] <= 120.f && bli - rs <= 120.f);
+      const float xfac = fact ? ex2(bli - rs) : 0.f;
       const int tvalid = p.T - i * kBT;  // queries c < tvalid exist
-      float rr = kInf, fsum = 0.f;
+      // Diagonal tile: rr = min phi over (key, query]; the second group starts from the minimum over (key, 63].
+      float rr = kInf;
+      if (diag && grp == 1)
+        for (int c = 0; c < 64; ++c)
+          if (c > r) rr = fminf(rr, vphi[c]);
+      float fsum = 0.f;
       float* grow = p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBT; c0 += 32) {
-        float sS[32], sP[32];
-        tmem_ld32(tl + C::COL_S + c0, sS);
-        tmem_ld32(tl + C::COL_P + c0, sP);
+      // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
+      // those 16 columns.
+      auto chunk = [&](int c0, auto fact_tag) {
+        constexpr bool FACT = decltype(fact_tag)::value;
+        float sS[16], sP[16];
+        tmem_ld16(tl + C::COL_S + c0, sS);
+        tmem_ld16(tl + C::COL_P + c0, sP);
         tmem_ld_wait();
-        uint32_t ppk[16], dpk[16];
-        float gbuf[32];
+        float gb[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < 16; ++e) {
           const int c = c0 + e;
           const bool valid = s_ok && c < tvalid && (!diag || c >= r);
           float x;
@@ -308,23 +342,34 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
           const float g = (valid && x <= 0.f) ? ds : 0.f;
           gsum += g;
           dbsum += ds * xm;
-          if (vrs) fsum += g * rcp_approx(sv_ + ex2(vprel[c] - rs));
-          gbuf[e] = g;
+          if (FACT)
+            fsum += g * rcp_approx(fmaf(vprey[c], xfac, sv_));
+          else if (vrs)
+            fsum += g * rcp_approx(sv_ + ex2(vprel[c] - rs));
+          gb[e] = g;
           sS[e] = pp;
           sP[e] = ds;
         }
+        uint32_t ppk[8], dpk[8];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
+        for (int e = 0; e < 16; e += 2) {
           ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
           dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
         }
-        tmem_st16(tl + C::COL_S + c0 / 2, ppk);
-        tmem_st16(tl + C::COL_P + c0 / 2, dpk);
+        tmem_st8(tl + C::COL_S + c0, ppk);
+        tmem_st8(tl + C::COL_P + c0, dpk);
         if (diag) {
           float4* dst = reinterpret_cast<float4*>(grow + c0);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dst[e] = make_float4(gbuf[4 * e], gbuf[4 * e + 1], gbuf[4 * e + 2], gbuf[4 * e + 3]);
+          for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
         }
+      };
+#pragma unroll 1
+      for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+        if (fact)
+          chunk(c0, std::true_type{});
+        else
+          chunk(c0, std::false_type{});
       }
       tmem_st_wait();
       tc_fence_before();
@@ -333,43 +378,54 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         if (vrs) wsum += ex2(c2_s - rs) * fsum;
         if (i > j + 1) {
           const float tot = rows_sum(vrs ? ex2(cmid2 - rs) * fsum : 0.f, red);
-          if (r == 0) p.tb[(size_t(z) * p.NB + i) * p.NB + j] = tot;
+          if (threadIdx.x == 0) p.tb[(size_t(z) * p.NB + i) * p.NB + j] = tot;
         }
         mid = fminf(mid, bmin[i]);
         midl = lse2(midl, bl[i]);
       }
     }
+    // Join the two groups' per-key sums (fixed order: group 0 + group 1).
+    float* xg = red + 32;
+    float* xw = red + 32 + kBT;
+    if (grp == 1) {
+      xg[r] = gsum;
+      xw[r] = wsum;
+    }
+    rows_sync();
     if (ok) ok = mbar_wait(acc_done, 0, p.status, 122);
     if (ok) {
       tc_fence_after();
       __half* dvrow = p.dv + b * p.dv_s[0] + h * p.dv_s[1] + int64_t(s_ok ? s : 0) * p.dv_s[2];
       __half* dkrow = p.dk + b * p.dk_s[0] + h * p.dk_s[1] + int64_t(s_ok ? s : 0) * p.dk_s[2];
+      constexpr int DH = D >= 32 ? D / 2 : D;  // head-dim columns stored by each group
+      if (D >= 32 || grp == 0) {
 #pragma unroll
-      for (int c = 0; c < D; c += 16) {
-        float a1[16], a2[16];
-        tmem_ld16(tl + C::COL_A1 + c, a1);
-        tmem_ld16(tl + C::COL_A2 + c, a2);
-        tmem_ld_wait();
-        if (s_ok) {
-          uint32_t u1[8], u2[8];
+        for (int c = grp * DH; c < grp * DH + DH; c += 16) {
+          float a1[16], a2[16];
+          tmem_ld16(tl + C::COL_A1 + c, a1);
+          tmem_ld16(tl + C::COL_A2 + c, a2);
+          tmem_ld_wait();
+          if (s_ok) {
+            uint32_t u1[8], u2[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            u1[e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
-            u2[e] = pack_half2(a2[2 * e] * p.scale, a2[2 * e + 1] * p.scale);
+            for (int e = 0; e < 8; ++e) {
+              u1[e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
+              u2[e] = pack_half2(a2[2 * e] * p.scale, a2[2 * e + 1] * p.scale);
+            }
+            reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(u1[0], u1[1], u1[2], u1[3]);
+            reinterpret_cast<uint4*>(dvrow + c)[1] = make_uint4(u1[4], u1[5], u1[6], u1[7]);
+            reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(u2[0], u2[1], u2[2], u2[3]);
+            reinterpret_cast<uint4*>(dkrow + c)[1] = make_uint4(u2[4], u2[5], u2[6], u2[7]);
           }
-          reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(u1[0], u1[1], u1[2], u1[3]);
-          reinterpret_cast<uint4*>(dvrow + c)[1] = make_uint4(u1[4], u1[5], u1[6], u1[7]);
-          reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(u2[0], u2[1], u2[2], u2[3]);
-          reinterpret_cast<uint4*>(dkrow + c)[1] = make_uint4(u2[4], u2[5], u2[6], u2[7]);
         }
       }
-      if (s_ok) {
-        p.dpsi[size_t(z) * p.T + s] = -bh * gsum;
-        p.w[zb + s] = wsum;
+      if (s_ok && grp == 0) {
+        p.dpsi[size_t(z) * p.T + s] = -bh * (gsum + xg[r]);
+        p.w[zb + s] = wsum + xw[r];
       }
     }
     const float db = rows_sum(dbsum, red);
-    if (r == 0) p.dbeta[size_t(z) * p.NB + j] = db;
+    if (threadIdx.x == 0) p.dbeta[size_t(z) * p.NB + j] = db;
   }
   tc_fence_before();
   __syncthreads();
@@ -386,7 +442,6 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                 const TcBwdParams p) {
   using C = TcBwdCfg<D>;
-  constexpr int COL_DS = C::COL_A1 + D;  // dS (fp16, 64 columns) in its own columns
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -413,7 +468,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       mbar_init(st_empty + s, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kRowThreads);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -424,6 +479,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const size_t zb = size_t(z) * p.TP;
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 56 and the
+  // two row groups take 224 each (128*56 + 256*224 = 384*168).
+  if (warp >= 8) regs_producer();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -445,7 +503,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       if (!ok) break;
       if (elect_one()) {
         uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
-        mbar_expect_tx(st_full + st, 2 * C::TILEB + 4 * C::VECB);
+        mbar_expect_tx(st_full + st, 2 * C::TILEB + 5 * C::VECB);
         for (int bx = 0; bx < C::NBOX; ++bx) {
           tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, st_full + st);
           tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, st_full + st);
@@ -455,6 +513,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         bulk_load(vec + 1 * C::VECB, p.psi + off, C::VECB, st_full + st);
         bulk_load(vec + 2 * C::VECB, p.sufl + off, C::VECB, st_full + st);
         bulk_load(vec + 3 * C::VECB, p.phi + off, C::VECB, st_full + st);
+        bulk_load(vec + 4 * C::VECB, p.sufy + off, C::VECB, st_full + st);
       }
       __syncwarp();
     }
@@ -477,7 +536,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       ok = mbar_wait(p_full, k & 1, p.status, 212);
       if (!ok) break;
       tc_fence_after();
-      issue_ts<D>(tmem + C::COL_A1, tmem + COL_DS, s1 + st * C::TILEB, k > 0);  // dQ += dS K
+      issue_ts<D>(tmem + C::COL_A1, tmem + C::COL_P, s1 + st * C::TILEB, k > 0);  // dQ += dS K
       mma_commit_w(st_empty + st);
       if (k + 1 < nsteps) {
         const int st1 = (k + 1) % C::NS;
@@ -492,11 +551,14 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 214);
-  } else if (warp < 4) {
-    const int r = threadIdx.x;  // query within the tile = TMEM lane
+  } else if (warp < 8) {
+    regs_rows();
+    const int grp = warp >> 2, wr = warp & 3;
+    const int r = wr * 32 + (threadIdx.x & 31);  // query within the tile = TMEM lane
+    const int cb = grp * 64;                     // this group's key columns [cb, cb + 64)
     const int t = i * kBT + r;
     const bool t_ok = t < p.T;
-    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
     const float betal = p.beta[h] * kLog2e;
     const float lse_t = p.lsep[zb + t];
     const float del_t = t_ok ? p.delta[zb + t] : 0.f;
@@ -519,20 +581,33 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       const float* vpsi = vec + kBT;
       const float* vsufl = vec + 2 * kBT;
       const float* vphi = vec + 3 * kBT;
+      const float* vsufy = vec + 4 * kBT;
       const bool diag = k == 0;
       const float cap = fminf(mid, pre_t);
       const float mterm = ex2(midl - c2_t) + bpre;
+      // 2^{SUFL_s - c2_t} = sufy_s * 2^{SUFL_first - c2_t} when both factors stay in range.
+      const float sufl0 = p.sufl[zb + size_t(j) * kBT];
+      // Warp-uniform (the chunk body holds warp-collective TMEM loads and stores). Rows beyond T take either path.
+      const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (p.sufr[size_t(z) * p.NB + j] <= 120.f &&
+                                                                      sufl0 - c2_t <= 120.f)));
+      const float yfac = (fact && t_ok) ? ex2(sufl0 - c2_t) : 0.f;
       const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
+      // Diagonal tile, keys descending: rr = min phi over (key, query]; the first group starts from the minimum
+      // over the second group's keys up to the query, [64, query].
       float rr = kInf;
-      // Keys in descending order so the diagonal tile can carry rr = min_{key<u<=t} phi_u.
-#pragma unroll 1
-      for (int c0 = kBT - 32; c0 >= 0; c0 -= 32) {
-        float sS[32], sP[32];
-        tmem_ld32(tl + C::COL_S + c0, sS);
-        tmem_ld32(tl + C::COL_P + c0, sP);
+      if (diag && grp == 0)
+        for (int c = 64; c < kBT; ++c)
+          if (c <= r) rr = fminf(rr, vphi[c]);
+      // 16 key columns per chunk, in descending order: load S and dP, compute dS (fp16) and write it over the
+      // first 8 of those 16 dP columns.
+      auto chunk = [&](int c0, auto fact_tag) {
+        constexpr bool FACT = decltype(fact_tag)::value;
+        float sS[16], sP[16];
+        tmem_ld16(tl + C::COL_S + c0, sS);
+        tmem_ld16(tl + C::COL_P + c0, sP);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 31; e >= 0; --e) {
+        for (int e = 15; e >= 0; --e) {
           const int c = c0 + e;
           const bool valid = t_ok && c < kvalid && (!diag || c <= r);
           float x;
@@ -548,14 +623,24 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
           const float ds = valid ? pp * (sP[e] - del_t) : 0.f;
           if (!diag) {
             const float g = (valid && x <= 0.f) ? ds : 0.f;
-            racc += g * rcp_approx(ex2(vsufl[c] - c2_t) + mterm);
+            if (FACT)
+              racc += g * rcp_approx(fmaf(vsufy[c], yfac, mterm));
+            else
+              racc += g * rcp_approx(ex2(vsufl[c] - c2_t) + mterm);
           }
           sP[e] = ds;
         }
-        uint32_t dpk[16];
+        uint32_t dpk[8];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
-        tmem_st16(tl + COL_DS + c0 / 2, dpk);
+        for (int e = 0; e < 16; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+        tmem_st8(tl + C::COL_P + c0, dpk);
+      };
+#pragma unroll 1
+      for (int c0 = cb + 48; c0 >= cb; c0 -= 16) {
+        if (fact)
+          chunk(c0, std::true_type{});
+        else
+          chunk(c0, std::false_type{});
       }
       tmem_st_wait();
       tc_fence_before();
@@ -569,27 +654,36 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     if (ok) {
       tc_fence_after();
       __half* dqrow = p.dq + b * p.dq_s[0] + h * p.dq_s[1] + int64_t(t_ok ? t : 0) * p.dq_s[2];
+      constexpr int DH = D >= 32 ? D / 2 : D;
+      if (D >= 32 || grp == 0) {
 #pragma unroll
-      for (int c = 0; c < D; c += 16) {
-        float a1[16];
-        tmem_ld16(tl + C::COL_A1 + c, a1);
-        tmem_ld_wait();
-        if (t_ok) {
-          uint32_t u[8];
+        for (int c = grp * DH; c < grp * DH + DH; c += 16) {
+          float a1[16];
+          tmem_ld16(tl + C::COL_A1 + c, a1);
+          tmem_ld_wait();
+          if (t_ok) {
+            uint32_t u[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) u[e] = pack_half2(a1[2 * e] * p.scale, a1[2 * e + 1] * p.scale);
-          reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(u[0], u[1], u[2], u[3]);
-          reinterpret_cast<uint4*>(dqrow + c)[1] = make_uint4(u[4], u[5], u[6], u[7]);
+            for (int e = 0; e < 8; ++e) u[e] = pack_half2(a1[2 * e] * p.scale, a1[2 * e + 1] * p.scale);
+            reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(u[0], u[1], u[2], u[3]);
+            reinterpret_cast<uint4*>(dqrow + c)[1] = make_uint4(u[4], u[5], u[6], u[7]);
+          }
         }
       }
     }
-    // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile).
-    float* rsh = red + kBT;
-    float* csh = red + 2 * kBT;
-    rsh[r] = racc;
-    csh[r] = c2_t;
+    // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile); r_t joins the two
+    // groups' partial sums in a fixed order.
+    float* rx = red + 32;
+    float* rsh = red + 32 + kBT;
+    float* csh = red + 32 + 2 * kBT;
+    if (grp == 1) rx[r] = racc;
     rows_sync();
-    if (t_ok) {
+    if (grp == 0) {
+      rsh[r] = racc + rx[r];
+      csh[r] = c2_t;
+    }
+    rows_sync();
+    if (grp == 0 && t_ok) {
       const int tend = min(kBT, p.T - i * kBT);
       const float a2 = -p.phi[zb + t] * p.il2;
       float p2 = 0.f;
@@ -607,7 +701,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
-               float* gd, float* lsep, int* status, cudaStream_t s, std::string* err) {
+               const Fact& fact, float* gd, float* lsep, int* status, cudaStream_t s, std::string* err) {
   using C = TcBwdCfg<D>;
   CUtensorMap mq, mk, mv, mdo;
   if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
@@ -629,6 +723,10 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.psi = cols.psi;
   p.phi = cols.phi;
   p.beta = a.beta;
+  p.prey = fact.prey;
+  p.sufy = fact.sufy;
+  p.prer = fact.prer;
+  p.sufr = fact.sufr;
   p.dq = static_cast<__half*>(a.dq);
   p.dk = static_cast<__half*>(a.dk);
   p.dv = static_cast<__half*>(a.dv);
@@ -661,12 +759,15 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     return FPA_ERR_CUDA;
   }
   const int grid = d.NB * d.BH();
+  prof_mark(s, "bwd_kv_tc");
   kv<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
+    prof_mark(s, "diag_dphi");
     e = launch_diag_dphi(a.phi, gd, d, a.tau, sc.dphi4, s);
   }
   if (e == cudaSuccess) {
+    prof_mark(s, "bwd_q_tc");
     qk<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
   }
@@ -682,7 +783,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
 size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
   return keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * sizeof(float)) +
-         align256(bh * d.TP * sizeof(float));
+         3 * align256(bh * d.TP * sizeof(float)) + 2 * align256(bh * d.NB * sizeof(float));
 }
 
 int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
@@ -706,21 +807,34 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   const size_t bh = size_t(d.BH());
   KeyCols cols = carve_keycols(extra, d);
   float* gd = reinterpret_cast<float*>(extra + keycols_bytes(d));
-  float* lsep = reinterpret_cast<float*>(extra + keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * 4));
-  // Raw key vectors and the padded lse copy (filled by the stats and delta kernels of this call).
-  cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s);
-  if (e == cudaSuccess)
+  char* q = extra + keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * 4);
+  float* lsep = reinterpret_cast<float*>(q);
+  q += align256(bh * d.TP * 4);
+  Fact fact;
+  fact.prey = reinterpret_cast<float*>(q);
+  q += align256(bh * d.TP * 4);
+  fact.sufy = reinterpret_cast<float*>(q);
+  q += align256(bh * d.TP * 4);
+  fact.prer = reinterpret_cast<float*>(q);
+  q += align256(bh * d.NB * 4);
+  fact.sufr = reinterpret_cast<float*>(q);
+  // Raw key vectors, the factorisation arrays and the padded lse copy (filled by the stats and delta kernels).
+  prof_mark(s, "stats");
+  cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
+  if (e == cudaSuccess) {
+    prof_mark(s, "delta");
     e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, a.lse, lsep, s);
+  }
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward prologue: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
   int rc;
   switch (d.D) {
-    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
-    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
-    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
-    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, gd, lsep, status, s, err); break;
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
   if (rc == FPA_OK) *launched = 5;  // stats, delta, kv-pass, diagonal dphi, q-pass

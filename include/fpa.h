@@ -127,6 +127,15 @@ FPA_API const char* fpa_status_string(int status);
 /* The message of the last error raised on the calling thread (empty string when none). */
 FPA_API const char* fpa_last_error(void);
 
+/* Kernel timing for profiling. While enabled, every kernel that fpa_fwd / fpa_bwd launch is bracketed by CUDA
+ * events recorded on the call's stream (this adds event records to the stream; leave it off for production).
+ * fpa_profile returns the previous setting. fpa_profile_report synchronises on the recorded events, writes one
+ * line "<kernel> <launches> <total ms>" per kernel into buf (NUL-terminated, truncated to len), clears the records
+ * and returns the number of kernels (or -1 on a CUDA error). No counterpart in the reference (its benchmark times
+ * whole calls, bench.py:11-23). */
+FPA_API int fpa_profile(int enable);
+FPA_API int fpa_profile_report(char* buf, size_t len);
+
 /* Size of the scratch array built into the library for fpa_fwd_noalloc (8 MiB per GPU that loads the library). */
 #define FPA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 
