@@ -135,6 +135,10 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
       fact.prer[size_t(z) * NB + j] = blj - pl;  // pl = PREL_first in thread 0
       fact.sufr[size_t(z) * NB + j] = lv >= 1 ? sufl0 - slse[lv] : 0.f;
     }
+    if (fact.kv4) {
+      const float y = t < T ? psi[size_t(z) * T + t] : 0.f;
+      fact.kv4[base + tid] = make_float4(t < T ? suf - y : kInf, y, ex2(sufl - sufl0), sufl);
+    }
   }
   if (cols.a) {
     const bool ok = t < T;
@@ -155,7 +159,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
                          const Fact* fact) {
-  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr};
+  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
                                                    cols_scaled, beta, d.H, f, status);
   return cudaGetLastError();
@@ -243,6 +247,25 @@ cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, St
   else
     delta_kernel<float><<<blocks, 256, 0, s>>>((const float*)o, so, (const float*)dout, sdo, d.H, d.T, d.D, d.TP,
                                                rows, delta, lse, lsep);
+  return cudaGetLastError();
+}
+
+// Per-query vectors of the tensor-core kv-pass, interleaved for one 16-byte load per query:
+// qv4[z][t] = (lse_t, delta_t, PRE_t, prey_t); beyond T: (+inf, 0, PRE_t, 1), so padded queries get P = 0.
+__global__ void qv_pack_kernel(const float* __restrict__ lse, const float* __restrict__ delta,
+                               const float* __restrict__ pre, const float* __restrict__ prey, int T, int TP, int n,
+                               float4* __restrict__ qv4) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n) return;
+  const int z = idx / TP, t = idx % TP;
+  const bool ok = t < T;
+  qv4[idx] = make_float4(ok ? lse[size_t(z) * T + t] : kInf, ok ? delta[idx] : 0.f, pre[idx], ok ? prey[idx] : 1.f);
+}
+
+cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
+                           float4* qv4, cudaStream_t s) {
+  const int n = d.BH() * d.TP;
+  qv_pack_kernel<<<(n + 255) / 256, 256, 0, s>>>(lse, delta, pre, prey, d.T, d.TP, n, qv4);
   return cudaGetLastError();
 }
 

@@ -86,6 +86,7 @@ struct Fact {
   float* sufy;  // [BH][TP]
   float* prer;  // [BH][NB]
   float* sufr;  // [BH][NB]
+  float4* kv4;  // [BH][TP] per key, interleaved for one 16-byte load: (SUF - psi, psi, sufy, SUFL)
 };
 
 // Scratch of the backward pass (all float32, per head z = b*H + h).

@@ -50,6 +50,8 @@ cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, 
                          const Fact* fact = nullptr);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          const float* lse, float* lsep, cudaStream_t s);
+cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
+                           float4* qv4, cudaStream_t s);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
                         const BwdScratch& sc, float* dphi, cudaStream_t s);

@@ -43,14 +43,14 @@ struct TcBwdCfg {
   static constexpr int TILEB = NBOX * BOXB;
   static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
   static constexpr int NS = 2;
-  static constexpr int NVEC = 6;
   static constexpr int VECB = kBT * 4;
+  static constexpr int VECSTAGE = 4 * VECB + 2 * VECB;   // float4 per row + two float vectors, per stage
   static constexpr int OFF_A = 0;                        // stationary operand 1
   static constexpr int OFF_B = TILEB;                    // stationary operand 2
   static constexpr int OFF_S1 = 2 * TILEB;               // streamed operand 1 [NS]
   static constexpr int OFF_S2 = OFF_S1 + NS * TILEB;     // streamed operand 2 [NS]
-  static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][NVEC][128] floats
-  static constexpr int OFF_RED = OFF_VEC + NS * NVEC * VECB;  // 32 + 4 * 128 floats of row-group scratch
+  static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][VECSTAGE]
+  static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
   static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
   static constexpr int NBAR = 1 + 2 * NS + 4;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
@@ -61,7 +61,8 @@ struct TcBwdCfg {
 
 struct TcBwdParams {
   // per-head [BH][TP] arrays (padded, tiles of 128)
-  const float* lsep;
+  const float4* qv4;   // per query: (lse or +inf beyond T, delta or 0, PRE, prey)
+  const float4* kv4;   // per key: (SUF - psi, psi, sufy, SUFL)
   const float* delta;
   const float* pre;
   const float* prel;
@@ -211,7 +212,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 101);
       if (!ok) break;
       if (elect_one()) {
-        uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
+        uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
         mbar_expect_tx(st_full + st, 2 * C::TILEB + 6 * C::VECB);
         for (int bx = 0; bx < C::NBOX; ++bx) {
           tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, st_full + st);
@@ -219,12 +220,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                       st_full + st);
         }
         const size_t off = zb + size_t(i) * kBT;
-        bulk_load(vec + 0 * C::VECB, p.lsep + off, C::VECB, st_full + st);
-        bulk_load(vec + 1 * C::VECB, p.delta + off, C::VECB, st_full + st);
-        bulk_load(vec + 2 * C::VECB, p.pre + off, C::VECB, st_full + st);
-        bulk_load(vec + 3 * C::VECB, p.prel + off, C::VECB, st_full + st);
-        bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
-        bulk_load(vec + 5 * C::VECB, p.prey + off, C::VECB, st_full + st);
+        bulk_load(vec, p.qv4 + off, 4 * C::VECB, st_full + st);
+        bulk_load(vec + 4 * C::VECB, p.prel + off, C::VECB, st_full + st);
+        bulk_load(vec + 5 * C::VECB, p.phi + off, C::VECB, st_full + st);
       }
       __syncwarp();
     }
@@ -288,13 +286,10 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       if (ok) ok = mbar_wait(s_full, k & 1, p.status, 121);
       if (!ok) break;
       tc_fence_after();
-      const float* vec = reinterpret_cast<const float*>(smem + C::OFF_VEC + st * C::NVEC * C::VECB);
-      const float* vlse = vec;
-      const float* vdel = vec + kBT;
-      const float* vpre = vec + 2 * kBT;
-      const float* vprel = vec + 3 * kBT;
-      const float* vphi = vec + 4 * kBT;
-      const float* vprey = vec + 5 * kBT;
+      const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
+      const float4* QV = reinterpret_cast<const float4*>(vbase);                // (lse, delta, PRE, prey)
+      const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
+      const float* vphi = reinterpret_cast<const float*>(vbase + 5 * C::VECB);
       const bool diag = k == 0;
       const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
       float rs = fmaxf(c2_s, cmid2);
@@ -307,7 +302,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       // factorised path or none of it does.
       const bool fact = __all_sync(0xffffffffu, vrs && p.prer[size_t(z) * p.NB + i] <= 120.f && bli - rs <= 120.f);
       const float xfac = fact ? ex2(bli - rs) : 0.f;
-      const int tvalid = p.T - i * kBT;  // queries c < tvalid exist
+      const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
       // Diagonal tile: rr = min phi over (key, query]; the second group starts from the minimum over (key, 63].
       float rr = kInf;
       if (diag && grp == 1)
@@ -316,8 +311,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       float fsum = 0.f;
       float* grow = p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
       // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
-      // those 16 columns.
-      auto chunk = [&](int c0, auto fact_tag) {
+      // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches.
+      auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
+        constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
         float sS[16], sP[16];
         tmem_ld16(tl + C::COL_S + c0, sS);
@@ -327,26 +323,32 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int c = c0 + e;
-          const bool valid = s_ok && c < tvalid && (!diag || c >= r);
+          const float4 v = QV[c];
           float x;
-          if (diag) {
-            if (c > r) rr = fminf(rr, vphi[c]);
+          if (DIAG) {
+            rr = c > r ? fminf(rr, vphi[c]) : rr;
             x = rr - psi_s;  // +inf for c <= r
           } else {
-            x = fminf(xs_s, fminf(mid, vpre[c]) - psi_s);
+            x = fminf(xs_s, fminf(mid, v.z) - psi_s);
           }
           const float xm = fminf(x, 0.f);
           const float sv = fmaf(sS[e], p.scale2, betal * xm);
-          const float pp = valid ? ex2(sv - vlse[c]) : 0.f;
-          const float ds = valid ? pp * (sP[e] - vdel[c]) : 0.f;
-          const float g = (valid && x <= 0.f) ? ds : 0.f;
+          float pp = ex2(sv - v.x);
+          float ds = pp * (sP[e] - v.y);
+          if (DIAG) {
+            const bool valid = s_ok && c >= r && c < tvalid;
+            pp = valid ? pp : 0.f;
+            ds = valid ? ds : 0.f;
+          }
+          const float g = x <= 0.f ? ds : 0.f;
           gsum += g;
-          dbsum += ds * xm;
-          if (FACT)
-            fsum += g * rcp_approx(fmaf(vprey[c], xfac, sv_));
-          else if (vrs)
-            fsum += g * rcp_approx(sv_ + ex2(vprel[c] - rs));
-          gb[e] = g;
+          dbsum = fmaf(ds, xm, dbsum);
+          if (!DIAG) {
+            const float den = FACT ? fmaf(v.w, xfac, sv_) : sv_ + ex2(vprel[c] - rs);
+            fsum = fmaf(g, rcp_approx(den), fsum);
+          } else {
+            gb[e] = g;
+          }
           sS[e] = pp;
           sP[e] = ds;
         }
@@ -358,7 +360,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         }
         tmem_st8(tl + C::COL_S + c0, ppk);
         tmem_st8(tl + C::COL_P + c0, dpk);
-        if (diag) {
+        if (DIAG) {
           float4* dst = reinterpret_cast<float4*>(grow + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
@@ -366,11 +368,14 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       };
 #pragma unroll 1
       for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-        if (fact)
-          chunk(c0, std::true_type{});
+        if (diag)
+          chunk(c0, std::true_type{}, std::false_type{});
+        else if (fact)
+          chunk(c0, std::false_type{}, std::true_type{});
         else
-          chunk(c0, std::false_type{});
+          chunk(c0, std::false_type{}, std::false_type{});
       }
+      if (!vrs) fsum = 0.f;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -502,18 +507,15 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 201);
       if (!ok) break;
       if (elect_one()) {
-        uint8_t* vec = smem + C::OFF_VEC + st * C::NVEC * C::VECB;
+        uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
         mbar_expect_tx(st_full + st, 2 * C::TILEB + 5 * C::VECB);
         for (int bx = 0; bx < C::NBOX; ++bx) {
           tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, st_full + st);
           tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, st_full + st);
         }
         const size_t off = zb + size_t(j) * kBT;
-        bulk_load(vec + 0 * C::VECB, p.xs + off, C::VECB, st_full + st);
-        bulk_load(vec + 1 * C::VECB, p.psi + off, C::VECB, st_full + st);
-        bulk_load(vec + 2 * C::VECB, p.sufl + off, C::VECB, st_full + st);
-        bulk_load(vec + 3 * C::VECB, p.phi + off, C::VECB, st_full + st);
-        bulk_load(vec + 4 * C::VECB, p.sufy + off, C::VECB, st_full + st);
+        bulk_load(vec, p.kv4 + off, 4 * C::VECB, st_full + st);
+        bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
       }
       __syncwarp();
     }
@@ -560,8 +562,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     const bool t_ok = t < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
     const float betal = p.beta[h] * kLog2e;
-    const float lse_t = p.lsep[zb + t];
-    const float del_t = t_ok ? p.delta[zb + t] : 0.f;
+    const float4 own = p.qv4[zb + t];  // (lse or +inf beyond T, delta or 0, PRE, prey)
+    const float lse_t = own.x;
+    const float del_t = own.y;
     const float pre_t = p.pre[zb + t];
     const float prel_t = p.prel[zb + t];
     const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
@@ -576,12 +579,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       if (ok) ok = mbar_wait(s_full, k & 1, p.status, 221);
       if (!ok) break;
       tc_fence_after();
-      const float* vec = reinterpret_cast<const float*>(smem + C::OFF_VEC + st * C::NVEC * C::VECB);
-      const float* vxs = vec;
-      const float* vpsi = vec + kBT;
-      const float* vsufl = vec + 2 * kBT;
-      const float* vphi = vec + 3 * kBT;
-      const float* vsufy = vec + 4 * kBT;
+      const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
+      const float4* KV = reinterpret_cast<const float4*>(vbase);   // (SUF - psi, psi, sufy, SUFL)
+      const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
       const bool diag = k == 0;
       const float cap = fminf(mid, pre_t);
       const float mterm = ex2(midl - c2_t) + bpre;
@@ -599,8 +599,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         for (int c = 64; c < kBT; ++c)
           if (c <= r) rr = fminf(rr, vphi[c]);
       // 16 key columns per chunk, in descending order: load S and dP, compute dS (fp16) and write it over the
-      // first 8 of those 16 dP columns.
-      auto chunk = [&](int c0, auto fact_tag) {
+      // first 8 of those 16 dP columns. DIAG and FACT are compile-time so the element loop has no branches.
+      auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
+        constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
         float sS[16], sP[16];
         tmem_ld16(tl + C::COL_S + c0, sS);
@@ -609,24 +610,25 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 #pragma unroll
         for (int e = 15; e >= 0; --e) {
           const int c = c0 + e;
-          const bool valid = t_ok && c < kvalid && (!diag || c <= r);
+          const float4 v = KV[c];
           float x;
-          if (diag) {
-            x = rr - vpsi[c];  // +inf at c == r
-            if (c <= r) rr = fminf(rr, vphi[c]);
+          if (DIAG) {
+            x = rr - v.y;  // +inf at c == r
+            rr = c <= r ? fminf(rr, vphi[c]) : rr;
           } else {
-            x = fminf(vxs[c], cap - vpsi[c]);
+            x = fminf(v.x, cap - v.y);
           }
           const float xm = fminf(x, 0.f);
           const float sv = fmaf(sS[e], p.scale2, betal * xm);
-          const float pp = valid ? ex2(sv - lse_t) : 0.f;
-          const float ds = valid ? pp * (sP[e] - del_t) : 0.f;
-          if (!diag) {
-            const float g = (valid && x <= 0.f) ? ds : 0.f;
-            if (FACT)
-              racc += g * rcp_approx(fmaf(vsufy[c], yfac, mterm));
-            else
-              racc += g * rcp_approx(ex2(vsufl[c] - c2_t) + mterm);
+          float pp = ex2(sv - lse_t);
+          float ds = pp * (sP[e] - del_t);
+          if (DIAG) {
+            const bool valid = c <= r && c < kvalid;
+            ds = valid ? ds : 0.f;
+          } else {
+            const float g = x <= 0.f ? ds : 0.f;
+            const float den = FACT ? fmaf(v.z, yfac, mterm) : ex2(v.w - c2_t) + mterm;
+            racc = fmaf(g, rcp_approx(den), racc);
           }
           sP[e] = ds;
         }
@@ -637,10 +639,12 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       };
 #pragma unroll 1
       for (int c0 = cb + 48; c0 >= cb; c0 -= 16) {
-        if (fact)
-          chunk(c0, std::true_type{});
+        if (diag)
+          chunk(c0, std::true_type{}, std::false_type{});
+        else if (fact)
+          chunk(c0, std::false_type{}, std::true_type{});
         else
-          chunk(c0, std::false_type{});
+          chunk(c0, std::false_type{}, std::false_type{});
       }
       tmem_st_wait();
       tc_fence_before();
@@ -701,7 +705,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
-               const Fact& fact, float* gd, float* lsep, int* status, cudaStream_t s, std::string* err) {
+               const Fact& fact, float* gd, const float4* qv4, int* status, cudaStream_t s, std::string* err) {
   using C = TcBwdCfg<D>;
   CUtensorMap mq, mk, mv, mdo;
   if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
@@ -711,7 +715,8 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     return FPA_ERR_CUDA;
   }
   TcBwdParams p;
-  p.lsep = lsep;
+  p.qv4 = qv4;
+  p.kv4 = fact.kv4;
   p.delta = sc.delta;
   p.pre = st.pre;
   p.prel = st.prel;
@@ -783,7 +788,8 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
 size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
   return keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * sizeof(float)) +
-         3 * align256(bh * d.TP * sizeof(float)) + 2 * align256(bh * d.NB * sizeof(float));
+         2 * align256(bh * d.TP * sizeof(float4)) + 2 * align256(bh * d.TP * sizeof(float)) +
+         2 * align256(bh * d.NB * sizeof(float));
 }
 
 int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
@@ -808,9 +814,11 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   KeyCols cols = carve_keycols(extra, d);
   float* gd = reinterpret_cast<float*>(extra + keycols_bytes(d));
   char* q = extra + keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * 4);
-  float* lsep = reinterpret_cast<float*>(q);
-  q += align256(bh * d.TP * 4);
+  float4* qv4 = reinterpret_cast<float4*>(q);
+  q += align256(bh * d.TP * sizeof(float4));
   Fact fact;
+  fact.kv4 = reinterpret_cast<float4*>(q);
+  q += align256(bh * d.TP * sizeof(float4));
   fact.prey = reinterpret_cast<float*>(q);
   q += align256(bh * d.TP * 4);
   fact.sufy = reinterpret_cast<float*>(q);
@@ -823,7 +831,11 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
   if (e == cudaSuccess) {
     prof_mark(s, "delta");
-    e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, a.lse, lsep, s);
+    e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, nullptr, nullptr, s);
+  }
+  if (e == cudaSuccess) {
+    prof_mark(s, "qv_pack");
+    e = launch_qv_pack(a.lse, sc.delta, st.pre, fact.prey, d, qv4, s);
   }
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward prologue: ") + cudaGetErrorString(e);
@@ -831,13 +843,13 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   }
   int rc;
   switch (d.D) {
-    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
-    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
-    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
-    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, lsep, status, s, err); break;
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  if (rc == FPA_OK) *launched = 5;  // stats, delta, kv-pass, diagonal dphi, q-pass
+  if (rc == FPA_OK) *launched = 6;  // stats, delta, qv pack, kv-pass, diagonal dphi, q-pass
   return rc;
 }
 
