@@ -9,9 +9,9 @@ size_t stats_bytes(const Dims& d) {
   return 4 * align256(bh * d.TP * sizeof(float)) + 2 * align256(bh * d.NB * sizeof(float));
 }
 
-size_t bwd_scratch_bytes(const Dims& d) {
+size_t bwd_scratch_bytes(const Dims& d, int tb_parts) {
   size_t bh = size_t(d.BH());
-  return 4 * align256(bh * d.TP * sizeof(float)) + align256(bh * d.NB * d.NB * sizeof(float)) +
+  return 4 * align256(bh * d.TP * sizeof(float)) + align256(bh * d.NB * d.NB * tb_parts * sizeof(float)) +
          align256(bh * d.NB * sizeof(float));
 }
 
@@ -33,14 +33,15 @@ Stats carve_stats(char* base, const Dims& d) {
   return s;
 }
 
-BwdScratch carve_bwd(char* base, const Dims& d) {
+BwdScratch carve_bwd(char* base, const Dims& d, int tb_parts) {
   size_t bh = size_t(d.BH());
   BwdScratch s;
+  s.tb_parts = tb_parts;
   s.delta = take(base, bh * d.TP);
   s.w = take(base, bh * d.TP);
   s.dphi2 = take(base, bh * d.TP);
   s.dphi4 = take(base, bh * d.TP);
-  s.tb = take(base, bh * d.NB * d.NB);
+  s.tb = take(base, bh * d.NB * d.NB * tb_parts);
   s.dbeta = take(base, bh * d.NB);
   return s;
 }
@@ -136,8 +137,13 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
       fact.sufr[size_t(z) * NB + j] = lv >= 1 ? sufl0 - slse[lv] : 0.f;
     }
     if (fact.kv4) {
+      // Pair layout: keys c, c+1 (c even) share kv4[c] and kv4[c + 1].
       const float y = t < T ? psi[size_t(z) * T + t] : 0.f;
-      fact.kv4[base + tid] = make_float4(t < T ? suf - y : kInf, y, ex2(sufl - sufl0), sufl);
+      float* kv = reinterpret_cast<float*>(fact.kv4 + base + (tid & ~1)) + (tid & 1);
+      kv[0] = t < T ? suf - y : kInf;
+      kv[2] = -y;
+      kv[4] = ex2(sufl - sufl0);
+      kv[6] = sufl;
     }
   }
   if (cols.a) {
@@ -250,22 +256,28 @@ cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, St
   return cudaGetLastError();
 }
 
-// Per-query vectors of the tensor-core kv-pass, interleaved for one 16-byte load per query:
-// qv4[z][t] = (lse_t, delta_t, PRE_t, prey_t); beyond T: (+inf, 0, PRE_t, 1), so padded queries get P = 0.
+// Per-query vectors of the tensor-core backward, two queries t, t+1 (t even) per pair of float4 so the kv-pass
+// reads them as operands of packed f32x2 arithmetic:
+//   qv4[t] = (-lse_t, -lse_t1, -delta_t, -delta_t1),  qv4[t + 1] = (PRE_t, PRE_t1, prey_t, prey_t1);
+// beyond T: lse = +inf, delta = 0, prey = 1, so padded queries get P = 0. One thread per pair.
 __global__ void qv_pack_kernel(const float* __restrict__ lse, const float* __restrict__ delta,
                                const float* __restrict__ pre, const float* __restrict__ prey, int T, int TP, int n,
                                float4* __restrict__ qv4) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n) return;
+  const int pidx = blockIdx.x * blockDim.x + threadIdx.x;  // pair index over [BH][TP / 2]
+  if (2 * pidx >= n) return;
+  const int idx = 2 * pidx;
   const int z = idx / TP, t = idx % TP;
-  const bool ok = t < T;
-  qv4[idx] = make_float4(ok ? lse[size_t(z) * T + t] : kInf, ok ? delta[idx] : 0.f, pre[idx], ok ? prey[idx] : 1.f);
+  const bool ok0 = t < T, ok1 = t + 1 < T;
+  const size_t lz = size_t(z) * T;
+  qv4[idx] = make_float4(ok0 ? -lse[lz + t] : -kInf, ok1 ? -lse[lz + t + 1] : -kInf, ok0 ? -delta[idx] : 0.f,
+                         ok1 ? -delta[idx + 1] : 0.f);
+  qv4[idx + 1] = make_float4(pre[idx], pre[idx + 1], ok0 ? prey[idx] : 1.f, ok1 ? prey[idx + 1] : 1.f);
 }
 
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
                            float4* qv4, cudaStream_t s) {
-  const int n = d.BH() * d.TP;
-  qv_pack_kernel<<<(n + 255) / 256, 256, 0, s>>>(lse, delta, pre, prey, d.T, d.TP, n, qv4);
+  const int n = d.BH() * d.TP;  // TP is a multiple of 128, so pairs never straddle heads
+  qv_pack_kernel<<<(n / 2 + 255) / 256, 256, 0, s>>>(lse, delta, pre, prey, d.T, d.TP, n, qv4);
   return cudaGetLastError();
 }
 
@@ -330,9 +342,14 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
   float s3 = 0.f;
   if (U > 0 && U < NB - 1) {
     const float cU = cb[U];
+    const int np = sc.tb_parts;
     for (int i = U + 1 + tid; i < NB; i += blockDim.x) {
-      const float* row = sc.tb + (size_t(z) * NB + i) * NB;
-      for (int j = 0; j < U; ++j) s3 += ex2(cU - fmaxf(A[j], Bv[i])) * row[j];
+      const float* row = sc.tb + (size_t(z) * NB + i) * NB * np;
+      for (int j = 0; j < U; ++j) {
+        float tbij = 0.f;
+        for (int q = 0; q < np; ++q) tbij += row[j * np + q];
+        s3 += ex2(cU - fmaxf(A[j], Bv[i])) * tbij;
+      }
     }
   }
   float S = block_sum(s3, red);

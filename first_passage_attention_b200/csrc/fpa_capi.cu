@@ -49,6 +49,8 @@ int pick_path(int requested, int dtype, int D) {
 
 int tile_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcBT : fpa::kSimtBT; }
 
+int tb_parts_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcTbParts : 1; }
+
 // The backward follows the same choice as the forward: tensor cores for fp16 with a supported D, FFMA otherwise.
 int bwd_path(int requested, int dtype, int D) { return pick_path(requested, dtype, D); }
 
@@ -59,7 +61,7 @@ size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
 
 size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
-  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d) +
+  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, tb_parts_of(path)) +
          (path == FPA_PATH_TENSOR ? fpa::tc_bwd_extra_bytes(d) : 0);
 }
 
@@ -143,11 +145,11 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   int* status = static_cast<int*>(a->workspace);
   char* ws = static_cast<char*>(a->workspace) + fpa::kStatusBytes;
   fpa::Stats st = fpa::carve_stats(ws, d);
-  fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d);
+  fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d, tb_parts_of(path));
   int n = 0;
   cudaError_t e;
   if (path == FPA_PATH_TENSOR) {
-    char* extra = ws + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d);
+    char* extra = ws + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, sc.tb_parts);
     int m = 0;
     rc = fpa::tc_bwd(*a, d, st, sc, extra, status, s, &m, &g_last_error);
     n += m;

@@ -86,7 +86,9 @@ struct Fact {
   float* sufy;  // [BH][TP]
   float* prer;  // [BH][NB]
   float* sufr;  // [BH][NB]
-  float4* kv4;  // [BH][TP] per key, interleaved for one 16-byte load: (SUF - psi, psi, sufy, SUFL)
+  // [BH][TP] per key, two keys c, c+1 (c even) per pair of float4 for packed f32x2 arithmetic:
+  // kv4[c] = (SUF_c - psi_c, SUF_c1 - psi_c1, -psi_c, -psi_c1), kv4[c + 1] = (sufy_c, sufy_c1, SUFL_c, SUFL_c1)
+  float4* kv4;
 };
 
 // Scratch of the backward pass (all float32, per head z = b*H + h).
@@ -95,8 +97,9 @@ struct BwdScratch {
   float* w;      // [BH][TP]   soft-min partial sums per key, normalised by 2^{c_s} (part "key tile")
   float* dphi2;  // [BH][TP]   soft-min contribution of u in the query's tile
   float* dphi4;  // [BH][TP]   soft-min contribution of u in the diagonal tile
-  float* tb;     // [BH][NB][NB] tile-pair totals, normalised by 2^{cmid}
+  float* tb;     // [BH][NB][NB][tb_parts] tile-pair totals, normalised by 2^{cmid}, as tb_parts partial sums
   float* dbeta;  // [BH][NB]   dbeta partial per key tile
+  int tb_parts;  // partial sums per tile pair (summed in a fixed order by the dphi kernel)
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }

@@ -37,9 +37,9 @@ void set_last_error(const std::string& msg);
 
 // Workspace carving (all arrays 256-byte aligned, after the 256-byte status word).
 size_t stats_bytes(const Dims& d);
-size_t bwd_scratch_bytes(const Dims& d);
+size_t bwd_scratch_bytes(const Dims& d, int tb_parts);
 Stats carve_stats(char* base, const Dims& d);
-BwdScratch carve_bwd(char* base, const Dims& d);
+BwdScratch carve_bwd(char* base, const Dims& d, int tb_parts);
 
 // fpa_aux.cu
 size_t keycols_bytes(const Dims& d);

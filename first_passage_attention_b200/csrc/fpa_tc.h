@@ -9,7 +9,8 @@
 
 namespace fpa {
 
-constexpr int kTcBT = 128;  // positions per tile of the tensor-core kernels (the MMA M and N)
+constexpr int kTcBT = 128;      // positions per tile of the tensor-core kernels (the MMA M and N)
+constexpr int kTcTbParts = 8;  // per-warp partial sums of each tile-pair total of the tensor-core kv-pass
 
 bool tc_supports(int D);
 

@@ -10,11 +10,12 @@
 //                     computes dS (fp16, into its own TMEM columns) and dQ += dS K; also r_t and from it the
 //                     soft-min part with u in the query's tile (DPHI2).
 //
-// Warp roles (384 threads): warps 0-3 and 4-7 are two row groups (thread = TMEM lane) that split the 128 columns
-// of each S / dP tile between them (64 each); warp 8 is the TMA producer (stationary tiles once, streamed tiles and
-// their per-row vectors through a 2-stage ring), warp 9 the MMA issuer (whole warp, one elected lane issues);
-// warps 10-11 only hand their registers to the row groups (setmaxnreg). Every mbarrier wait is bounded
-// (fpa::sm100::mbar_wait).
+// Warp roles (384 threads): warps 0-3 and 4-7 are two row groups (thread = TMEM lane); group g owns columns
+// [64 g, 64 g + 64) of every S / dP tile and runs on its own barriers, so the MMA warp serves the groups in turn
+// (its products for one group overlap the other group's element work). Warp 8 is the TMA producer (stationary
+// tiles once, streamed tiles and their per-row vectors through a 2-stage ring), warp 9 the MMA issuer (whole warp,
+// one elected lane issues); warps 10-11 only hand their registers to the row groups (setmaxnreg). Every mbarrier
+// wait is bounded (fpa::sm100::mbar_wait).
 #include <cuda.h>
 
 #include <type_traits>
@@ -31,8 +32,10 @@ constexpr int kBT = kTcBT;
 constexpr int kThreads = 384;
 constexpr int kWarpProducer = 8;
 constexpr int kWarpMma = 9;
-constexpr int kRowThreads = 256;  // two row groups of 128
-constexpr int kNamedBarRows = 1;  // bar.sync id used by the 256 row threads
+constexpr int kRowThreads = 256;    // two row groups of 128
+constexpr int kGroupThreads = 128;
+constexpr int kHalf = kBT / 2;      // columns of one row group
+constexpr int kNamedBarRows = 1;    // bar.sync id used by the 256 row threads
 
 template <int D>
 struct TcBwdCfg {
@@ -52,9 +55,9 @@ struct TcBwdCfg {
   static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][VECSTAGE]
   static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
   static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
-  static constexpr int NBAR = 1 + 2 * NS + 4;
+  static constexpr int NBAR = 1 + 2 * NS + 2 + 2 + 2;  // a_full, st_full/empty, s_full[2], p_full[2], acc_done, drain
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-  static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
+  static constexpr uint32_t IDESC_S = idesc_f16(kBT, kHalf, 0);  // 128 rows x one group's 64 columns
   static constexpr uint32_t IDESC_ACC = idesc_f16(kBT, D, 1);
   static constexpr int COL_S = 0, COL_P = kBT, COL_A1 = 2 * kBT, COL_A2 = 2 * kBT + D;
 };
@@ -85,7 +88,7 @@ struct TcBwdParams {
   int64_t dq_s[3], dk_s[3], dv_s[3];  // b, h, t strides (d stride 1)
   float* dpsi;         // [BH][T]
   float* w;            // [BH][TP]
-  float* tb;           // [BH][NB][NB]
+  float* tb;           // [BH][NB][NB][kTcTbParts]
   float* dbeta;        // [BH][NB]
   float* gd;           // [BH][NB][128][128]
   float* dphi2;        // [BH][TP]
@@ -122,8 +125,9 @@ __device__ __forceinline__ float rows_sum(float v, float* red) {
 __device__ __forceinline__ void regs_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory"); }
 __device__ __forceinline__ void regs_rows() { asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory"); }
 
+// D[128 x 64] = A[128 x D] * B[64 x D]^T, both K-major in shared memory; `b` points at the group's first B row.
 template <int D>
-__device__ __forceinline__ void issue_ss(uint32_t d, uint32_t a, uint32_t b) {
+__device__ __forceinline__ void issue_ss_half(uint32_t d, uint32_t a, uint32_t b) {
   using C = TcBwdCfg<D>;
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
@@ -133,16 +137,17 @@ __device__ __forceinline__ void issue_ss(uint32_t d, uint32_t a, uint32_t b) {
   }
 }
 
-// D[128 x D] (+)= A[128 x 128 from TMEM, fp16 packed] * B[128 x D from smem, N-contiguous]. The K-step kk of A
-// (16 values, 8 packed columns) sits at column a_tmem + 16 kk: the row groups write it over the first half of the
-// 16 fp32 columns they read it from, so no column is overwritten before it is read.
+// D[128 x D] (+)= A[128 x 64 from TMEM, fp16 packed] * B[64 x D from smem, N-contiguous], for row group g: A holds
+// the group's 64 columns and B its 64 rows (rows 64 g .. 64 g + 63 of the tile). The K-step kk of A (16 values,
+// 8 packed columns) sits at column a_tmem + 16 kk: the row groups write it over the first half of the 16 fp32
+// columns they read it from, so no column is overwritten before it is read.
 template <int D>
-__device__ __forceinline__ void issue_ts(uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
+__device__ __forceinline__ void issue_ts_half(uint32_t d, uint32_t a_tmem, uint32_t b, int g, bool acc) {
   using C = TcBwdCfg<D>;
 #pragma unroll
-  for (int kk = 0; kk < kBT / 16; ++kk)
-    mma_ts_w(d, a_tmem + kk * 16, smem_desc(b + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_ACC,
-             (acc || kk > 0) ? 1u : 0u);
+  for (int kk = 0; kk < kHalf / 16; ++kk)
+    mma_ts_w(d, a_tmem + kk * 16, smem_desc(b + (g * (kHalf / 16) + kk) * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW),
+             C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
 }
 
 // ------------------------------------------------------------------------------------------------ kv-pass ----
@@ -158,9 +163,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   uint64_t* a_full = bars;
   uint64_t* st_full = bars + 1;
   uint64_t* st_empty = st_full + C::NS;
-  uint64_t* s_full = st_empty + C::NS;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* acc_done = p_full + 1;
+  uint64_t* s_full = st_empty + C::NS;  // [2] one per row group
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* acc_done = p_full + 2;
   uint64_t* drain = acc_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
@@ -177,8 +182,10 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kRowThreads);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(p_full + g, kGroupThreads);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -230,32 +237,43 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
       mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 103);
   } else if (warp == kWarpMma) {
+    // Per query tile k and row group g (query columns [64 g, 64 g + 64)): once the group has written P^T and dS^T,
+    // dV += P^T dO and dK += dS^T Q over its 64 queries, then S^T and dP^T of its next tile into the same columns
+    // (tcgen05.mma from one thread execute in order, so the reads come first). While one group waits for these,
+    // the other computes.
     const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
     const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
     bool ok = mbar_wait(a_full, 0, p.status, 110);
     if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 111);
     tc_fence_after();
     if (ok) {
-      issue_ss<D>(tmem + C::COL_S, sa, s1);  // S^T  = K Q^T
-      issue_ss<D>(tmem + C::COL_P, sb, s2);  // dP^T = V dO^T
-      mma_commit_w(s_full);
+      for (int g = 0; g < 2; ++g) {
+        issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + g * kHalf * C::SWB);  // S^T  = K Q^T
+        issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + g * kHalf * C::SWB);  // dP^T = V dO^T
+        mma_commit_w(s_full + g);
+      }
     }
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS;
-      ok = mbar_wait(p_full, k & 1, p.status, 112);
-      if (!ok) break;
-      tc_fence_after();
-      issue_ts<D>(tmem + C::COL_A1, tmem + C::COL_S, s2 + st * C::TILEB, k > 0);  // dV += P^T dO
-      issue_ts<D>(tmem + C::COL_A2, tmem + C::COL_P, s1 + st * C::TILEB, k > 0);  // dK += dS^T Q
-      mma_commit_w(st_empty + st);
-      if (k + 1 < nsteps) {
-        const int st1 = (k + 1) % C::NS;
-        ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 113);
+      for (int g = 0; g < 2 && ok; ++g) {
+        ok = mbar_wait(p_full + g, k & 1, p.status, 112);
         if (!ok) break;
         tc_fence_after();
-        issue_ss<D>(tmem + C::COL_S, sa, s1 + st1 * C::TILEB);
-        issue_ss<D>(tmem + C::COL_P, sb, s2 + st1 * C::TILEB);
-        mma_commit_w(s_full);
+        const bool acc = k > 0 || g > 0;
+        issue_ts_half<D>(tmem + C::COL_A1, tmem + C::COL_S + g * kHalf, s2 + st * C::TILEB, g, acc);  // dV += P^T dO
+        issue_ts_half<D>(tmem + C::COL_A2, tmem + C::COL_P + g * kHalf, s1 + st * C::TILEB, g, acc);  // dK += dS^T Q
+        if (g == 1) mma_commit_w(st_empty + st);
+        if (k + 1 < nsteps) {
+          const int st1 = (k + 1) % C::NS;
+          if (g == 0) {
+            ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 113);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + st1 * C::TILEB + g * kHalf * C::SWB);
+          issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + st1 * C::TILEB + g * kHalf * C::SWB);
+          mma_commit_w(s_full + g);
+        }
       }
     }
     mma_commit_w(acc_done);
@@ -264,30 +282,33 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   } else if (warp < 8) {
     regs_rows();
     const int grp = warp >> 2, wr = warp & 3;
-    const int r = wr * 32 + (threadIdx.x & 31);  // key within the tile = TMEM lane
-    const int cb = grp * 64;                     // this group's query columns [cb, cb + 64)
+    const int r = wr * 32 + lane;  // key within the tile = TMEM lane
+    const int cb = grp * kHalf;    // this group's query columns [cb, cb + 64)
     const int s = j * kBT + r;
     const bool s_ok = s < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
     const float bh = p.beta[h], betal = bh * kLog2e;
     const float psi_s = p.psi[zb + s];
-    const float xs_s = p.xs[zb + s];    // SUF_s - psi_s (+inf for the last key of the tile)
+    const float xs_s = p.xs[zb + s];  // SUF_s - psi_s (+inf for the last key of the tile)
     const float suf_s = p.suf[zb + s];
     const float sufl_s = p.sufl[zb + s];
     const float c2_s = suf_s < kInf ? -suf_s * p.il2 : -kInf;
     const float* bmin = p.bmin + size_t(z) * p.NB;
     const float* bl = p.bl + size_t(z) * p.NB;
+    const float2 sc2 = make_float2(p.scale2, p.scale2), bet2 = make_float2(betal, betal);
+    const float2 npsi2 = make_float2(-psi_s, -psi_s);
     float gsum = 0.f, dbsum = 0.f, wsum = 0.f;
+    float2 gsum2 = make_float2(0.f, 0.f), dbsum2 = make_float2(0.f, 0.f);
     float mid = kInf, midl = -kInf;
     bool ok = true;
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS, i = j + k;
       ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 120);
-      if (ok) ok = mbar_wait(s_full, k & 1, p.status, 121);
+      if (ok) ok = mbar_wait(s_full + grp, k & 1, p.status, 121);
       if (!ok) break;
       tc_fence_after();
       const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
-      const float4* QV = reinterpret_cast<const float4*>(vbase);                // (lse, delta, PRE, prey)
+      const float4* QV = reinterpret_cast<const float4*>(vbase);  // query pairs: (-lse, -delta), (PRE, prey)
       const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
       const float* vphi = reinterpret_cast<const float*>(vbase + 5 * C::VECB);
       const bool diag = k == 0;
@@ -302,16 +323,23 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       // factorised path or none of it does.
       const bool fact = __all_sync(0xffffffffu, vrs && p.prer[size_t(z) * p.NB + i] <= 120.f && bli - rs <= 120.f);
       const float xfac = fact ? ex2(bli - rs) : 0.f;
+      const float2 xf2 = make_float2(xfac, xfac), sv2 = make_float2(sv_, sv_);
       const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
+      // Off the diagonal x_ts = min(a_s, PRE_t - psi_s) with a_s = min(SUF_s - psi_s, mid - psi_s): x_ts <= 0 iff
+      // a_s <= 0 or PRE_t <= psi_s, and min(x_ts, 0) = min(min(a_s, 0), PRE_t - psi_s).
+      const float a_s = fminf(xs_s, mid - psi_s);
+      const float am = fminf(a_s, 0.f);
+      const bool pa = a_s <= 0.f;
       // Diagonal tile: rr = min phi over (key, query]; the second group starts from the minimum over (key, 63].
       float rr = kInf;
       if (diag && grp == 1)
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < kHalf; ++c)
           if (c > r) rr = fminf(rr, vphi[c]);
-      float fsum = 0.f;
+      float2 fsum2 = make_float2(0.f, 0.f);
       float* grow = p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
       // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
-      // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches.
+      // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal
+      // two queries are handled per step with packed f32x2 arithmetic.
       auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
         constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
@@ -319,55 +347,66 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         tmem_ld16(tl + C::COL_S + c0, sS);
         tmem_ld16(tl + C::COL_P + c0, sP);
         tmem_ld_wait();
-        float gb[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int c = c0 + e;
-          const float4 v = QV[c];
-          float x;
-          if (DIAG) {
-            rr = c > r ? fminf(rr, vphi[c]) : rr;
-            x = rr - psi_s;  // +inf for c <= r
-          } else {
-            x = fminf(xs_s, fminf(mid, v.z) - psi_s);
-          }
-          const float xm = fminf(x, 0.f);
-          const float sv = fmaf(sS[e], p.scale2, betal * xm);
-          float pp = ex2(sv - v.x);
-          float ds = pp * (sP[e] - v.y);
-          if (DIAG) {
-            const bool valid = s_ok && c >= r && c < tvalid;
-            pp = valid ? pp : 0.f;
-            ds = valid ? ds : 0.f;
-          }
-          const float g = x <= 0.f ? ds : 0.f;
-          gsum += g;
-          dbsum = fmaf(ds, xm, dbsum);
-          if (!DIAG) {
-            const float den = FACT ? fmaf(v.w, xfac, sv_) : sv_ + ex2(vprel[c] - rs);
-            fsum = fmaf(g, rcp_approx(den), fsum);
-          } else {
-            gb[e] = g;
-          }
-          sS[e] = pp;
-          sP[e] = ds;
-        }
         uint32_t ppk[8], dpk[8];
+        if constexpr (DIAG) {
+          float gb[16];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
-          dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
-        }
-        tmem_st8(tl + C::COL_S + c0, ppk);
-        tmem_st8(tl + C::COL_P + c0, dpk);
-        if (DIAG) {
+          for (int e = 0; e < 16; ++e) {
+            const int c = c0 + e;
+            const float4 va = QV[c0 + (e & ~1)];
+            const float nl = (e & 1) ? va.y : va.x, nd = (e & 1) ? va.w : va.z;
+            rr = c > r ? fminf(rr, vphi[c]) : rr;
+            const float x = rr - psi_s;  // +inf for c <= r
+            const float xm = fminf(x, 0.f);
+            const float sv = fmaf(sS[e], p.scale2, betal * xm);
+            const bool valid = s_ok && c >= r && c < tvalid;
+            const float pp = valid ? ex2(sv + nl) : 0.f;
+            const float ds = valid ? pp * (sP[e] + nd) : 0.f;
+            const float g = x <= 0.f ? ds : 0.f;
+            gsum += g;
+            dbsum = fmaf(ds, xm, dbsum);
+            gb[e] = g;
+            sS[e] = pp;
+            sP[e] = ds;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
+            dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+          }
           float4* dst = reinterpret_cast<float4*>(grow + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float4 va = QV[c0 + e];      // (-lse_c, -lse_c1, -delta_c, -delta_c1)
+            const float4 vb = QV[c0 + e + 1];  // (PRE_c, PRE_c1, prey_c, prey_c1)
+            const float2 dd = __fadd2_rn(make_float2(vb.x, vb.y), npsi2);
+            const float2 xm = make_float2(fminf(am, dd.x), fminf(am, dd.y));
+            const bool in0 = pa || dd.x <= 0.f, in1 = pa || dd.y <= 0.f;
+            float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
+            sv = __fadd2_rn(sv, make_float2(va.x, va.y));
+            const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
+            const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), make_float2(va.z, va.w)));
+            const float2 g = make_float2(in0 ? ds.x : 0.f, in1 ? ds.y : 0.f);
+            gsum2 = __fadd2_rn(gsum2, g);
+            dbsum2 = __ffma2_rn(ds, xm, dbsum2);
+            float2 den;
+            if constexpr (FACT)
+              den = __ffma2_rn(make_float2(vb.z, vb.w), xf2, sv2);
+            else
+              den = make_float2(sv_ + ex2(vprel[c0 + e] - rs), sv_ + ex2(vprel[c0 + e + 1] - rs));
+            fsum2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), fsum2);
+            ppk[e / 2] = pack_half2(pp.x, pp.y);
+            dpk[e / 2] = pack_half2(ds.x, ds.y);
+          }
         }
+        tmem_st8(tl + C::COL_S + c0, ppk);
+        tmem_st8(tl + C::COL_P + c0, dpk);
       };
 #pragma unroll 1
-      for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      for (int c0 = cb; c0 < cb + kHalf; c0 += 16) {
         if (diag)
           chunk(c0, std::true_type{}, std::false_type{});
         else if (fact)
@@ -375,20 +414,23 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         else
           chunk(c0, std::false_type{}, std::false_type{});
       }
-      if (!vrs) fsum = 0.f;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + grp);
       if (!diag) {
+        const float fsum = vrs ? fsum2.x + fsum2.y : 0.f;
         if (vrs) wsum += ex2(c2_s - rs) * fsum;
         if (i > j + 1) {
-          const float tot = rows_sum(vrs ? ex2(cmid2 - rs) * fsum : 0.f, red);
-          if (threadIdx.x == 0) p.tb[(size_t(z) * p.NB + i) * p.NB + j] = tot;
+          // Tile-pair total: one partial per warp (8 per pair), summed in a fixed order by the dphi kernel.
+          const float tot = group_sum<32>(vrs ? ex2(cmid2 - rs) * fsum : 0.f);
+          if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + warp] = tot;
         }
         mid = fminf(mid, bmin[i]);
         midl = lse2(midl, bl[i]);
       }
     }
+    gsum += gsum2.x + gsum2.y;
+    dbsum += dbsum2.x + dbsum2.y;
     // Join the two groups' per-key sums (fixed order: group 0 + group 1).
     float* xg = red + 32;
     float* xw = red + 32 + kBT;
@@ -453,9 +495,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   uint64_t* a_full = bars;
   uint64_t* st_full = bars + 1;
   uint64_t* st_empty = st_full + C::NS;
-  uint64_t* s_full = st_empty + C::NS;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* acc_done = p_full + 1;
+  uint64_t* s_full = st_empty + C::NS;  // [2] one per row group
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* acc_done = p_full + 2;
   uint64_t* drain = acc_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
@@ -472,8 +514,10 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kRowThreads);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(p_full + g, kGroupThreads);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -523,31 +567,40 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
       mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 203);
   } else if (warp == kWarpMma) {
+    // Per key tile k and row group g (key columns [64 g, 64 g + 64)): once the group has written dS, dQ += dS K
+    // over its 64 keys, then S and dP of its next tile into the same columns (in issue order, so the read of dS
+    // comes first). While one group waits for these, the other computes.
     const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
     const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
     bool ok = mbar_wait(a_full, 0, p.status, 210);
     if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 211);
     tc_fence_after();
     if (ok) {
-      issue_ss<D>(tmem + C::COL_S, sa, s1);  // S  = Q K^T
-      issue_ss<D>(tmem + C::COL_P, sb, s2);  // dP = dO V^T
-      mma_commit_w(s_full);
+      for (int g = 0; g < 2; ++g) {
+        issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + g * kHalf * C::SWB);  // S  = Q K^T
+        issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + g * kHalf * C::SWB);  // dP = dO V^T
+        mma_commit_w(s_full + g);
+      }
     }
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS;
-      ok = mbar_wait(p_full, k & 1, p.status, 212);
-      if (!ok) break;
-      tc_fence_after();
-      issue_ts<D>(tmem + C::COL_A1, tmem + C::COL_P, s1 + st * C::TILEB, k > 0);  // dQ += dS K
-      mma_commit_w(st_empty + st);
-      if (k + 1 < nsteps) {
-        const int st1 = (k + 1) % C::NS;
-        ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 213);
+      for (int g = 0; g < 2 && ok; ++g) {
+        ok = mbar_wait(p_full + g, k & 1, p.status, 212);
         if (!ok) break;
         tc_fence_after();
-        issue_ss<D>(tmem + C::COL_S, sa, s1 + st1 * C::TILEB);
-        issue_ss<D>(tmem + C::COL_P, sb, s2 + st1 * C::TILEB);
-        mma_commit_w(s_full);
+        issue_ts_half<D>(tmem + C::COL_A1, tmem + C::COL_P + g * kHalf, s1 + st * C::TILEB, g, k > 0 || g > 0);
+        if (g == 1) mma_commit_w(st_empty + st);
+        if (k + 1 < nsteps) {
+          const int st1 = (k + 1) % C::NS;
+          if (g == 0) {
+            ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 213);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + st1 * C::TILEB + g * kHalf * C::SWB);
+          issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + st1 * C::TILEB + g * kHalf * C::SWB);
+          mma_commit_w(s_full + g);
+        }
       }
     }
     mma_commit_w(acc_done);
@@ -557,30 +610,33 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     regs_rows();
     const int grp = warp >> 2, wr = warp & 3;
     const int r = wr * 32 + (threadIdx.x & 31);  // query within the tile = TMEM lane
-    const int cb = grp * 64;                     // this group's key columns [cb, cb + 64)
+    const int cb = grp * kHalf;                  // this group's key columns [cb, cb + 64)
     const int t = i * kBT + r;
     const bool t_ok = t < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
     const float betal = p.beta[h] * kLog2e;
-    const float4 own = p.qv4[zb + t];  // (lse or +inf beyond T, delta or 0, PRE, prey)
-    const float lse_t = own.x;
-    const float del_t = own.y;
+    const float* own = reinterpret_cast<const float*>(p.qv4 + zb + (t & ~1));  // (-lse, -delta) pair of t
+    const float nlse = own[t & 1];   // -inf beyond T
+    const float ndel = own[2 + (t & 1)];
     const float pre_t = p.pre[zb + t];
     const float prel_t = p.prel[zb + t];
     const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
     const float bpre = t_ok ? ex2(prel_t - c2_t) : 1.f;
     const float* bmin = p.bmin + size_t(z) * p.NB;
     const float* bl = p.bl + size_t(z) * p.NB;
-    float racc = 0.f, mid = kInf, midl = -kInf;
+    const float2 sc2 = make_float2(p.scale2, p.scale2), bet2 = make_float2(betal, betal);
+    const float2 nlse2 = make_float2(nlse, nlse), ndel2 = make_float2(ndel, ndel);
+    float2 racc2 = make_float2(0.f, 0.f);
+    float mid = kInf, midl = -kInf;
     bool ok = true;
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS, j = i - k;
       ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 220);
-      if (ok) ok = mbar_wait(s_full, k & 1, p.status, 221);
+      if (ok) ok = mbar_wait(s_full + grp, k & 1, p.status, 221);
       if (!ok) break;
       tc_fence_after();
       const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
-      const float4* KV = reinterpret_cast<const float4*>(vbase);   // (SUF - psi, psi, sufy, SUFL)
+      const float4* KV = reinterpret_cast<const float4*>(vbase);  // key pairs: (SUF - psi, -psi), (sufy, SUFL)
       const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
       const bool diag = k == 0;
       const float cap = fminf(mid, pre_t);
@@ -591,15 +647,17 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (p.sufr[size_t(z) * p.NB + j] <= 120.f &&
                                                                       sufl0 - c2_t <= 120.f)));
       const float yfac = (fact && t_ok) ? ex2(sufl0 - c2_t) : 0.f;
+      const float2 cap2 = make_float2(cap, cap), yf2 = make_float2(yfac, yfac), mt2 = make_float2(mterm, mterm);
       const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
       // Diagonal tile, keys descending: rr = min phi over (key, query]; the first group starts from the minimum
       // over the second group's keys up to the query, [64, query].
       float rr = kInf;
       if (diag && grp == 0)
-        for (int c = 64; c < kBT; ++c)
+        for (int c = kHalf; c < kBT; ++c)
           if (c <= r) rr = fminf(rr, vphi[c]);
-      // 16 key columns per chunk, in descending order: load S and dP, compute dS (fp16) and write it over the
-      // first 8 of those 16 dP columns. DIAG and FACT are compile-time so the element loop has no branches.
+      // 16 key columns per chunk: load S and dP, compute dS (fp16) and write it over the first 8 of those 16 dP
+      // columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal two keys
+      // are handled per step with packed f32x2 arithmetic.
       auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
         constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
@@ -607,38 +665,48 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         tmem_ld16(tl + C::COL_S + c0, sS);
         tmem_ld16(tl + C::COL_P + c0, sP);
         tmem_ld_wait();
-#pragma unroll
-        for (int e = 15; e >= 0; --e) {
-          const int c = c0 + e;
-          const float4 v = KV[c];
-          float x;
-          if (DIAG) {
-            x = rr - v.y;  // +inf at c == r
-            rr = c <= r ? fminf(rr, vphi[c]) : rr;
-          } else {
-            x = fminf(v.x, cap - v.y);
-          }
-          const float xm = fminf(x, 0.f);
-          const float sv = fmaf(sS[e], p.scale2, betal * xm);
-          float pp = ex2(sv - lse_t);
-          float ds = pp * (sP[e] - del_t);
-          if (DIAG) {
-            const bool valid = c <= r && c < kvalid;
-            ds = valid ? ds : 0.f;
-          } else {
-            const float g = x <= 0.f ? ds : 0.f;
-            const float den = FACT ? fmaf(v.z, yfac, mterm) : ex2(v.w - c2_t) + mterm;
-            racc = fmaf(g, rcp_approx(den), racc);
-          }
-          sP[e] = ds;
-        }
         uint32_t dpk[8];
+        if constexpr (DIAG) {
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+          for (int e = 15; e >= 0; --e) {
+            const int c = c0 + e;
+            const float4 va = KV[c0 + (e & ~1)];
+            const float npsi = (e & 1) ? va.w : va.z;
+            const float x = rr + npsi;  // +inf at c == r
+            rr = c <= r ? fminf(rr, vphi[c]) : rr;
+            const float xm = fminf(x, 0.f);
+            const float sv = fmaf(sS[e], p.scale2, betal * xm);
+            const bool valid = c <= r && c < kvalid;
+            sP[e] = valid ? ex2(sv + nlse) * (sP[e] + ndel) : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float4 va = KV[c0 + e];      // (SUF_c - psi_c, SUF_c1 - psi_c1, -psi_c, -psi_c1)
+            const float4 vb = KV[c0 + e + 1];  // (sufy_c, sufy_c1, SUFL_c, SUFL_c1)
+            const float2 dd = __fadd2_rn(cap2, make_float2(va.z, va.w));
+            const float2 x = make_float2(fminf(va.x, dd.x), fminf(va.y, dd.y));
+            const float2 xm = make_float2(fminf(x.x, 0.f), fminf(x.y, 0.f));
+            float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
+            sv = __fadd2_rn(sv, nlse2);
+            const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
+            const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), ndel2));
+            const float2 g = make_float2(x.x <= 0.f ? ds.x : 0.f, x.y <= 0.f ? ds.y : 0.f);
+            float2 den;
+            if constexpr (FACT)
+              den = __ffma2_rn(make_float2(vb.x, vb.y), yf2, mt2);
+            else
+              den = make_float2(ex2(vb.z - c2_t) + mterm, ex2(vb.w - c2_t) + mterm);
+            racc2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), racc2);
+            dpk[e / 2] = pack_half2(ds.x, ds.y);
+          }
+        }
         tmem_st8(tl + C::COL_P + c0, dpk);
       };
 #pragma unroll 1
-      for (int c0 = cb + 48; c0 >= cb; c0 -= 16) {
+      for (int c0 = cb + kHalf - 16; c0 >= cb; c0 -= 16) {
         if (diag)
           chunk(c0, std::true_type{}, std::false_type{});
         else if (fact)
@@ -648,12 +716,13 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + grp);
       if (!diag) {
         mid = fminf(mid, bmin[j]);
         midl = lse2(midl, bl[j]);
       }
     }
+    const float racc = racc2.x + racc2.y;
     if (ok) ok = mbar_wait(acc_done, 0, p.status, 222);
     if (ok) {
       tc_fence_after();
