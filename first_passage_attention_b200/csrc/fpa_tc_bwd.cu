@@ -37,29 +37,48 @@ constexpr int kGroupThreads = 128;
 constexpr int kHalf = kBT / 2;      // columns of one row group
 constexpr int kNamedBarRows = 1;    // bar.sync id used by the 256 row threads
 
+// Shared-memory layout of one [128 x D] fp16 tile as TMA writes it: boxes of 128 rows x min(64, D) columns with
+// the swizzle of the box row width.
 template <int D>
-struct TcBwdCfg {
+struct TileLayout {
   static constexpr int BOXC = D >= 64 ? 64 : D;
   static constexpr int NBOX = D / BOXC;
   static constexpr int SWB = BOXC * 2;
   static constexpr int BOXB = kBT * SWB;
   static constexpr int TILEB = NBOX * BOXB;
   static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
-  static constexpr int NS = 2;
-  static constexpr int VECB = kBT * 4;
-  static constexpr int VECSTAGE = 4 * VECB + 2 * VECB;   // float4 per row + two float vectors, per stage
-  static constexpr int OFF_A = 0;                        // stationary operand 1
-  static constexpr int OFF_B = TILEB;                    // stationary operand 2
-  static constexpr int OFF_S1 = 2 * TILEB;               // streamed operand 1 [NS]
-  static constexpr int OFF_S2 = OFF_S1 + NS * TILEB;     // streamed operand 2 [NS]
-  static constexpr int OFF_VEC = OFF_S2 + NS * TILEB;    // [NS][VECSTAGE]
-  static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
-  static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
-  static constexpr int NBAR = 1 + 2 * NS + 2 + 2 + 2;  // a_full, st_full/empty, s_full[2], p_full[2], acc_done, drain
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static constexpr uint32_t IDESC_S = idesc_f16(kBT, kHalf, 0);  // 128 rows x one group's 64 columns
   static constexpr uint32_t IDESC_ACC = idesc_f16(kBT, D, 1);
-  static constexpr int COL_S = 0, COL_P = kBT, COL_A1 = 2 * kBT, COL_A2 = 2 * kBT + D;
+};
+
+// Per-pass configuration. TMEM holds NSLOT slots of 128 columns, each the job of one row group for one tile (its
+// 64 columns of S, then its 64 columns of dP); job n = 2 k + g (tile k, group g) uses slot n % NSLOT, so with three
+// slots the products of a group's next tile are computed while it still works on the current one. The
+// accumulators follow the slots (dV, dK for the kv-pass; dQ for the q-pass), then the two stationary operands
+// (D/2 columns each) when they fit in the 512 columns; otherwise those are read from shared memory.
+template <int D, bool KV>
+struct TcBwdCfg : TileLayout<D> {
+  using L = TileLayout<D>;
+  static constexpr int NSLOT = D <= 64 ? 3 : 2;
+  static constexpr int NS = NSLOT;  // shared-memory stages of the streamed tiles
+  static constexpr int COL_A1 = 128 * NSLOT, COL_A2 = COL_A1 + D;
+  static constexpr int COL_X = COL_A1 + (KV ? 2 : 1) * D;
+  static constexpr bool AT = COL_X + D <= 512;
+  static constexpr int NSTAT = AT ? 0 : 2;  // stationary tiles kept in shared memory
+  static constexpr int VECB = kBT * 4;
+  static constexpr int VECSTAGE = 4 * VECB + 2 * VECB;  // float4 per row + two float vectors, per stage
+  static constexpr int OFF_A = 0;                       // stationary operand 1 (when !AT)
+  static constexpr int OFF_B = L::TILEB;                // stationary operand 2 (when !AT)
+  static constexpr int OFF_S1 = NSTAT * L::TILEB;       // streamed operand 1 [NS]
+  static constexpr int OFF_S2 = OFF_S1 + NS * L::TILEB;  // streamed operand 2 [NS]
+  static constexpr int OFF_VEC = OFF_S2 + NS * L::TILEB;  // [NS][VECSTAGE]
+  static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
+  static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
+  // a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full
+  static constexpr int NBAR = 1 + 2 * NS + 2 * NSLOT + 2 + 1;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(KV || AT, "the q-pass keeps Q and dO in TMEM");
 };
 
 struct TcBwdParams {
@@ -82,6 +101,12 @@ struct TcBwdParams {
   const float* prer;   // [BH][NB] BL - PREL_first
   const float* sufr;   // [BH][NB] SUFL_first - min finite SUFL
   // outputs
+  // inputs read row by row into TMEM (the stationary MMA operands)
+  const __half* q;
+  const __half* k;
+  const __half* v;
+  const __half* dout;
+  int64_t q_s[3], k_s[3], v_s[3], do_s[3];  // b, h, t strides (d stride 1)
   __half* dq;
   __half* dk;
   __half* dv;
@@ -122,18 +147,25 @@ __device__ __forceinline__ float rows_sum(float v, float* red) {
   return r;
 }
 
-__device__ __forceinline__ void regs_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory"); }
-__device__ __forceinline__ void regs_rows() { asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory"); }
+__device__ __forceinline__ void regs_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory"); }
+__device__ __forceinline__ void regs_rows() { asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory"); }
+
+// The descriptor of the same operand layout `off` bytes further on: the start address is the low 14-bit field
+// (address >> 4) and shared-memory addresses stay below 2^18, so the offset adds to the low word without a carry.
+// Built once per operand, each K-step then costs one integer add in the MMA warp.
+__device__ __forceinline__ uint64_t desc_at(uint64_t d, uint32_t off) {
+  return (d & 0xFFFFFFFF00000000ull) | uint32_t(uint32_t(d) + (off >> 4));
+}
 
 // D[128 x 64] = A[128 x D] * B[64 x D]^T, both K-major in shared memory; `b` points at the group's first B row.
 template <int D>
 __device__ __forceinline__ void issue_ss_half(uint32_t d, uint32_t a, uint32_t b) {
-  using C = TcBwdCfg<D>;
+  using C = TileLayout<D>;
+  const uint64_t da = smem_desc(a, 16, 8 * C::SWB, C::SW), db = smem_desc(b, 16, 8 * C::SWB, C::SW);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
-    mma_ss_w(d, smem_desc(a + off, 16, 8 * C::SWB, C::SW), smem_desc(b + off, 16, 8 * C::SWB, C::SW), C::IDESC_S,
-             kk > 0);
+    mma_ss_w(d, desc_at(da, off), desc_at(db, off), C::IDESC_S, kk > 0);
   }
 }
 
@@ -143,11 +175,47 @@ __device__ __forceinline__ void issue_ss_half(uint32_t d, uint32_t a, uint32_t b
 // columns they read it from, so no column is overwritten before it is read.
 template <int D>
 __device__ __forceinline__ void issue_ts_half(uint32_t d, uint32_t a_tmem, uint32_t b, int g, bool acc) {
-  using C = TcBwdCfg<D>;
+  using C = TileLayout<D>;
+  const uint64_t db = smem_desc(b + g * kHalf * C::SWB, C::BOXB, 8 * C::SWB, C::SW);
 #pragma unroll
   for (int kk = 0; kk < kHalf / 16; ++kk)
-    mma_ts_w(d, a_tmem + kk * 16, smem_desc(b + (g * (kHalf / 16) + kk) * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW),
-             C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
+    mma_ts_w(d, a_tmem + kk * 16, desc_at(db, kk * 16 * C::SWB), C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
+}
+
+// D[128 x 64] = A[128 x D from TMEM] * B[64 x D]^T (B K-major in shared memory, `b` at the group's first row).
+// A is packed densely, two fp16 per 32-bit column in K order: K-step kk (16 values) at columns a_tmem + 8 kk.
+template <int D>
+__device__ __forceinline__ void issue_ts_k(uint32_t d, uint32_t a_tmem, uint32_t b) {
+  using C = TileLayout<D>;
+  const uint64_t db = smem_desc(b, 16, 8 * C::SWB, C::SW);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
+    mma_ts_w(d, a_tmem + 8 * kk, desc_at(db, off), C::IDESC_S, kk > 0);
+  }
+}
+
+// One row of a stationary operand (D fp16 values, zeros when !ok) into this thread's TMEM lane, D/2 columns from
+// `taddr` (the packing issue_ts_k expects). Warp-collective.
+template <int D>
+__device__ __forceinline__ void row_to_tmem(uint32_t taddr, const __half* row, bool ok) {
+  uint32_t u[D / 2];
+#pragma unroll
+  for (int q = 0; q < D / 8; ++q) {
+    const uint4 x = ok ? reinterpret_cast<const uint4*>(row)[q] : make_uint4(0u, 0u, 0u, 0u);
+    u[4 * q] = x.x;
+    u[4 * q + 1] = x.y;
+    u[4 * q + 2] = x.z;
+    u[4 * q + 3] = x.w;
+  }
+  if constexpr (D == 16) {
+    tmem_st8(taddr, u);
+  } else if constexpr (D == 32) {
+    tmem_st16(taddr, u);
+  } else {
+#pragma unroll
+    for (int c = 0; c < D / 2; c += 32) tmem_st32(taddr + c, u + c);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ kv-pass ----
@@ -156,18 +224,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                  const TcBwdParams p) {
-  using C = TcBwdCfg<D>;
+  using C = TcBwdCfg<D, true>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* a_full = bars;
   uint64_t* st_full = bars + 1;
   uint64_t* st_empty = st_full + C::NS;
-  uint64_t* s_full = st_empty + C::NS;  // [2] one per row group
-  uint64_t* p_full = s_full + 2;        // [2]
-  uint64_t* acc_done = p_full + 2;
+  uint64_t* s_full = st_empty + C::NS;  // [NSLOT] S and dP of the job in the slot are ready
+  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT] the group of the job in the slot has written its P / dS
+  uint64_t* acc_done = p_full + C::NSLOT;
   uint64_t* drain = acc_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* at_full = drain + 1;        // stationary operands written into TMEM by the row threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(at_full + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -175,6 +244,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   const int j = int(blockIdx.x) / nbh;  // key tile 0 has the most query tiles: first in launch order
   const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
   const int nsteps = p.NB - j;
+  // K and V as TMEM operands of S^T and dP^T (both stationary) when the columns fit.
+  constexpr bool AT = C::AT;
+  constexpr int COL_K = C::COL_X, COL_V = COL_K + D / 2;
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
@@ -182,12 +254,13 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(s_full + g, 1);
-      mbar_init(p_full + g, kGroupThreads);
+    for (int x = 0; x < C::NSLOT; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, kGroupThreads);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
+    mbar_init(at_full, kRowThreads);
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -196,8 +269,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const size_t zb = size_t(z) * p.TP;
-  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 56 and the
-  // two row groups take 224 each (128*56 + 256*224 = 384*168).
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
+  // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
   if (warp >= 8) regs_producer();
 
   if (warp == kWarpProducer) {
@@ -206,10 +279,12 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
-      mbar_expect_tx(a_full, 2 * C::TILEB);
-      for (int bx = 0; bx < C::NBOX; ++bx) {
-        tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
-        tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
+      if constexpr (!AT) {
+        mbar_expect_tx(a_full, 2 * C::TILEB);
+        for (int bx = 0; bx < C::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
+          tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
+        }
       }
     }
     __syncwarp();
@@ -233,48 +308,54 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       }
       __syncwarp();
     }
-    mbar_wait(a_full, 0, p.status, 102);
+    if constexpr (!AT) mbar_wait(a_full, 0, p.status, 102);
     for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
       mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 103);
   } else if (warp == kWarpMma) {
-    // Per query tile k and row group g (query columns [64 g, 64 g + 64)): once the group has written P^T and dS^T,
-    // dV += P^T dO and dK += dS^T Q over its 64 queries, then S^T and dP^T of its next tile into the same columns
-    // (tcgen05.mma from one thread execute in order, so the reads come first). While one group waits for these,
-    // the other computes.
+    // Jobs n = 2 k + g in order (query tile k, row group g = query columns [64 g, 64 g + 64)). S^T and dP^T of job
+    // n go into slot n % NSLOT; once the group has written P^T and dS^T there, dV += P^T dO and dK += dS^T Q over
+    // its 64 queries, then the products of job n + NSLOT into the same slot (tcgen05.mma from one thread execute
+    // in order, so the reads come first).
     const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
     const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
-    bool ok = mbar_wait(a_full, 0, p.status, 110);
-    if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 111);
-    tc_fence_after();
-    if (ok) {
-      for (int g = 0; g < 2; ++g) {
-        issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + g * kHalf * C::SWB);  // S^T  = K Q^T
-        issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + g * kHalf * C::SWB);  // dP^T = V dO^T
-        mma_commit_w(s_full + g);
+    const int njobs = 2 * nsteps;
+    auto issue_s = [&](int n) {
+      const int g = n & 1, st = (n >> 1) % C::NS;
+      const uint32_t dcol = tmem + (n % C::NSLOT) * 128;
+      const uint32_t bq = s1 + st * C::TILEB + g * kHalf * C::SWB, bdo = s2 + st * C::TILEB + g * kHalf * C::SWB;
+      if constexpr (AT) {
+        issue_ts_k<D>(dcol, tmem + COL_K, bq);              // S^T  = K Q^T
+        issue_ts_k<D>(dcol + kHalf, tmem + COL_V, bdo);     // dP^T = V dO^T
+      } else {
+        issue_ss_half<D>(dcol, sa, bq);
+        issue_ss_half<D>(dcol + kHalf, sb, bdo);
       }
-    }
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS;
-      for (int g = 0; g < 2 && ok; ++g) {
-        ok = mbar_wait(p_full + g, k & 1, p.status, 112);
-        if (!ok) break;
+      mma_commit_w(s_full + n % C::NSLOT);
+    };
+    bool ok = AT ? mbar_wait(at_full, 0, p.status, 115) : mbar_wait(a_full, 0, p.status, 110);
+    int loaded = -1;  // streamed tiles known to be in shared memory: 0 .. loaded
+    auto need_tile = [&](int kt) {
+      if (ok && kt > loaded) {
+        ok = mbar_wait(st_full + kt % C::NS, (kt / C::NS) & 1, p.status, 111);
+        loaded = kt;
         tc_fence_after();
-        const bool acc = k > 0 || g > 0;
-        issue_ts_half<D>(tmem + C::COL_A1, tmem + C::COL_S + g * kHalf, s2 + st * C::TILEB, g, acc);  // dV += P^T dO
-        issue_ts_half<D>(tmem + C::COL_A2, tmem + C::COL_P + g * kHalf, s1 + st * C::TILEB, g, acc);  // dK += dS^T Q
-        if (g == 1) mma_commit_w(st_empty + st);
-        if (k + 1 < nsteps) {
-          const int st1 = (k + 1) % C::NS;
-          if (g == 0) {
-            ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 113);
-            if (!ok) break;
-            tc_fence_after();
-          }
-          issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + st1 * C::TILEB + g * kHalf * C::SWB);
-          issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + st1 * C::TILEB + g * kHalf * C::SWB);
-          mma_commit_w(s_full + g);
-        }
       }
+      return ok;
+    };
+    tc_fence_after();
+    for (int n = 0; n < C::NSLOT && n < njobs; ++n)
+      if (need_tile(n >> 1)) issue_s(n);
+    for (int n = 0; n < njobs && ok; ++n) {
+      const int g = n & 1, k = n >> 1, st = k % C::NS;
+      ok = mbar_wait(p_full + n % C::NSLOT, (n / C::NSLOT) & 1, p.status, 112);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t acol = tmem + (n % C::NSLOT) * 128;
+      issue_ts_half<D>(tmem + C::COL_A1, acol, s2 + st * C::TILEB, g, n > 0);          // dV += P^T dO
+      issue_ts_half<D>(tmem + C::COL_A2, acol + kHalf, s1 + st * C::TILEB, g, n > 0);  // dK += dS^T Q
+      if (g == 1) mma_commit_w(st_empty + st);
+      const int m = n + C::NSLOT;
+      if (m < njobs && need_tile(m >> 1)) issue_s(m);
     }
     mma_commit_w(acc_done);
     mma_commit_w(drain);
@@ -287,6 +368,15 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     const int s = j * kBT + r;
     const bool s_ok = s < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
+    if constexpr (AT) {
+      // Group 0 writes the key's row of K, group 1 its row of V, into TMEM.
+      const __half* row = grp == 0 ? p.k + b * p.k_s[0] + h * p.k_s[1] + int64_t(s_ok ? s : 0) * p.k_s[2]
+                                   : p.v + b * p.v_s[0] + h * p.v_s[1] + int64_t(s_ok ? s : 0) * p.v_s[2];
+      row_to_tmem<D>(tl + (grp == 0 ? COL_K : COL_V), row, s_ok);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(at_full);
+    }
     const float bh = p.beta[h], betal = bh * kLog2e;
     const float psi_s = p.psi[zb + s];
     const float xs_s = p.xs[zb + s];  // SUF_s - psi_s (+inf for the last key of the tile)
@@ -301,12 +391,25 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     float2 gsum2 = make_float2(0.f, 0.f), dbsum2 = make_float2(0.f, 0.f);
     float mid = kInf, midl = -kInf;
     bool ok = true;
+    // Per-tile scalars of query tile i, loaded one tile ahead so their latency hides behind the element work.
+    const float* prer = p.prer + size_t(z) * p.NB;
+    float bl_n = bl[j], bmin_n = bmin[j], prer_n = prer[j];
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS, i = j + k;
+      const float bli = bl_n, bmini = bmin_n, preri = prer_n;
+      if (i + 1 < p.NB) {
+        bl_n = bl[i + 1];
+        bmin_n = bmin[i + 1];
+        prer_n = prer[i + 1];
+      }
+      const int n = 2 * k + grp, slot = n % C::NSLOT;
       ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 120);
-      if (ok) ok = mbar_wait(s_full + grp, k & 1, p.status, 121);
+      if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 121);
       if (!ok) break;
       tc_fence_after();
+      // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
+      // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
+      const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
       const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
       const float4* QV = reinterpret_cast<const float4*>(vbase);  // query pairs: (-lse, -delta), (PRE, prey)
       const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
@@ -318,10 +421,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       rs = vrs ? rs : 0.f;
       const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
       // 2^{PREL_t - rs} = prey_t * 2^{BL_i - rs} when both factors stay in range (no exp2 per element).
-      const float bli = bl[i];
       // Warp-uniform: the chunk body holds warp-collective TMEM loads and stores, so the whole warp takes the
       // factorised path or none of it does.
-      const bool fact = __all_sync(0xffffffffu, vrs && p.prer[size_t(z) * p.NB + i] <= 120.f && bli - rs <= 120.f);
+      const bool fact = __all_sync(0xffffffffu, vrs && preri <= 120.f && bli - rs <= 120.f);
       const float xfac = fact ? ex2(bli - rs) : 0.f;
       const float2 xf2 = make_float2(xfac, xfac), sv2 = make_float2(sv_, sv_);
       const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
@@ -340,13 +442,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
       // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal
       // two queries are handled per step with packed f32x2 arithmetic.
-      auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
+      auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
         constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
-        float sS[16], sP[16];
-        tmem_ld16(tl + C::COL_S + c0, sS);
-        tmem_ld16(tl + C::COL_P + c0, sP);
-        tmem_ld_wait();
         uint32_t ppk[8], dpk[8];
         if constexpr (DIAG) {
           float gb[16];
@@ -402,21 +500,39 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             dpk[e / 2] = pack_half2(ds.x, ds.y);
           }
         }
-        tmem_st8(tl + C::COL_S + c0, ppk);
-        tmem_st8(tl + C::COL_P + c0, dpk);
+        tmem_st8(tS + c0, ppk);
+        tmem_st8(tP + c0, dpk);
       };
-#pragma unroll 1
-      for (int c0 = cb; c0 < cb + kHalf; c0 += 16) {
-        if (diag)
-          chunk(c0, std::true_type{}, std::false_type{});
-        else if (fact)
-          chunk(c0, std::false_type{}, std::true_type{});
-        else
-          chunk(c0, std::false_type{}, std::false_type{});
-      }
+      // The group's four chunks, ascending, with the TMEM loads of the next chunk in flight during the current one.
+      auto tile = [&](auto diag_tag, auto fact_tag) {
+        float sA[16], pA[16], sB[16], pB[16];
+        tmem_ld16(tS + cb, sA);
+        tmem_ld16(tP + cb, pA);
+        tmem_ld_wait_regs(sA, pA);
+#pragma unroll
+        for (int q = 0; q < kHalf / 16; q += 2) {
+          const int c0 = cb + 16 * q;
+          tmem_ld16(tS + c0 + 16, sB);
+          tmem_ld16(tP + c0 + 16, pB);
+          chunk(c0, sA, pA, diag_tag, fact_tag);
+          tmem_ld_wait_regs(sB, pB);
+          if (q + 2 < kHalf / 16) {
+            tmem_ld16(tS + c0 + 32, sA);
+            tmem_ld16(tP + c0 + 32, pA);
+          }
+          chunk(c0 + 16, sB, pB, diag_tag, fact_tag);
+          if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
+        }
+      };
+      if (diag)
+        tile(std::true_type{}, std::false_type{});
+      else if (fact)
+        tile(std::false_type{}, std::true_type{});
+      else
+        tile(std::false_type{}, std::false_type{});
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full + grp);
+      mbar_arrive(p_full + slot);
       if (!diag) {
         const float fsum = vrs ? fsum2.x + fsum2.y : 0.f;
         if (vrs) wsum += ex2(c2_s - rs) * fsum;
@@ -425,8 +541,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
           const float tot = group_sum<32>(vrs ? ex2(cmid2 - rs) * fsum : 0.f);
           if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + warp] = tot;
         }
-        mid = fminf(mid, bmin[i]);
-        midl = lse2(midl, bl[i]);
+        mid = fminf(mid, bmini);
+        midl = lse2(midl, bli);
       }
     }
     gsum += gsum2.x + gsum2.y;
@@ -488,18 +604,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                 const TcBwdParams p) {
-  using C = TcBwdCfg<D>;
+  using C = TcBwdCfg<D, false>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* a_full = bars;
   uint64_t* st_full = bars + 1;
   uint64_t* st_empty = st_full + C::NS;
-  uint64_t* s_full = st_empty + C::NS;  // [2] one per row group
-  uint64_t* p_full = s_full + 2;        // [2]
-  uint64_t* acc_done = p_full + 2;
+  uint64_t* s_full = st_empty + C::NS;  // [NSLOT] S and dP of the job in the slot are ready
+  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT] the group of the job in the slot has written its P / dS
+  uint64_t* acc_done = p_full + C::NSLOT;
   uint64_t* drain = acc_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* at_full = drain + 1;        // stationary operands written into TMEM by the row threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(at_full + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
   const int warp = threadIdx.x >> 5;
@@ -507,6 +624,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   const int i = p.NB - 1 - int(blockIdx.x) / nbh;  // longest query tiles first
   const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
   const int nsteps = i + 1;                         // key tiles j = i, i-1, ..., 0
+  // Q and dO (stationary) as TMEM operands of S and dP.
+  constexpr int COL_Q = C::COL_X, COL_DO = COL_Q + D / 2;
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
@@ -514,12 +633,13 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(s_full + g, 1);
-      mbar_init(p_full + g, kGroupThreads);
+    for (int x = 0; x < C::NSLOT; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, kGroupThreads);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
+    mbar_init(at_full, kRowThreads);
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -528,8 +648,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const size_t zb = size_t(z) * p.TP;
-  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 56 and the
-  // two row groups take 224 each (128*56 + 256*224 = 384*168).
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
+  // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
   if (warp >= 8) regs_producer();
 
   if (warp == kWarpProducer) {
@@ -538,11 +658,6 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
-      mbar_expect_tx(a_full, 2 * C::TILEB);
-      for (int bx = 0; bx < C::NBOX; ++bx) {
-        tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, a_full);
-        tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b, a_full);
-      }
     }
     __syncwarp();
     bool ok = true;
@@ -563,45 +678,43 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
       __syncwarp();
     }
-    mbar_wait(a_full, 0, p.status, 202);
     for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
       mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 203);
   } else if (warp == kWarpMma) {
-    // Per key tile k and row group g (key columns [64 g, 64 g + 64)): once the group has written dS, dQ += dS K
-    // over its 64 keys, then S and dP of its next tile into the same columns (in issue order, so the read of dS
-    // comes first). While one group waits for these, the other computes.
-    const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
+    // Jobs n = 2 k + g in order (key tile k, row group g = key columns [64 g, 64 g + 64)). S and dP of job n go
+    // into slot n % NSLOT; once the group has written dS there, dQ += dS K over its 64 keys, then the products of
+    // job n + NSLOT into the same slot (in issue order, so the read of dS comes first).
     const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
-    bool ok = mbar_wait(a_full, 0, p.status, 210);
-    if (ok) ok = mbar_wait(st_full + 0, 0, p.status, 211);
-    tc_fence_after();
-    if (ok) {
-      for (int g = 0; g < 2; ++g) {
-        issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + g * kHalf * C::SWB);  // S  = Q K^T
-        issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + g * kHalf * C::SWB);  // dP = dO V^T
-        mma_commit_w(s_full + g);
-      }
-    }
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS;
-      for (int g = 0; g < 2 && ok; ++g) {
-        ok = mbar_wait(p_full + g, k & 1, p.status, 212);
-        if (!ok) break;
+    const int njobs = 2 * nsteps;
+    auto issue_s = [&](int n) {
+      const int g = n & 1, st = (n >> 1) % C::NS;
+      const uint32_t dcol = tmem + (n % C::NSLOT) * 128;
+      issue_ts_k<D>(dcol, tmem + COL_Q, s1 + st * C::TILEB + g * kHalf * C::SWB);           // S  = Q K^T
+      issue_ts_k<D>(dcol + kHalf, tmem + COL_DO, s2 + st * C::TILEB + g * kHalf * C::SWB);  // dP = dO V^T
+      mma_commit_w(s_full + n % C::NSLOT);
+    };
+    bool ok = mbar_wait(at_full, 0, p.status, 210);
+    int loaded = -1;  // streamed tiles known to be in shared memory: 0 .. loaded
+    auto need_tile = [&](int kt) {
+      if (ok && kt > loaded) {
+        ok = mbar_wait(st_full + kt % C::NS, (kt / C::NS) & 1, p.status, 211);
+        loaded = kt;
         tc_fence_after();
-        issue_ts_half<D>(tmem + C::COL_A1, tmem + C::COL_P + g * kHalf, s1 + st * C::TILEB, g, k > 0 || g > 0);
-        if (g == 1) mma_commit_w(st_empty + st);
-        if (k + 1 < nsteps) {
-          const int st1 = (k + 1) % C::NS;
-          if (g == 0) {
-            ok = mbar_wait(st_full + st1, ((k + 1) / C::NS) & 1, p.status, 213);
-            if (!ok) break;
-            tc_fence_after();
-          }
-          issue_ss_half<D>(tmem + C::COL_S + g * kHalf, sa, s1 + st1 * C::TILEB + g * kHalf * C::SWB);
-          issue_ss_half<D>(tmem + C::COL_P + g * kHalf, sb, s2 + st1 * C::TILEB + g * kHalf * C::SWB);
-          mma_commit_w(s_full + g);
-        }
       }
+      return ok;
+    };
+    tc_fence_after();
+    for (int n = 0; n < C::NSLOT && n < njobs; ++n)
+      if (need_tile(n >> 1)) issue_s(n);
+    for (int n = 0; n < njobs && ok; ++n) {
+      const int g = n & 1, k = n >> 1, st = k % C::NS;
+      ok = mbar_wait(p_full + n % C::NSLOT, (n / C::NSLOT) & 1, p.status, 212);
+      if (!ok) break;
+      tc_fence_after();
+      issue_ts_half<D>(tmem + C::COL_A1, tmem + (n % C::NSLOT) * 128 + kHalf, s1 + st * C::TILEB, g, n > 0);
+      if (g == 1) mma_commit_w(st_empty + st);
+      const int m = n + C::NSLOT;
+      if (m < njobs && need_tile(m >> 1)) issue_s(m);
     }
     mma_commit_w(acc_done);
     mma_commit_w(drain);
@@ -614,6 +727,15 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     const int t = i * kBT + r;
     const bool t_ok = t < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
+    {
+      // Group 0 writes the query's row of Q, group 1 its row of dO, into TMEM.
+      const __half* row = grp == 0 ? p.q + b * p.q_s[0] + h * p.q_s[1] + int64_t(t_ok ? t : 0) * p.q_s[2]
+                                   : p.dout + b * p.do_s[0] + h * p.do_s[1] + int64_t(t_ok ? t : 0) * p.do_s[2];
+      row_to_tmem<D>(tl + (grp == 0 ? COL_Q : COL_DO), row, t_ok);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(at_full);
+    }
     const float betal = p.beta[h] * kLog2e;
     const float* own = reinterpret_cast<const float*>(p.qv4 + zb + (t & ~1));  // (-lse, -delta) pair of t
     const float nlse = own[t & 1];   // -inf beyond T
@@ -629,12 +751,26 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     float2 racc2 = make_float2(0.f, 0.f);
     float mid = kInf, midl = -kInf;
     bool ok = true;
+    // Per-tile scalars of key tile j, loaded one tile ahead so their latency hides behind the element work.
+    const float* sufr = p.sufr + size_t(z) * p.NB;
+    float bl_n = bl[i], bmin_n = bmin[i], sufr_n = sufr[i], sufl0_n = p.sufl[zb + size_t(i) * kBT];
     for (int k = 0; k < nsteps && ok; ++k) {
       const int st = k % C::NS, j = i - k;
+      const float blj = bl_n, bminj = bmin_n, sufrj = sufr_n, sufl0 = sufl0_n;
+      if (j > 0) {
+        bl_n = bl[j - 1];
+        bmin_n = bmin[j - 1];
+        sufr_n = sufr[j - 1];
+        sufl0_n = p.sufl[zb + size_t(j - 1) * kBT];
+      }
+      const int n = 2 * k + grp, slot = n % C::NSLOT;
       ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 220);
-      if (ok) ok = mbar_wait(s_full + grp, k & 1, p.status, 221);
+      if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 221);
       if (!ok) break;
       tc_fence_after();
+      // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
+      // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
+      const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
       const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
       const float4* KV = reinterpret_cast<const float4*>(vbase);  // key pairs: (SUF - psi, -psi), (sufy, SUFL)
       const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
@@ -642,10 +778,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       const float cap = fminf(mid, pre_t);
       const float mterm = ex2(midl - c2_t) + bpre;
       // 2^{SUFL_s - c2_t} = sufy_s * 2^{SUFL_first - c2_t} when both factors stay in range.
-      const float sufl0 = p.sufl[zb + size_t(j) * kBT];
       // Warp-uniform (the chunk body holds warp-collective TMEM loads and stores). Rows beyond T take either path.
-      const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (p.sufr[size_t(z) * p.NB + j] <= 120.f &&
-                                                                      sufl0 - c2_t <= 120.f)));
+      const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (sufrj <= 120.f && sufl0 - c2_t <= 120.f)));
       const float yfac = (fact && t_ok) ? ex2(sufl0 - c2_t) : 0.f;
       const float2 cap2 = make_float2(cap, cap), yf2 = make_float2(yfac, yfac), mt2 = make_float2(mterm, mterm);
       const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
@@ -658,13 +792,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       // 16 key columns per chunk: load S and dP, compute dS (fp16) and write it over the first 8 of those 16 dP
       // columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal two keys
       // are handled per step with packed f32x2 arithmetic.
-      auto chunk = [&](int c0, auto diag_tag, auto fact_tag) {
+      auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
         constexpr bool DIAG = decltype(diag_tag)::value;
         constexpr bool FACT = decltype(fact_tag)::value;
-        float sS[16], sP[16];
-        tmem_ld16(tl + C::COL_S + c0, sS);
-        tmem_ld16(tl + C::COL_P + c0, sP);
-        tmem_ld_wait();
         uint32_t dpk[8];
         if constexpr (DIAG) {
 #pragma unroll
@@ -703,23 +833,42 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             dpk[e / 2] = pack_half2(ds.x, ds.y);
           }
         }
-        tmem_st8(tl + C::COL_P + c0, dpk);
+        tmem_st8(tP + c0, dpk);
       };
-#pragma unroll 1
-      for (int c0 = cb + kHalf - 16; c0 >= cb; c0 -= 16) {
-        if (diag)
-          chunk(c0, std::true_type{}, std::false_type{});
-        else if (fact)
-          chunk(c0, std::false_type{}, std::true_type{});
-        else
-          chunk(c0, std::false_type{}, std::false_type{});
-      }
+      // The group's four chunks, descending, with the TMEM loads of the next chunk in flight during the current one.
+      auto tile = [&](auto diag_tag, auto fact_tag) {
+        float sA[16], pA[16], sB[16], pB[16];
+        const int top = cb + kHalf - 16;
+        tmem_ld16(tS + top, sA);
+        tmem_ld16(tP + top, pA);
+        tmem_ld_wait_regs(sA, pA);
+#pragma unroll
+        for (int q = 0; q < kHalf / 16; q += 2) {
+          const int c0 = top - 16 * q;
+          tmem_ld16(tS + c0 - 16, sB);
+          tmem_ld16(tP + c0 - 16, pB);
+          chunk(c0, sA, pA, diag_tag, fact_tag);
+          tmem_ld_wait_regs(sB, pB);
+          if (q + 2 < kHalf / 16) {
+            tmem_ld16(tS + c0 - 32, sA);
+            tmem_ld16(tP + c0 - 32, pA);
+          }
+          chunk(c0 - 16, sB, pB, diag_tag, fact_tag);
+          if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
+        }
+      };
+      if (diag)
+        tile(std::true_type{}, std::false_type{});
+      else if (fact)
+        tile(std::false_type{}, std::true_type{});
+      else
+        tile(std::false_type{}, std::false_type{});
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full + grp);
+      mbar_arrive(p_full + slot);
       if (!diag) {
-        mid = fminf(mid, bmin[j]);
-        midl = lse2(midl, bl[j]);
+        mid = fminf(mid, bminj);
+        midl = lse2(midl, blj);
       }
     }
     const float racc = racc2.x + racc2.y;
@@ -775,7 +924,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
                const Fact& fact, float* gd, const float4* qv4, int* status, cudaStream_t s, std::string* err) {
-  using C = TcBwdCfg<D>;
+  using CK = TcBwdCfg<D, true>;
+  using CQ = TcBwdCfg<D, false>;
   CUtensorMap mq, mk, mv, mdo;
   if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
       !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D) ||
@@ -801,10 +951,18 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.sufy = fact.sufy;
   p.prer = fact.prer;
   p.sufr = fact.sufr;
+  p.q = static_cast<const __half*>(a.q);
+  p.k = static_cast<const __half*>(a.k);
+  p.v = static_cast<const __half*>(a.v);
+  p.dout = static_cast<const __half*>(a.dout);
   p.dq = static_cast<__half*>(a.dq);
   p.dk = static_cast<__half*>(a.dk);
   p.dv = static_cast<__half*>(a.dv);
   for (int q = 0; q < 3; ++q) {
+    p.q_s[q] = a.q_stride[q];
+    p.k_s[q] = a.k_stride[q];
+    p.v_s[q] = a.v_stride[q];
+    p.do_s[q] = a.dout_stride[q];
     p.dq_s[q] = a.dq_stride[q];
     p.dk_s[q] = a.dk_stride[q];
     p.dv_s[q] = a.dv_stride[q];
@@ -826,15 +984,15 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.il2 = kLog2e / a.tau;
   auto kv = tc_bwd_kv_kernel<D>;
   auto qk = tc_bwd_q_kernel<D>;
-  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK::SMEM);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, CQ::SMEM);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
   const int grid = d.NB * d.BH();
   prof_mark(s, "bwd_kv_tc");
-  kv<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
+  kv<<<grid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
     prof_mark(s, "diag_dphi");
@@ -842,7 +1000,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   }
   if (e == cudaSuccess) {
     prof_mark(s, "bwd_q_tc");
-    qk<<<grid, kThreads, C::SMEM, s>>>(mq, mk, mv, mdo, p);
+    qk<<<grid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
