@@ -274,6 +274,63 @@ __global__ void qv_pack_kernel(const float* __restrict__ lse, const float* __res
   qv4[idx + 1] = make_float4(pre[idx], pre[idx + 1], ok0 ? prey[idx] : 1.f, ok1 ? prey[idx + 1] : 1.f);
 }
 
+// delta fused with the pair packing above, for fp16 O and dO with unit innermost stride and 16-byte aligned rows:
+// G = D / 8 lanes per row (16-byte loads) over all BH * TP padded rows (rows beyond T read nothing: delta = 0);
+// rows t and t+1 of a pair sit in adjacent lane groups of one warp, and the even row's first lane writes the pair.
+template <int G>
+__global__ void qv_delta_f16_kernel(const __half* __restrict__ o, Str4 so, const __half* __restrict__ dout, Str4 sdo,
+                                    const float* __restrict__ lse, const float* __restrict__ pre,
+                                    const float* __restrict__ prey, int H, int T, int TP, int rows,
+                                    float4* __restrict__ qv4) {
+  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = gid / G, part = gid % G;
+  const bool in = row < rows;
+  const int z = in ? row / TP : 0, t = in ? row % TP : 0;
+  const bool ok = in && t < T;
+  float acc = 0.f;
+  if (ok) {
+    const int b = z / H, h = z % H;
+    const uint4 a = *reinterpret_cast<const uint4*>(o + b * so.b + h * so.h + int64_t(t) * so.t + part * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(dout + b * sdo.b + h * sdo.h + int64_t(t) * sdo.t + part * 8);
+    const __half2* ah = reinterpret_cast<const __half2*>(&a);
+    const __half2* ch = reinterpret_cast<const __half2*>(&c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 x = __half22float2(ah[q]), y = __half22float2(ch[q]);
+      acc = fmaf(x.x, y.x, acc);
+      acc = fmaf(x.y, y.y, acc);
+    }
+  }
+  acc = group_sum<G>(acc);
+  const float acc1 = __shfl_down_sync(0xffffffffu, acc, G);  // row t + 1
+  if (in && part == 0 && (t & 1) == 0) {
+    const bool ok1 = t + 1 < T;
+    const size_t lz = size_t(z) * T;
+    qv4[row] = make_float4(ok ? -lse[lz + t] : -kInf, ok1 ? -lse[lz + t + 1] : -kInf, ok ? -acc : 0.f,
+                           ok1 ? -acc1 : 0.f);
+    qv4[row + 1] = make_float4(pre[row], pre[row + 1], ok ? prey[row] : 1.f, ok1 ? prey[row + 1] : 1.f);
+  }
+}
+
+bool qv_delta_fusable(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d) {
+  return dtype == FPA_DTYPE_F16 && d.D >= 16 && d.D <= 128 && vec16_ok(o, so) && vec16_ok(dout, sdo);
+}
+
+cudaError_t launch_qv_delta(const void* o, Str4 so, const void* dout, Str4 sdo, const float* lse, const float* pre,
+                            const float* prey, const Dims& d, float4* qv4, cudaStream_t s) {
+  const int rows = d.BH() * d.TP, G = d.D / 8;
+  const int blocks = int((int64_t(rows) * G + 255) / 256);
+  auto a = static_cast<const __half*>(o);
+  auto c = static_cast<const __half*>(dout);
+  switch (G) {
+    case 2: qv_delta_f16_kernel<2><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
+    case 4: qv_delta_f16_kernel<4><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
+    case 8: qv_delta_f16_kernel<8><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
+    default: qv_delta_f16_kernel<16><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
                            float4* qv4, cudaStream_t s) {
   const int n = d.BH() * d.TP;  // TP is a multiple of 128, so pairs never straddle heads
@@ -338,18 +395,23 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     }
   }
   __syncthreads();
-  // part3 partial sums: thread handles query tiles i = U+1+tid, U+1+tid+blockDim, ...
+  // part3 partial sums over the tile pairs (i, j), j < U < i, spread over the threads (fixed assignment); each
+  // pair's total joins its tb_parts partial sums in order.
   float s3 = 0.f;
   if (U > 0 && U < NB - 1) {
     const float cU = cb[U];
-    const int np = sc.tb_parts;
-    for (int i = U + 1 + tid; i < NB; i += blockDim.x) {
-      const float* row = sc.tb + (size_t(z) * NB + i) * NB * np;
-      for (int j = 0; j < U; ++j) {
-        float tbij = 0.f;
-        for (int q = 0; q < np; ++q) tbij += row[j * np + q];
-        s3 += ex2(cU - fmaxf(A[j], Bv[i])) * tbij;
+    const int np = sc.tb_parts, npairs = (NB - 1 - U) * U;
+    for (int pi = tid; pi < npairs; pi += blockDim.x) {
+      const int i = U + 1 + pi / U, j = pi % U;
+      const float* part = sc.tb + ((size_t(z) * NB + i) * NB + j) * np;
+      float tbij = 0.f;
+      if (np == 8) {
+        const float4 u = reinterpret_cast<const float4*>(part)[0], v = reinterpret_cast<const float4*>(part)[1];
+        tbij = (((u.x + u.y) + u.z) + u.w) + (((v.x + v.y) + v.z) + v.w);
+      } else {
+        for (int q = 0; q < np; ++q) tbij += part[q];
       }
+      s3 += ex2(cU - fmaxf(A[j], Bv[i])) * tbij;
     }
   }
   float S = block_sum(s3, red);
@@ -448,18 +510,20 @@ cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, f
   return cudaGetLastError();
 }
 
-// dbeta_h = sum over batch b and key tiles j of the per-tile partials, in a fixed order (kernel.py:450).
+// dbeta_h = sum over batch b and key tiles j of the per-tile partials (kernel.py:450). One warp per head: lane l
+// sums the partials l, l + 32, ... in order, then a fixed shuffle tree joins the lanes (deterministic).
 __global__ void dbeta_kernel(int B, int H, int NB, const float* __restrict__ part, float* __restrict__ dbeta) {
-  int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= H) return;
+  const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (h >= H) return;  // whole warps leave together
+  const int n = B * NB;
   float acc = 0.f;
-  for (int b = 0; b < B; ++b)
-    for (int j = 0; j < NB; ++j) acc += part[(size_t(b) * H + h) * NB + j];
-  dbeta[h] = acc;
+  for (int e = lane; e < n; e += 32) acc += part[(size_t(e / NB) * H + h) * NB + e % NB];
+  acc = group_sum<32>(acc);
+  if (lane == 0) dbeta[h] = acc;
 }
 
 cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s) {
-  dbeta_kernel<<<(d.H + 63) / 64, 64, 0, s>>>(d.B, d.H, d.NB, sc.dbeta, dbeta);
+  dbeta_kernel<<<(d.H + 3) / 4, 128, 0, s>>>(d.B, d.H, d.NB, sc.dbeta, dbeta);
   return cudaGetLastError();
 }
 

@@ -52,6 +52,11 @@ cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, St
                          const float* lse, float* lsep, cudaStream_t s);
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
                            float4* qv4, cudaStream_t s);
+// delta fused with the pair packing (one launch) when O and dO are fp16 with unit innermost stride and 16-byte
+// aligned rows and D <= 128; otherwise launch_delta + launch_qv_pack.
+bool qv_delta_fusable(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d);
+cudaError_t launch_qv_delta(const void* o, Str4 so, const void* dout, Str4 sdo, const float* lse, const float* pre,
+                            const float* prey, const Dims& d, float4* qv4, cudaStream_t s);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
                         const BwdScratch& sc, float* dphi, cudaStream_t s);

@@ -10,12 +10,12 @@
 //                     computes dS (fp16, into its own TMEM columns) and dQ += dS K; also r_t and from it the
 //                     soft-min part with u in the query's tile (DPHI2).
 //
-// Warp roles (384 threads): warps 0-3 and 4-7 are two row groups (thread = TMEM lane); group g owns columns
-// [64 g, 64 g + 64) of every S / dP tile and runs on its own barriers, so the MMA warp serves the groups in turn
-// (its products for one group overlap the other group's element work). Warp 8 is the TMA producer (stationary
-// tiles once, streamed tiles and their per-row vectors through a 2-stage ring), warp 9 the MMA issuer (whole warp,
-// one elected lane issues); warps 10-11 only hand their registers to the row groups (setmaxnreg). Every mbarrier
-// wait is bounded (fpa::sm100::mbar_wait).
+// Warp roles (384 threads): warp 0 issues the MMAs (whole warp, one elected lane issues), warp 1 is the TMA
+// producer (streamed tiles and their per-row vectors through a ring of stages), warps 2-3 only hand their
+// registers to the row groups (setmaxnreg). Warps 4-7 and 8-11 are two row groups (thread = TMEM lane); group g
+// owns columns [64 g, 64 g + 64) of every S / dP tile and runs on its own barriers; S and dP live in TMEM slots
+// that rotate over the jobs (tile, group), so the products of a group's next tile are computed while it works on
+// the current one. Every mbarrier wait is bounded (fpa::sm100::mbar_wait).
 #include <cuda.h>
 
 #include <type_traits>
@@ -30,8 +30,11 @@ namespace {
 
 constexpr int kBT = kTcBT;
 constexpr int kThreads = 384;
-constexpr int kWarpProducer = 8;
-constexpr int kWarpMma = 9;
+// The MMA and producer warps come first: the warp schedulers favour older warps, and these two must issue promptly
+// while the row warps sharing their schedulers are busy.
+constexpr int kWarpMma = 0;
+constexpr int kWarpProducer = 1;
+constexpr int kRowWarp0 = 4;  // row warps 4..11
 constexpr int kRowThreads = 256;    // two row groups of 128
 constexpr int kGroupThreads = 128;
 constexpr int kHalf = kBT / 2;      // columns of one row group
@@ -139,7 +142,7 @@ __device__ __forceinline__ void rows_sync() { asm volatile("bar.sync %0, 256;" :
 // 256 threads call it; the result is returned to every thread.
 __device__ __forceinline__ float rows_sum(float v, float* red) {
   v = group_sum<32>(v);
-  const int w = threadIdx.x >> 5;
+  const int w = (threadIdx.x >> 5) - kRowWarp0;
   if ((threadIdx.x & 31) == 0) red[w] = v;
   rows_sync();
   const float r = ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
@@ -271,7 +274,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   const size_t zb = size_t(z) * p.TP;
   // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
   // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
-  if (warp >= 8) regs_producer();
+  if (warp < kRowWarp0) regs_producer();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -360,9 +363,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 114);
-  } else if (warp < 8) {
+  } else if (warp >= kRowWarp0) {
     regs_rows();
-    const int grp = warp >> 2, wr = warp & 3;
+    const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
     const int r = wr * 32 + lane;  // key within the tile = TMEM lane
     const int cb = grp * kHalf;    // this group's query columns [cb, cb + 64)
     const int s = j * kBT + r;
@@ -539,7 +542,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         if (i > j + 1) {
           // Tile-pair total: one partial per warp (8 per pair), summed in a fixed order by the dphi kernel.
           const float tot = group_sum<32>(vrs ? ex2(cmid2 - rs) * fsum : 0.f);
-          if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + warp] = tot;
+          if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + (warp - kRowWarp0)] = tot;
         }
         mid = fminf(mid, bmini);
         midl = lse2(midl, bli);
@@ -588,7 +591,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       }
     }
     const float db = rows_sum(dbsum, red);
-    if (threadIdx.x == 0) p.dbeta[size_t(z) * p.NB + j] = db;
+    if (threadIdx.x == kRowWarp0 * 32) p.dbeta[size_t(z) * p.NB + j] = db;
   }
   tc_fence_before();
   __syncthreads();
@@ -650,7 +653,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   const size_t zb = size_t(z) * p.TP;
   // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
   // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
-  if (warp >= 8) regs_producer();
+  if (warp < kRowWarp0) regs_producer();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -719,9 +722,9 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 214);
-  } else if (warp < 8) {
+  } else if (warp >= kRowWarp0) {
     regs_rows();
-    const int grp = warp >> 2, wr = warp & 3;
+    const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
     const int r = wr * 32 + (threadIdx.x & 31);  // query within the tile = TMEM lane
     const int cb = grp * kHalf;                  // this group's key columns [cb, cb + 64)
     const int t = i * kBT + r;
@@ -1056,13 +1059,21 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   // Raw key vectors, the factorisation arrays and the padded lse copy (filled by the stats and delta kernels).
   prof_mark(s, "stats");
   cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
-  if (e == cudaSuccess) {
-    prof_mark(s, "delta");
-    e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, nullptr, nullptr, s);
-  }
-  if (e == cudaSuccess) {
-    prof_mark(s, "qv_pack");
-    e = launch_qv_pack(a.lse, sc.delta, st.pre, fact.prey, d, qv4, s);
+  int nprep = 1;
+  if (e == cudaSuccess && qv_delta_fusable(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d)) {
+    prof_mark(s, "qv_delta");
+    e = launch_qv_delta(a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), a.lse, st.pre, fact.prey, d, qv4, s);
+    nprep += 1;
+  } else {
+    if (e == cudaSuccess) {
+      prof_mark(s, "delta");
+      e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, nullptr, nullptr, s);
+    }
+    if (e == cudaSuccess) {
+      prof_mark(s, "qv_pack");
+      e = launch_qv_pack(a.lse, sc.delta, st.pre, fact.prey, d, qv4, s);
+    }
+    nprep += 2;
   }
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward prologue: ") + cudaGetErrorString(e);
@@ -1076,7 +1087,7 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
     case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  if (rc == FPA_OK) *launched = 6;  // stats, delta, qv pack, kv-pass, diagonal dphi, q-pass
+  if (rc == FPA_OK) *launched = nprep + 3;  // stats, delta (+ pack), kv-pass, diagonal dphi, q-pass
   return rc;
 }
 
