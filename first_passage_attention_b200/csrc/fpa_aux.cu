@@ -442,11 +442,14 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
 }
 
 // In-tile soft-min gradient of the diagonal tiles from their stored g (the tensor-core backward writes
-// g_ts = dS_ts [x_ts <= 0] of each diagonal tile to `gd` [BH][NB][128][128], indexed [key s][query t]). For key s:
-//   H(t) = g_ts + (Z_{s,t} / Z_{s,t+1}) H(t+1),  contribution to u = t: (2^{a2_t} / Z_{s,t}) H(t),
-// Z_{s,t} = sum_{s<u<=t} 2^{a2_u} (kernel.py:269-283 evaluates the same sums with scans). Every factor lies in
-// [0, 1]. Thread = key: log2 Z_{s,t} for all t is kept in registers (the forward running sum carries its maximum
-// separately, so its chain is one exp2 and one FMA per step); the contributions are summed per u in a fixed order.
+// g_ts = dS_ts [x_ts <= 0] of each diagonal tile to `gd` [BH][NB][128][128], indexed [key s][query t]). For key s
+// and Z_{s,t} = sum_{s<u<=t} 2^{a2_u} (kernel.py:269-283 evaluates the same sums with scans), with
+// w_t = 2^{a2_t} / Z_{s,t} in (0, 1]:
+//   H(t) = g_ts + (1 - w_{t+1}) H(t+1)    (Z_{s,t} / Z_{s,t+1} = 1 - w_{t+1}),   contribution to u = t: w_t H(t).
+// Thread = key: w_t for all t of the tile stays in registers; the forward pass keeps Z as a scaled sum with its
+// running maximum (one exp2 and one reciprocal per step), the reverse pass needs no transcendental. A warp's keys
+// lie in [32 w, 32 w + 32), so it skips the 32-position blocks before its first key. The contributions are summed
+// per u in a fixed order.
 constexpr int kDiagBT = 128;
 
 __global__ void __launch_bounds__(kDiagBT)
@@ -454,50 +457,78 @@ diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, in
                  float* __restrict__ dphi4) {
   constexpr int BT = kDiagBT, LD = BT + 1;
   extern __shared__ float dsm[];
-  float* G = dsm;          // [BT][BT+1]
+  float* G = dsm;           // [BT][BT+1]
   float* a2 = G + BT * LD;  // [BT]
-  const int j = blockIdx.x, z = blockIdx.y, sl = threadIdx.x;
+  const int j = blockIdx.x, z = blockIdx.y, sl = threadIdx.x, wq = sl >> 5;
   const size_t TP = size_t(NB) * BT;
   const float4* g4 = reinterpret_cast<const float4*>(gd + (size_t(z) * NB + j) * BT * BT);
-  for (int e = sl; e < BT * BT / 4; e += BT) {
-    const float4 v = g4[e];
-    const int row = (4 * e) / BT, col = (4 * e) % BT;
-    G[row * LD + col] = v.x;
-    G[row * LD + col + 1] = v.y;
-    G[row * LD + col + 2] = v.z;
-    G[row * LD + col + 3] = v.w;
+  // All 32 loads of the thread in flight before the first store (the tile is 64 KB).
+  {
+    float4 v[BT * BT / 4 / BT];
+#pragma unroll
+    for (int q = 0; q < BT / 4; ++q) v[q] = g4[sl + q * BT];
+#pragma unroll
+    for (int q = 0; q < BT / 4; ++q) {
+      const int e = sl + q * BT, row = (4 * e) / BT, col = (4 * e) % BT;
+      G[row * LD + col] = v[q].x;
+      G[row * LD + col + 1] = v[q].y;
+      G[row * LD + col + 2] = v[q].z;
+      G[row * LD + col + 3] = v[q].w;
+    }
   }
   const int p0 = j * BT;
   a2[sl] = p0 + sl < T ? -phi[size_t(z) * T + p0 + sl] * il2 : -kInf;
   __syncthreads();
   const int tend = min(BT, T - p0);
-  float L[BT];
+  float w[BT];
+  // Forward: Z_{s,t} = zz 2^{mz} over t = s+1 .. tend-1.
   float mz = -kInf, zz = 0.f;
 #pragma unroll
-  for (int t = 0; t < BT; ++t) {
-    const float at = a2[t];
-    const float d = at - mz;
-    const bool up = d > 0.f;
-    const float e = ex2(-fabsf(d));
-    const float znew = up ? fmaf(zz, e, 1.f) : zz + e;
-    const bool on = t > sl && t < tend;
-    zz = on ? znew : zz;
-    mz = on ? (up ? at : mz) : mz;
-    L[t] = mz + lg2(zz);
-  }
-  float Hh = 0.f;
+  for (int tb = 0; tb < BT / 32; ++tb) {
+    if (tb < wq) continue;  // warp-uniform
 #pragma unroll
-  for (int t = BT - 1; t >= 0; --t) {
-    const bool on = t > sl && t < tend;
-    const float rho = (t + 1 < BT && t + 1 < tend) ? ex2(L[t] - L[t + 1 < BT ? t + 1 : t]) : 0.f;
-    Hh = on ? fmaf(Hh, rho, G[sl * LD + t]) : 0.f;
-    if (on) G[sl * LD + t] = ex2(a2[t] - L[t]) * Hh;
+    for (int i = 0; i < 32; ++i) {
+      const int t = 32 * tb + i;
+      const float at = a2[t];
+      const float d = at - mz;
+      const bool up = d > 0.f;
+      const float e = ex2(-fabsf(d));  // d = +inf on the first term: e = 0
+      const bool on = t > sl && t < tend;
+      const float znew = up ? fmaf(zz, e, 1.f) : zz + e;
+      const float term = up ? 1.f : e;
+      zz = on ? znew : zz;
+      mz = (on && up) ? at : mz;
+      w[t] = on ? term * rcp_approx_f(znew) : 0.f;
+    }
+  }
+  // Reverse: H and the contributions, written over g in place.
+  float Hh = 0.f, wn = 0.f;  // w_{t+1}
+#pragma unroll
+  for (int tb = BT / 32 - 1; tb >= 0; --tb) {
+    if (tb < wq) continue;  // warp-uniform
+#pragma unroll
+    for (int i = 31; i >= 0; --i) {
+      const int t = 32 * tb + i;
+      const bool on = t > sl && t < tend;
+      const float hn = fmaf(1.f - wn, Hh, G[sl * LD + t]);
+      Hh = on ? hn : 0.f;
+      if (on) G[sl * LD + t] = w[t] * Hh;
+      wn = w[t];
+    }
   }
   __syncthreads();
   if (sl < tend) {
-    float acc = 0.f;
-    for (int s2 = 0; s2 < sl; ++s2) acc += G[s2 * LD + sl];
-    dphi4[size_t(z) * TP + p0 + sl] = acc;
+    // Four interleaved partial sums (keys s2 = 0, 1, 2, 3 mod 4), joined in a fixed order.
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int s2 = 0;
+    for (; s2 + 4 <= sl; s2 += 4) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] += G[(s2 + q) * LD + sl];
+    }
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+      if (s2 + q < sl) acc[q] += G[(s2 + q) * LD + sl];
+    dphi4[size_t(z) * TP + p0 + sl] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
 }
 
