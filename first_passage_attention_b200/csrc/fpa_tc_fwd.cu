@@ -7,8 +7,10 @@
 //   warps 4-7  softmax group 1 (query tile i1)
 //   warp  8    TMA producer: Q tiles once, then K, V tiles and the per-key vectors through an NS-stage ring
 //   warp  9    MMA issuer (one thread): S_x = Q_x K^T into TMEM, O_x += P_x V with P_x read from TMEM
-// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D); P_x (fp16, packed two per
-// column) overwrites the first 64 columns of S_x after the softmax has read S_x.
+// TMEM (512 columns): NSLOT slots of 128 columns for S (three for D <= 64, two for D = 128), then O0 and O1 (D
+// each). The jobs (key step k, group x) run in order n = 0, 1, ...; job n uses slot n % NSLOT, so the S of a
+// group's next key tile is computed while it still works on the current one. P (fp16, packed two per column)
+// overwrites the first 64 columns of its slot after the softmax has read S.
 //
 // The bias of query t (tile i) and key s (tile j) in log2 units is b' * min(0, x_ts), b' = beta * log2 e, with
 //   off-diagonal (j < i):  b' min(0, x_ts) = min(b' a_s, b' min(mid_ij, PRE_t) - b' psi_s),  a_s = min(SUF_s - psi_s, 0)
@@ -21,8 +23,9 @@
 //   q_full              producer -> MMA       (TMA bytes)
 //   k_full[s], v_full[s] producer -> MMA, softmax (TMA / bulk bytes)
 //   kv_empty[s]         MMA commit -> producer (stage s free again)
-//   s_full[x]           MMA commit -> softmax x (S_x ready; also implies the previous O_x += P_x V completed)
-//   p_full[x]           softmax x (128 arrivals) -> MMA (P_x in TMEM, O_x corrected)
+//   s_full[slot]        MMA commit -> softmax (S of the slot's job ready)
+//   p_full[slot]        softmax (128 arrivals) -> MMA (P of the slot's job in TMEM, O_x corrected)
+//   o_ready[x]          MMA commit -> softmax x (the group's previous O_x += P V completed: O_x may be rescaled)
 //   o_done[x]           MMA commit -> softmax x (final O_x complete)
 #include <cuda.h>
 
@@ -58,11 +61,13 @@ struct TcFwdCfg {
   static constexpr int OFF_V = OFF_K + NS * TILEB;
   static constexpr int OFF_COL = OFF_V + NS * TILEB;  // per stage: a, psi, phi
   static constexpr int OFF_BAR = OFF_COL + NS * 3 * COLB;
-  static constexpr int NBAR = 1 + 3 * NS + 2 + 2 + 2 + 1;
+  static constexpr int NSLOT = D <= 64 ? 3 : 2;  // TMEM slots for S / P
+  static constexpr int NBAR = 1 + 3 * NS + 2 * NSLOT + 2 + 2 + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot + alignment slack
   static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
   static constexpr uint32_t IDESC_O = idesc_f16(kBT, D, 1);
-  static constexpr int COL_O = 2 * kBT;
+  static constexpr int COL_O = NSLOT * kBT;
+  static_assert(COL_O + 2 * D <= 512, "TMEM columns");
 };
 
 struct TcFwdParams {
@@ -126,9 +131,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + C::NS;
   uint64_t* kv_empty = v_full + C::NS;
-  uint64_t* s_full = kv_empty + C::NS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 2;
+  uint64_t* s_full = kv_empty + C::NS;  // [NSLOT]
+  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT]
+  uint64_t* o_ready = p_full + C::NSLOT;  // [2]
+  uint64_t* o_done = o_ready + 2;        // [2]
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -143,6 +149,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   const int jtop = has1 ? i1 : i0;
   const int nsteps = jtop + 1;
   const int k0 = has1 ? 1 : 0;  // first step in which query tile i0 takes part
+  // Jobs in order: with both tiles (k, x) = (0, 1), (1, 0), (1, 1), (2, 0), ...; with one tile (k, 0).
+  const int njobs = has1 ? 2 * nsteps - 1 : nsteps;
+  auto job_k = [&](int n) { return has1 ? (n + 1) >> 1 : n; };
+  auto job_x = [&](int n) { return has1 ? (n + 1) & 1 : 0; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -151,9 +161,12 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       mbar_init(v_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
+    for (int sl = 0; sl < C::NSLOT; ++sl) {
+      mbar_init(s_full + sl, 1);
+      mbar_init(p_full + sl, 128);
+    }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(s_full + x, 1);
-      mbar_init(p_full + x, 128);
+      mbar_init(o_ready + x, 1);
       mbar_init(o_done + x, 1);
     }
     mbar_init(drain, 1);
@@ -216,72 +229,57 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   } else if (warp == kWarpMma) {
     {  // whole warp, converged: operands stay warp-uniform; one elected lane issues each MMA
       const uint32_t q0 = smem_u32(smem + C::OFF_Q), q1 = q0 + C::TILEB;
-      auto issue_s = [&](int x, int st) {
+      auto issue_s = [&](int n) {  // S of job n into its slot
+        const int x = job_x(n), st = job_k(n) % C::NS;
         const uint32_t qa = x == 0 ? q0 : q1;
         const uint32_t ka = smem_u32(smem + C::OFF_K + st * C::TILEB);
+        const uint32_t dcol = tmem + (n % C::NSLOT) * kBT;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
-          mma_ss_w(tmem + x * kBT, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
-                 C::IDESC_S, kk > 0);
+          mma_ss_w(dcol, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
+                   C::IDESC_S, kk > 0);
         }
+        mma_commit_w(s_full + n % C::NSLOT);
       };
-      auto issue_pv = [&](int x, int st, bool acc) {
+      auto issue_pv = [&](int n, bool acc) {  // O_x += P V of job n
+        const int x = job_x(n), st = job_k(n) % C::NS;
         const uint32_t va = smem_u32(smem + C::OFF_V + st * C::TILEB);
+        const uint32_t acol = tmem + (n % C::NSLOT) * kBT;
 #pragma unroll
         for (int kk = 0; kk < kBT / 16; ++kk) {
-          mma_ts_w(tmem + C::COL_O + x * D, tmem + x * kBT + kk * 8,
-                 smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_O, (acc || kk > 0) ? 1u : 0u);
+          mma_ts_w(tmem + C::COL_O + x * D, acol + kk * 8, smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW),
+                   C::IDESC_O, (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, p.status, 10);
-      if (ok) ok = mbar_wait(k_full + 0, 0, p.status, 11);
+      int kload = -1, vload = -1;  // key steps whose K (V) stage is known to be loaded: up to kload (vload)
+      auto need_k = [&](int kt) {
+        if (ok && kt > kload) {
+          ok = mbar_wait(k_full + kt % C::NS, (kt / C::NS) & 1, p.status, 11);
+          kload = kt;
+          tc_fence_after();
+        }
+        return ok;
+      };
       tc_fence_after();
-      if (ok) {
-        if (k0 == 0) {
-          issue_s(0, 0);
-          mma_commit_w(s_full + 0);
+      for (int n = 0; n < C::NSLOT && n < njobs; ++n)
+        if (need_k(job_k(n))) issue_s(n);
+      for (int n = 0; n < njobs && ok; ++n) {
+        const int k = job_k(n), x = job_x(n), st = k % C::NS;
+        if (k > vload) {
+          ok = mbar_wait(v_full + st, (k / C::NS) & 1, p.status, 12);
+          vload = k;
+          if (!ok) break;
         }
-        if (has1) {
-          issue_s(1, 0);
-          mma_commit_w(s_full + 1);
-        }
-      }
-      int cnt0 = 0, cnt1 = 0;
-      for (int k = 0; k < nsteps && ok; ++k) {
-        const int st = k % C::NS;
-        ok = mbar_wait(v_full + st, (k / C::NS) & 1, p.status, 12);
+        ok = mbar_wait(p_full + n % C::NSLOT, (n / C::NSLOT) & 1, p.status, 13);
         if (!ok) break;
-        const bool more = k + 1 < nsteps;
-        const int st1 = (k + 1) % C::NS;
-        if (k >= k0) {  // query tile i0
-          ok = mbar_wait(p_full + 0, cnt0 & 1, p.status, 13);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(0, st, cnt0 > 0);
-          ++cnt0;
-        }
-        if (more) {
-          ok = mbar_wait(k_full + st1, ((k + 1) / C::NS) & 1, p.status, 14);
-          if (!ok) break;
-          tc_fence_after();
-          if (k + 1 >= k0) {
-            issue_s(0, st1);
-            mma_commit_w(s_full + 0);
-          }
-        }
-        if (has1) {  // query tile i1 takes part in every step
-          ok = mbar_wait(p_full + 1, cnt1 & 1, p.status, 15);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(1, st, cnt1 > 0);
-          ++cnt1;
-        }
-        mma_commit_w(kv_empty + st);
-        if (more && has1) {
-          issue_s(1, st1);
-          mma_commit_w(s_full + 1);
-        }
+        tc_fence_after();
+        issue_pv(n, x == 0 ? k > k0 : k > 0);
+        mma_commit_w(o_ready + x);
+        if (x == 1 || !has1) mma_commit_w(kv_empty + st);  // last job of key step k
+        const int m = n + C::NSLOT;
+        if (m < njobs && need_k(job_k(m))) issue_s(m);
       }
       mma_commit_w(o_done + 0);
       mma_commit_w(o_done + 1);
@@ -298,7 +296,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     const bool active_wg = (x == 0) || has1;
     const int t = i * kBT + r;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
-    const uint32_t col_s = x * kBT, col_o = C::COL_O + x * D;
+    const uint32_t col_o = C::COL_O + x * D;
     const float betal = p.beta[h] * kLog2e;
     const float pre_t = p.pre[size_t(z) * p.TP + t];
     const float* bmin = p.bmin + size_t(z) * p.NB;
@@ -314,8 +312,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       const float2 sc2 = make_float2(p.scale2, p.scale2);
       for (int k = kfirst; k < nsteps && ok; ++k) {
         const int j = jtop - k, st = k % C::NS;
+        const int n = has1 ? 2 * k - 1 + x : k, slot = n % C::NSLOT;  // this group's job at step k
+        const uint32_t col_s = slot * kBT;
         ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 20);
-        if (ok) ok = mbar_wait(s_full + x, cnt & 1, p.status, 21);
+        if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 21);
         if (!ok) break;
         tc_fence_after();
         float s[kBT];
@@ -372,6 +372,12 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           alpha = ex2(mrow - mnew);
           mrow = mnew;
         }
+        // The group's previous O += P V must be complete before O is touched (and before this job's P is handed on).
+        if (cnt > 0) {
+          ok = mbar_wait(o_ready + x, (cnt - 1) & 1, p.status, 23);
+          if (!ok) break;
+          tc_fence_after();
+        }
         if (__any_sync(0xffffffffu, need)) {
           lrow *= alpha;
 #pragma unroll
@@ -402,7 +408,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         lrow += ls.x + ls.y;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(p_full + x);
+        mbar_arrive(p_full + slot);
         ++cnt;
       }
     };
