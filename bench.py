@@ -95,7 +95,7 @@ class ClockSampler:
     REASONS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap", 0x1: "gpu_idle"}
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.002):
         self.index, self.period = index, period
         self.samples, self.reasons = [], set()
         self._stop = threading.Event()
@@ -254,20 +254,50 @@ def main():
             x.grad = None
         first_passage_attention(*leaves, impl="cuda").backward(do)
 
-    # End-to-end: pinned host inputs copied in and all outputs copied out every step.
+    # End-to-end: pinned host inputs copied in and all outputs (o and the six gradients) copied out every step,
+    # through the public API. The step is pipelined over the batch: sequence b's host->device copy, its forward +
+    # backward and its device->host copy run on three streams, so the copies of one sequence overlap the compute
+    # of the next (PCIe is full duplex). dbeta sums the per-sequence parts on the device.
     host_in = [t.cpu().pin_memory() for t in (q, k, v, phi, psi, beta, do)]
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, q, q, q, phi, psi, beta)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dbeta_dev = torch.zeros(Hr, device=device)
 
     def e2e():
-        dev = [t.to(device, non_blocking=True) for t in host_in]
-        xs = [t.requires_grad_() for t in dev[:6]]
-        o = first_passage_attention(*xs, impl="cuda")
-        o.backward(dev[6])
-        outs = [o.detach()] + [x.grad for x in xs]
-        for hst, d in zip(host_out, outs):
-            hst.copy_(d, non_blocking=True)
+        main = torch.cuda.current_stream()
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        with torch.cuda.stream(s_in):
+            beta_d = host_in[5].to(device, non_blocking=True)
+        dbeta_dev.zero_()
+        for bi in range(Br):
+            with torch.cuda.stream(s_in):
+                dev = [host_in[n][bi:bi + 1].to(device, non_blocking=True) for n in (0, 1, 2, 3, 4, 6)]
+                ev_in = torch.cuda.Event()
+                ev_in.record()
+            main.wait_event(ev_in)
+            for t in dev:
+                t.record_stream(main)
+            xs = [t.requires_grad_() for t in dev[:5]] + [beta_d.detach().requires_grad_()]
+            o = first_passage_attention(*xs, impl="cuda")
+            o.backward(dev[5])
+            dbeta_dev.add_(xs[5].grad)
+            outs = [o.detach()] + [x.grad for x in xs[:5]]
+            ev_c = torch.cuda.Event()
+            ev_c.record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_c)
+                for hst, d in zip(host_out[:6], outs):
+                    d.record_stream(s_out)
+                    hst[bi:bi + 1].copy_(d, non_blocking=True)
+        ev_b = torch.cuda.Event()
+        ev_b.record(main)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_b)
+            host_out[6].copy_(dbeta_dev, non_blocking=True)
+        main.wait_stream(s_out)
 
     def sync_all():
         torch.cuda.synchronize()
@@ -290,10 +320,34 @@ def main():
     for _ in range(args.warmup):
         fwd_bwd()
     sync_all()
+    # The device-side step is replayed from a CUDA graph (the library's launches captured once), so the host-side
+    # cost of the Python autograd call does not leave the GPU idle between kernels; eager timing if capture fails.
+    graph, launches_per_step = None, None
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fwd_bwd()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        LaunchStats.reset()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fwd_bwd()
+        launches_per_step = LaunchStats.kernels
+        torch.cuda.synchronize()
+    except Exception as exc:  # keep the benchmark alive with eager timing
+        print(f"# CUDA graph capture failed ({exc}); timing eagerly", file=sys.stderr, flush=True)
+        graph = None
+    step_fn = graph.replay if graph is not None else fwd_bwd
+    for _ in range(args.warmup):
+        step_fn()
+    sync_all()
     LaunchStats.reset()
     with sampler:
-        step_total = max_over_ranks(timed(fwd_bwd, args.steps, 0, flush))
-    launches = LaunchStats.kernels
+        step_total = max_over_ranks(timed(step_fn, args.steps, 0, flush))
+    launches = LaunchStats.kernels if graph is None else launches_per_step * args.steps
     sync_all()
     e2e_total = max_over_ranks(timed(e2e, args.steps, args.warmup, flush))
     sync_all()
@@ -362,6 +416,7 @@ def main():
             "e2e": {"value": f_step * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "step_graph": graph is not None,
             "clocks": sampler.summary(),
             "cpu_baseline": cpu,
         }
