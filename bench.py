@@ -256,46 +256,56 @@ def main():
 
     # End-to-end: pinned host inputs copied in and all outputs (o and the six gradients) copied out every step,
     # through the public API. The step is pipelined over the batch: sequence b's host->device copy, its forward +
-    # backward and its device->host copy run on three streams, so the copies of one sequence overlap the compute
-    # of the next (PCIe is full duplex). dbeta sums the per-sequence parts on the device.
+    # backward and its device->host copy run on separate streams, so the copies of one sequence overlap the compute
+    # of the others (PCIe is full duplex). dbeta sums the per-sequence parts on the device.
     host_in = [t.cpu().pin_memory() for t in (q, k, v, phi, psi, beta, do)]
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, q, q, q, phi, psi, beta)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    dbeta_dev = torch.zeros(Hr, device=device)
+    # Two compute streams take the sequences in turn, so one sequence's kernels (a quarter of the batch fills the
+    # GPU poorly) overlap the next one's.
+    s_comp = [torch.cuda.Stream(device), torch.cuda.Stream(device)]
 
     def e2e():
         main = torch.cuda.current_stream()
-        s_in.wait_stream(main)
-        s_out.wait_stream(main)
+        for st_ in [s_in, s_out] + s_comp:
+            st_.wait_stream(main)
         with torch.cuda.stream(s_in):
             beta_d = host_in[5].to(device, non_blocking=True)
-        dbeta_dev.zero_()
+        dbetas = []
         for bi in range(Br):
+            cs = s_comp[bi % 2]
             with torch.cuda.stream(s_in):
                 dev = [host_in[n][bi:bi + 1].to(device, non_blocking=True) for n in (0, 1, 2, 3, 4, 6)]
                 ev_in = torch.cuda.Event()
                 ev_in.record()
-            main.wait_event(ev_in)
-            for t in dev:
-                t.record_stream(main)
-            xs = [t.requires_grad_() for t in dev[:5]] + [beta_d.detach().requires_grad_()]
-            o = first_passage_attention(*xs, impl="cuda")
-            o.backward(dev[5])
-            dbeta_dev.add_(xs[5].grad)
-            outs = [o.detach()] + [x.grad for x in xs[:5]]
-            ev_c = torch.cuda.Event()
-            ev_c.record(main)
+            cs.wait_event(ev_in)
+            with torch.cuda.stream(cs):
+                for t in dev + [beta_d]:
+                    t.record_stream(cs)
+                xs = [t.requires_grad_() for t in dev[:5]] + [beta_d.detach().requires_grad_()]
+                o = first_passage_attention(*xs, impl="cuda")
+                o.backward(dev[5])
+                dbetas.append(xs[5].grad)
+                outs = [o.detach()] + [x.grad for x in xs[:5]]
+                ev_c = torch.cuda.Event()
+                ev_c.record(cs)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_c)
                 for hst, d in zip(host_out[:6], outs):
                     d.record_stream(s_out)
                     hst[bi:bi + 1].copy_(d, non_blocking=True)
+        for cs in s_comp:
+            main.wait_stream(cs)
+        dbeta_dev = dbetas[0]
+        for g_ in dbetas[1:]:
+            dbeta_dev = dbeta_dev + g_
         ev_b = torch.cuda.Event()
         ev_b.record(main)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_b)
+            dbeta_dev.record_stream(s_out)
             host_out[6].copy_(dbeta_dev, non_blocking=True)
         main.wait_stream(s_out)
 
@@ -349,7 +359,28 @@ def main():
         step_total = max_over_ranks(timed(step_fn, args.steps, 0, flush))
     launches = LaunchStats.kernels if graph is None else launches_per_step * args.steps
     sync_all()
-    e2e_total = max_over_ranks(timed(e2e, args.steps, args.warmup, flush))
+    # The pipelined end-to-end step is host-bound when enqueued eagerly (four API calls per step), so it is also
+    # replayed from a CUDA graph that holds the copies from and to the pinned host buffers, the library's kernels
+    # and the stream fork / join; eager if capture fails.
+    e2e_graph = None
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                e2e()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(e2e_graph):
+            e2e()
+        torch.cuda.synchronize()
+    except Exception as exc:
+        print(f"# CUDA graph capture of the end-to-end step failed ({exc}); timing eagerly", file=sys.stderr,
+              flush=True)
+        e2e_graph = None
+    e2e_total = max_over_ranks(timed(e2e_graph.replay if e2e_graph is not None else e2e, args.steps, args.warmup,
+                                     flush))
     sync_all()
     # Per-kernel device times of the library's launches (CUDA events around each launch, on the call's stream),
     # in a separate pass so the event records stay out of the timed regions above.
@@ -414,7 +445,8 @@ def main():
             "roofline": roof,
             "kernels_us_per_launch": {k: round(v, 2) for k, v in sorted(per_launch_us.items())},
             "e2e": {"value": f_step * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "graph": e2e_graph is not None,
+                    "pipeline": f"{Br} sequences on copy-in / 2 compute / copy-out streams"},
             "gpu_launches": launches,
             "step_graph": graph is not None,
             "clocks": sampler.summary(),

@@ -418,11 +418,43 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
   if (tid == 0) red[0] = S;
   __syncthreads();
   S = red[0];
+  // part1 as an exclusive scan over s of W_s 2^{-c_s} kept as (m, v) = v 2^m with a running maximum m (the
+  // partial sums span any range); then part1_u = v 2^{m + a2_u}, where m + a2_u <= 0 since SUF_s <= phi_u.
+  // Fixed shuffle tree within warps, warp totals joined in order: deterministic.
+  float pm = -kInf, pv = 0.f;
+  if (tid < BT && c2s[tid] > -kInf) {
+    pm = -c2s[tid];
+    pv = Ws[tid];
+  }
+  auto join = [](float m1, float v1, float m2, float v2, float& mo, float& vo) {
+    const float m = fmaxf(m1, m2);
+    mo = m;
+    vo = m == -kInf ? 0.f : v1 * ex2(m1 - m) + v2 * ex2(m2 - m);
+  };
+  const int lane = tid & 31, wq = tid >> 5, nwq = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {  // inclusive scan within the warp
+    const float qm = __shfl_up_sync(0xffffffffu, pm, o), qv = __shfl_up_sync(0xffffffffu, pv, o);
+    if (lane >= o) join(qm, qv, pm, pv, pm, pv);
+  }
+  __syncthreads();
+  if (lane == 31) {
+    red[wq] = pm;
+    red[8 + wq] = pv;
+  }
+  __syncthreads();
+  float bm = -kInf, bv = 0.f;  // total of the warps before this one
+  for (int w = 0; w < wq && w < nwq; ++w) join(bm, bv, red[w], red[8 + w], bm, bv);
+  // exclusive: the inclusive value of the previous lane, joined after the earlier warps' total
+  float em = __shfl_up_sync(0xffffffffu, pm, 1), ev = __shfl_up_sync(0xffffffffu, pv, 1);
+  if (lane == 0) {
+    em = -kInf;
+    ev = 0.f;
+  }
+  join(bm, bv, em, ev, em, ev);
   if (tid < BT && u < T) {
     float a2 = -phi[size_t(z) * T + u] * il2;
-    float part1 = 0.f;
-    for (int s = 0; s < tid; ++s)
-      if (c2s[s] > -kInf) part1 += ex2(a2 - c2s[s]) * Ws[s];
+    const float part1 = em == -kInf ? 0.f : ev * ex2(em + a2);
     float part3 = (U > 0 && U < NB - 1) ? ex2(a2 - cb[U]) * S : 0.f;
     size_t p = size_t(z) * TP + u;
     dphi[size_t(z) * T + u] = beta[h] * (part1 + sc.dphi2[p] + sc.dphi4[p] + part3);

@@ -39,6 +39,7 @@ constexpr int kRowThreads = 256;    // two row groups of 128
 constexpr int kGroupThreads = 128;
 constexpr int kHalf = kBT / 2;      // columns of one row group
 constexpr int kNamedBarRows = 1;    // bar.sync id used by the 256 row threads
+constexpr int kNamedBarDiag = 2;    // bar.sync id used by the 64 threads of warps 2-3 (diagonal soft-min)
 
 // Shared-memory layout of one [128 x D] fp16 tile as TMA writes it: boxes of 128 rows x min(64, D) columns with
 // the swizzle of the box row width.
@@ -76,9 +77,15 @@ struct TcBwdCfg : TileLayout<D> {
   static constexpr int OFF_S2 = OFF_S1 + NS * L::TILEB;  // streamed operand 2 [NS]
   static constexpr int OFF_VEC = OFF_S2 + NS * L::TILEB;  // [NS][VECSTAGE]
   static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
-  static constexpr int OFF_BAR = OFF_RED + (32 + 4 * kBT) * 4;
-  // a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full
-  static constexpr int NBAR = 1 + 2 * NS + 2 * NSLOT + 2 + 1;
+  static constexpr int OFF_G = OFF_RED + (32 + 4 * kBT) * 4;
+  // a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full, g_full
+  static constexpr int NBAR = 1 + 2 * NS + 2 * NSLOT + 2 + 1 + 1;
+  // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions stay in shared memory, where warps
+  // 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
+  static constexpr int GLD = kBT + 1;
+  static constexpr int GBYTES = (kBT * GLD + kBT) * 4;
+  static constexpr bool FUSEDIAG = KV && OFF_G + GBYTES + NBAR * 8 + 16 + 1024 <= 227 * 1024;
+  static constexpr int OFF_BAR = OFF_G + (FUSEDIAG ? GBYTES : 0);
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(KV || AT, "the q-pass keeps Q and dO in TMEM");
@@ -118,7 +125,8 @@ struct TcBwdParams {
   float* w;            // [BH][TP]
   float* tb;           // [BH][NB][NB][kTcTbParts]
   float* dbeta;        // [BH][NB]
-  float* gd;           // [BH][NB][128][128]
+  float* gd;           // [BH][NB][128][128] (when the kv-pass does not run the diagonal soft-min itself)
+  float* dphi4;        // [BH][TP]
   float* dphi2;        // [BH][TP]
   int* status;
   int B, H, T, NB, TP;
@@ -239,7 +247,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   uint64_t* acc_done = p_full + C::NSLOT;
   uint64_t* drain = acc_done + 1;
   uint64_t* at_full = drain + 1;        // stationary operands written into TMEM by the row threads
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(at_full + 1);
+  uint64_t* g_full = at_full + 1;       // the diagonal tile's g is in shared memory (fused diagonal soft-min)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,6 +273,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     mbar_init(at_full, kRowThreads);
+    mbar_init(g_full, kRowThreads);
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -363,6 +373,63 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 114);
+  } else if (C::FUSEDIAG && (warp == 2 || warp == 3)) {
+    // ---- In-tile soft-min of the diagonal tile (DPHI4), concurrent with the row groups. For key s and
+    // Z_{s,t} = sum_{s<u<=t} 2^{a2_u} (kernel.py:269-283 evaluates the same sums with scans), with
+    // w_t = 2^{a2_t} / Z_{s,t} in (0, 1]:
+    //   H(t) = g_ts + (1 - w_{t+1}) H(t+1),  contribution to u = t: w_t H(t)   (Z_{s,t} / Z_{s,t+1} = 1 - w_{t+1}).
+    // g_ts sits at G[s][t] (t >= s); w_t of key s is kept at G[t][s] (below the diagonal, unused by g). Each of
+    // the 64 threads takes keys wt and 127 - wt (equal work), then positions wt and 127 - wt for the column sums.
+    constexpr int LD = C::GLD;
+    float* G = reinterpret_cast<float*>(smem + C::OFF_G);
+    float* a2s = G + kBT * LD;
+    const int wt = threadIdx.x - 64;
+    const int tend = min(kBT, p.T - j * kBT);
+    for (int t = wt; t < kBT; t += 64) a2s[t] = -p.phi[zb + size_t(j) * kBT + t] * p.il2;  // phi = +inf beyond T
+    asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+    bool ok = mbar_wait(g_full, 0, p.status, 130);
+    if (ok) {
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        const int s = q == 0 ? wt : kBT - 1 - wt;
+        float mz = -kInf, zz = 0.f;
+        for (int t = s + 1; t < tend; ++t) {
+          const float at = a2s[t];
+          const float dd = at - mz;
+          const bool up = dd > 0.f;
+          const float e = ex2(-fabsf(dd));
+          zz = up ? fmaf(zz, e, 1.f) : zz + e;
+          mz = up ? at : mz;
+          G[t * LD + s] = (up ? 1.f : e) * rcp_approx(zz);
+        }
+        float H = 0.f, wn = 0.f;
+        for (int t = tend - 1; t > s; --t) {
+          const float w = G[t * LD + s];
+          H = fmaf(1.f - wn, H, G[s * LD + t]);
+          G[s * LD + t] = w * H;
+          wn = w;
+        }
+      }
+    }
+    asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+    if (ok) {
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        const int u = q == 0 ? wt : kBT - 1 - wt;
+        if (u < tend) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};  // keys s = 0, 1, 2, 3 mod 4, joined in a fixed order
+          int s2 = 0;
+          for (; s2 + 4 <= u; s2 += 4) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] += G[(s2 + e) * LD + u];
+          }
+#pragma unroll
+          for (int e = 0; e < 3; ++e)
+            if (s2 + e < u) acc[e] += G[(s2 + e) * LD + u];
+          p.dphi4[zb + size_t(j) * kBT + u] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        }
+      }
+    }
   } else if (warp >= kRowWarp0) {
     regs_rows();
     const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
@@ -441,7 +508,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         for (int c = 0; c < kHalf; ++c)
           if (c > r) rr = fminf(rr, vphi[c]);
       float2 fsum2 = make_float2(0.f, 0.f);
-      float* grow = p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
+      float* grow = C::FUSEDIAG ? nullptr : p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
       // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
       // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal
       // two queries are handled per step with packed f32x2 arithmetic.
@@ -475,9 +542,15 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
             dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
           }
-          float4* dst = reinterpret_cast<float4*>(grow + c0);
+          if constexpr (C::FUSEDIAG) {
+            float* grs = reinterpret_cast<float*>(smem + C::OFF_G) + r * C::GLD + c0;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
+            for (int e = 0; e < 16; ++e) grs[e] = gb[e];
+          } else {
+            float4* dst = reinterpret_cast<float4*>(grow + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 16; e += 2) {
@@ -533,6 +606,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         tile(std::false_type{}, std::true_type{});
       else
         tile(std::false_type{}, std::false_type{});
+      if (C::FUSEDIAG && diag) mbar_arrive(g_full);  // release: the g columns written above
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + slot);
@@ -975,6 +1049,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.tb = sc.tb;
   p.dbeta = sc.dbeta;
   p.gd = gd;
+  p.dphi4 = sc.dphi4;
   p.dphi2 = sc.dphi2;
   p.status = status;
   p.B = d.B;
@@ -997,7 +1072,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   prof_mark(s, "bwd_kv_tc");
   kv<<<grid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
-  if (e == cudaSuccess) {
+  if (e == cudaSuccess && !CK::FUSEDIAG) {
     prof_mark(s, "diag_dphi");
     e = launch_diag_dphi(a.phi, gd, d, a.tau, sc.dphi4, s);
   }
@@ -1015,9 +1090,23 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
 
 }  // namespace
 
+// Whether the kv-pass runs the diagonal soft-min itself (else the stored g goes through diag_dphi_kernel).
+bool kv_fuses_diag(int D) {
+  switch (D) {
+    case 16: return TcBwdCfg<16, true>::FUSEDIAG;
+    case 32: return TcBwdCfg<32, true>::FUSEDIAG;
+    case 64: return TcBwdCfg<64, true>::FUSEDIAG;
+    default: return TcBwdCfg<128, true>::FUSEDIAG;
+  }
+}
+
+size_t gd_bytes(const Dims& d) {
+  return kv_fuses_diag(d.D) ? 0 : align256(size_t(d.BH()) * d.NB * size_t(kBT) * kBT * sizeof(float));
+}
+
 size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
-  return keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * sizeof(float)) +
+  return keycols_bytes(d) + gd_bytes(d) +
          2 * align256(bh * d.TP * sizeof(float4)) + 2 * align256(bh * d.TP * sizeof(float)) +
          2 * align256(bh * d.NB * sizeof(float));
 }
@@ -1042,8 +1131,8 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   }
   const size_t bh = size_t(d.BH());
   KeyCols cols = carve_keycols(extra, d);
-  float* gd = reinterpret_cast<float*>(extra + keycols_bytes(d));
-  char* q = extra + keycols_bytes(d) + align256(bh * d.NB * size_t(kBT) * kBT * 4);
+  float* gd = kv_fuses_diag(d.D) ? nullptr : reinterpret_cast<float*>(extra + keycols_bytes(d));
+  char* q = extra + keycols_bytes(d) + gd_bytes(d);
   float4* qv4 = reinterpret_cast<float4*>(q);
   q += align256(bh * d.TP * sizeof(float4));
   Fact fact;
@@ -1087,7 +1176,7 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
     case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  if (rc == FPA_OK) *launched = nprep + 3;  // stats, delta (+ pack), kv-pass, diagonal dphi, q-pass
+  if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, delta (+ pack), kv, [diag], q
   return rc;
 }
 
