@@ -41,7 +41,100 @@ def parse():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--shape", default="4,12,2048,64", help="B,H,T,D per rank (weak) or in total (strong)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
+    ap.add_argument("--workload", choices=["operator", "lm"], default="operator",
+                    help="operator: configuration 2 (the BASELINE metric); lm: configuration 5, the LM training step")
+    ap.add_argument("--lm-layers", type=int, default=12, help="blocks of the LM (configuration 5: 12)")
+    ap.add_argument("--lm-batch", type=int, default=8, help="sequences per GPU (configuration 5: 8)")
     return ap.parse_args()
+
+
+LM_METRIC = "LM training step tokens/s (GPT-2-small-shaped FPA decoder, T=2048, batch 8/GPU, fp16 autocast)"
+
+
+def lm_main(args, rank, world, local):
+    """Configuration 5: one data-parallel training step of the FPA language model per step (forward, loss,
+    backward with the DDP gradient all-reduce over NCCL, AdamW), tokens/s over all ranks."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    from first_passage_attention_b200 import LaunchStats
+    from first_passage_attention_b200.lm import FPALanguageModel, LMConfig, LMTrainer, make_tokens
+    cfg = LMConfig(n_layers=args.lm_layers)
+    T, Bt = 2048, args.lm_batch
+    torch.manual_seed(0)  # the same initial weights on every rank
+    model = FPALanguageModel(cfg).to(device)
+    trainer = LMTrainer(model)
+    host_tok = make_tokens(Bt, T, cfg.vocab, seed=1000 + rank, device="cpu").pin_memory()
+    host_loss = torch.empty((), dtype=torch.float32, pin_memory=True)
+
+    def step():
+        tok = host_tok.to(device, non_blocking=True)  # the step's inputs from pinned host memory
+        loss = trainer.step(tok)
+        host_loss.copy_(loss, non_blocking=True)      # and its result back
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+    LaunchStats.reset()
+    sampler = ClockSampler(local)
+    evs = []
+    with sampler:
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    launches = LaunchStats.kernels
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    tokens = Bt * T * world
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # The same model and step on the host cores with the reference (dense PyTorch) attention, one sequence of
+        # T=256 (bounded sample), reported in tokens/s.
+        torch.set_num_threads(os.cpu_count())
+        torch.manual_seed(0)
+        cpu_model = FPALanguageModel(cfg, impl="reference")
+        cpu_tr = LMTrainer(cpu_model, ddp=False)
+        tok = make_tokens(1, 256, cfg.vocab, seed=7, device="cpu")
+        cpu_tr.step(tok)
+        t0 = time.time()
+        cpu_tr.step(tok)
+        dt = time.time() - t0
+        cpu = {"value": 256 / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"one sequence of T=256 through the same {cfg.n_layers}-block model with the reference "
+                         f"(dense PyTorch) attention, fp32, one training step, {dt:.1f} s"}
+    if rank == 0:
+        line = {"metric": LM_METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16 (autocast), f32 master weights",
+                "data": "synthetic token ids, random-init weights",
+                "config": {"workload": f"configuration 5: {cfg.n_layers} blocks, d_model {cfg.d_model}, "
+                                       f"{cfg.n_heads} heads, vocab {cfg.vocab}, T {T}, batch {Bt} per GPU",
+                           "params": model.n_params(), "parallelism": f"DDP over {world} GPU(s), NCCL all-reduce",
+                           "l2": "working set (weights, optimizer state, activations) far above L2"},
+                "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": host_tok.numel() * 8,
+                        "d2h_bytes_per_step": 4},
+                "gpu_launches": launches, "clocks": sampler.summary(), "cpu_baseline": cpu,
+                "loss": float(host_loss)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def flops(B, H, T, D, which):
@@ -217,6 +310,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     B, H, T, D = (int(x) for x in args.shape.split(","))
+    if args.workload == "lm":
+        lm_main(args, rank, world, local)
+        return
     if args.impl == "reference":
         reference_arm(args, B, H, T, D, rank, world)
         return
