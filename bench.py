@@ -202,14 +202,20 @@ class ClockSampler:
         except Exception:  # NVML unavailable: report no clocks rather than fail the benchmark
             self._nvml = None
 
+    def sample(self):
+        """One reading (also called from the timing loop while queued GPU work runs)."""
+        if not self._nvml:
+            return
+        try:
+            self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+            r = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            self.reasons.update(n for bit, n in self.REASONS.items() if r & bit)
+        except Exception:
+            pass
+
     def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
-                r = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.reasons.update(n for bit, n in self.REASONS.items() if r & bit)
-            except Exception:
-                pass
+            self.sample()
             time.sleep(self.period)
 
     def __enter__(self):
@@ -230,9 +236,10 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
-def timed(fn, steps, warmup, flush):
+def timed(fn, steps, warmup, flush, during=None):
     """Runs fn warmup times, then `steps` times with an L2 flush (a 256 MiB write) before each; each step is
-    bracketed by CUDA events on the current stream. Returns the summed device time in ms."""
+    bracketed by CUDA events on the current stream. `during` is called while the enqueued steps run on the GPU
+    (clock sampling). Returns the summed device time in ms."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -245,6 +252,8 @@ def timed(fn, steps, warmup, flush):
         fn()
         b.record()
         evs.append((a, b))
+    if during is not None:
+        during()
     torch.cuda.synchronize()
     for a, b in evs:
         total += a.elapsed_time(b)
@@ -363,7 +372,12 @@ def main():
     # GPU poorly) overlap the next one's.
     s_comp = [torch.cuda.Stream(device), torch.cuda.Stream(device)]
 
-    def e2e():
+    host_loss = torch.empty(Br, dtype=torch.float32, pin_memory=True)
+
+    def e2e(copy_all=False):
+        """copy_all=False: the step's result read back is its loss, sum(o * do) per sequence (the configuration's
+        grad_o = ones is the gradient of sum(o)); the gradients stay on the device as in a training step.
+        copy_all=True: o and all six gradients are copied back as well."""
         main = torch.cuda.current_stream()
         for st_ in [s_in, s_out] + s_comp:
             st_.wait_stream(main)
@@ -384,25 +398,30 @@ def main():
                 o = first_passage_attention(*xs, impl="cuda")
                 o.backward(dev[5])
                 dbetas.append(xs[5].grad)
+                loss = (o.detach().float() * dev[5].float()).sum()
                 outs = [o.detach()] + [x.grad for x in xs[:5]]
                 ev_c = torch.cuda.Event()
                 ev_c.record(cs)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_c)
-                for hst, d in zip(host_out[:6], outs):
-                    d.record_stream(s_out)
-                    hst[bi:bi + 1].copy_(d, non_blocking=True)
+                loss.record_stream(s_out)
+                host_loss[bi:bi + 1].copy_(loss.reshape(1), non_blocking=True)
+                if copy_all:
+                    for hst, d in zip(host_out[:6], outs):
+                        d.record_stream(s_out)
+                        hst[bi:bi + 1].copy_(d, non_blocking=True)
         for cs in s_comp:
             main.wait_stream(cs)
         dbeta_dev = dbetas[0]
         for g_ in dbetas[1:]:
             dbeta_dev = dbeta_dev + g_
-        ev_b = torch.cuda.Event()
-        ev_b.record(main)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_b)
-            dbeta_dev.record_stream(s_out)
-            host_out[6].copy_(dbeta_dev, non_blocking=True)
+        if copy_all:
+            ev_b = torch.cuda.Event()
+            ev_b.record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_b)
+                dbeta_dev.record_stream(s_out)
+                host_out[6].copy_(dbeta_dev, non_blocking=True)
         main.wait_stream(s_out)
 
     def sync_all():
@@ -451,32 +470,45 @@ def main():
         step_fn()
     sync_all()
     LaunchStats.reset()
+    def clock_samples():  # the GPU is busy with the queued steps (about 10 ms) while these run
+        for _ in range(4):
+            sampler.sample()
+            time.sleep(0.001)
+
     with sampler:
-        step_total = max_over_ranks(timed(step_fn, args.steps, 0, flush))
+        step_total = max_over_ranks(timed(step_fn, args.steps, 0, flush, during=clock_samples))
     launches = LaunchStats.kernels if graph is None else launches_per_step * args.steps
     sync_all()
     # The pipelined end-to-end step is host-bound when enqueued eagerly (four API calls per step), so it is also
     # replayed from a CUDA graph that holds the copies from and to the pinned host buffers, the library's kernels
     # and the stream fork / join; eager if capture fails.
-    e2e_graph = None
-    try:
-        side = torch.cuda.Stream(device)
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                e2e()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        e2e_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(e2e_graph):
-            e2e()
-        torch.cuda.synchronize()
-    except Exception as exc:
-        print(f"# CUDA graph capture of the end-to-end step failed ({exc}); timing eagerly", file=sys.stderr,
-              flush=True)
-        e2e_graph = None
+    def capture(fn):
+        try:
+            side = torch.cuda.Stream(device)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            torch.cuda.synchronize()
+            return g
+        except Exception as exc:
+            print(f"# CUDA graph capture of the end-to-end step failed ({exc}); timing eagerly", file=sys.stderr,
+                  flush=True)
+            return None
+
+    e2e_graph = capture(e2e)
     e2e_total = max_over_ranks(timed(e2e_graph.replay if e2e_graph is not None else e2e, args.steps, args.warmup,
                                      flush))
+    sync_all()
+    e2e_all = lambda: e2e(copy_all=True)  # noqa: E731
+    e2e_all_graph = capture(e2e_all)
+    e2e_all_total = max_over_ranks(timed(e2e_all_graph.replay if e2e_all_graph is not None else e2e_all, args.steps,
+                                         args.warmup, flush))
     sync_all()
     # Per-kernel device times of the library's launches (CUDA events around each launch, on the call's stream),
     # in a separate pass so the event records stay out of the timed regions above.
@@ -492,7 +524,7 @@ def main():
     kernels = _lib.profile_report()
 
     K = args.steps
-    fwd_ms, step_ms, e2e_ms = fwd_total / K, step_total / K, e2e_total / K
+    fwd_ms, step_ms, e2e_ms, e2e_all_ms = fwd_total / K, step_total / K, e2e_total / K, e2e_all_total / K
     f_fwd, f_step = flops(Br, Hr, T, D, "fwd"), flops(Br, Hr, T, D, "fwd_bwd")
     peak, peak_src = load_peak()
     job_step = f_step * world / (step_ms * 1e-3) / 1e12
@@ -541,8 +573,12 @@ def main():
             "roofline": roof,
             "kernels_us_per_launch": {k: round(v, 2) for k, v in sorted(per_launch_us.items())},
             "e2e": {"value": f_step * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "graph": e2e_graph is not None,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * Br, "graph": e2e_graph is not None,
+                    "result_read_back": "the loss sum(o * grad_o) of each sequence; gradients stay on the device",
                     "pipeline": f"{Br} sequences on copy-in / 2 compute / copy-out streams"},
+            "e2e_all_outputs": {"value": f_step * world / (e2e_all_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                "ms_per_step": e2e_all_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                                "graph": e2e_all_graph is not None},
             "gpu_launches": launches,
             "step_graph": graph is not None,
             "clocks": sampler.summary(),
