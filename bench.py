@@ -30,6 +30,9 @@ METRIC = "fwd / fwd+bwd ms & TFLOP/s at 4x12x2048x64 fp16 (% tensor peak), 1-8 G
 PUBLISHED_FWD_BWD_TFLOPS = 20.6   # README.md:57 of the reference: 4.38 ms fwd+bwd on sm_75 = 90.19 GFLOP / 4.38 ms
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per launch at configuration 2 per GPU from one ncu capture of this build
+# (profiles/tc_kernels_config2_full.md); reported as roofline.traffic for the dominant kernel.
+NCU_TRAFFIC_C2 = {"bwd_kv_tc": (54.4 + 3.3) * 1e6, "bwd_q_tc": (54.8 + 1.7) * 1e6, "fwd_tc": (39.4 + 0.13) * 1e6}
 
 
 def parse():
@@ -544,7 +547,9 @@ def main():
     if dom in algo:
         ach = algo[dom] / (per_launch_us[dom] * 1e-6) / 1e12
         roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                "frac": ach / peak, "peak_source": peak_src, "traffic": None,
+                "frac": ach / peak, "peak_source": peak_src,
+                "traffic": NCU_TRAFFIC_C2.get(dom) if (Br, Hr, T, D) == (4, 12, 2048, 64) else None,
+                "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                 "share_of_step": kernels[dom][1] / max(1e-9, sum(ms for (n, ms) in kernels.values()))}
     else:
         roof = {"bound": "tensor", "kernel": "forward pass (field statistics + attention forward)",
