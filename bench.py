@@ -51,6 +51,20 @@ def parse():
     return ap.parse_args()
 
 
+# Named configurations of the reference's benchmarks, per GPU (B, H, T, D); the published number applies to 2 only.
+NAMED_SHAPES = {(4, 12, 2048, 64): "configuration 2", (1, 16, 16383, 128): "configuration 4"}
+
+
+def shape_label(B, H, T, D):
+    return NAMED_SHAPES.get((B, H, T, D), "custom shape")
+
+
+def metric_for(B, H, T, D):
+    if (B, H, T, D) == (4, 12, 2048, 64):
+        return METRIC
+    return f"fwd / fwd+bwd ms & TFLOP/s at {B}x{H}x{T}x{D} fp16 (% tensor peak), 1-8 GPU"
+
+
 LM_METRIC = "LM training step tokens/s (GPT-2-small-shaped FPA decoder, T=2048, batch 8/GPU, fp16 autocast)"
 
 
@@ -306,10 +320,11 @@ def reference_arm(args, B, H, T, D, rank, world):
     ms = 1e3 * sum(times) / len(times)
     val = flops(1, 1, Ts, D, "fwd_bwd") / (ms * 1e-3) / 1e12
     sample = f"one (b,h) head of B{B} H{H} T{T} D{D}, prefix T={Ts}, fwd+bwd, float64 NumPy oracle"
-    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": metric_for(B, H, T, D), "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"configuration 2 (B{B} H{H} T{T} D{D} fp16) fwd+bwd, sampled", "B": B, "H": H,
+            "config": {"workload": f"{shape_label(B, H, T, D)} (B{B} H{H} T{T} D{D} fp16) fwd+bwd, sampled",
+                       "B": B, "H": H,
                        "T": T, "D": D},
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -566,10 +581,13 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": job_step, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "metric": metric_for(B, H, T, D), "value": job_step, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": args.scaling,
-            "vs_baseline": job_step / PUBLISHED_FWD_BWD_TFLOPS, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"configuration 2: B{Br} H{Hr} T{T} D{D} fp16 fwd+bwd per GPU ({args.scaling})",
+            "vs_baseline": (job_step / PUBLISHED_FWD_BWD_TFLOPS
+                            if shape_label(B, H, T, D) == "configuration 2" else None),
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"{shape_label(B, H, T, D)}: B{Br} H{Hr} T{T} D{D} fp16 fwd+bwd per GPU "
+                                   f"({args.scaling})",
                        "global_heads": Br * Hr * world, "T": T, "D": D, "accumulate": "f32",
                        "parallelism": f"heads sharded over {world} GPU(s), no collective",
                        "l2": "flushed before every timed step (256 MiB write, outside the events)"},
