@@ -389,25 +389,52 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
     bool ok = mbar_wait(g_full, 0, p.status, 130);
     if (ok) {
+      // Both recurrences run in blocks of kRun positions: the block's shared-memory operands are loaded into
+      // registers first, so only the FMA/select chain is serial (the exponentials and reciprocals of a block
+      // overlap). Positions past the end of the chain load neutral values (a2 = -inf: e = 0, zz unchanged) and
+      // store nothing.
+      constexpr int kRun = 8;
 #pragma unroll 1
       for (int q = 0; q < 2; ++q) {
         const int s = q == 0 ? wt : kBT - 1 - wt;
         float mz = -kInf, zz = 0.f;
-        for (int t = s + 1; t < tend; ++t) {
-          const float at = a2s[t];
-          const float dd = at - mz;
-          const bool up = dd > 0.f;
-          const float e = ex2(-fabsf(dd));
-          zz = up ? fmaf(zz, e, 1.f) : zz + e;
-          mz = up ? at : mz;
-          G[t * LD + s] = (up ? 1.f : e) * rcp_approx(zz);
+#pragma unroll 1
+        for (int t0 = s + 1; t0 < tend; t0 += kRun) {
+          float at[kRun], wv[kRun];
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) at[e] = t0 + e < tend ? a2s[t0 + e] : -kInf;
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            const float dd = at[e] - mz;
+            const bool up = dd > 0.f;
+            const float ee = ex2(-fabsf(dd));
+            zz = up ? fmaf(zz, ee, 1.f) : zz + ee;
+            mz = up ? at[e] : mz;
+            wv[e] = (up ? 1.f : ee) * rcp_approx(zz);
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e)
+            if (t0 + e < tend) G[(t0 + e) * LD + s] = wv[e];
         }
         float H = 0.f, wn = 0.f;
-        for (int t = tend - 1; t > s; --t) {
-          const float w = G[t * LD + s];
-          H = fmaf(1.f - wn, H, G[s * LD + t]);
-          G[s * LD + t] = w * H;
-          wn = w;
+#pragma unroll 1
+        for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
+          float w[kRun], g[kRun];
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            const bool in = t1 - e > s;
+            w[e] = in ? G[(t1 - e) * LD + s] : 0.f;
+            g[e] = in ? G[s * LD + t1 - e] : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            H = fmaf(1.f - wn, H, g[e]);
+            g[e] = w[e] * H;
+            wn = w[e];
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e)
+            if (t1 - e > s) G[s * LD + t1 - e] = g[e];
         }
       }
     }
@@ -949,6 +976,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
     }
     const float racc = racc2.x + racc2.y;
+    const float a2_t = t_ok ? -p.phi[zb + t] * p.il2 : 0.f;  // for DPHI2 below; loaded while dQ drains
     if (ok) ok = mbar_wait(acc_done, 0, p.status, 222);
     if (ok) {
       tc_fence_after();
@@ -971,7 +999,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
     }
     // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile); r_t joins the two
-    // groups' partial sums in a fixed order.
+    // groups' partial sums in a fixed order. The two groups split each position's range of t in halves (group 0
+    // the lower one), each with four accumulators joined in a fixed order.
     float* rx = red + 32;
     float* rsh = red + 32 + kBT;
     float* csh = red + 32 + 2 * kBT;
@@ -982,13 +1011,25 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       csh[r] = c2_t;
     }
     rows_sync();
-    if (grp == 0 && t_ok) {
+    float p2 = 0.f;
+    if (t_ok) {
       const int tend = min(kBT, p.T - i * kBT);
-      const float a2 = -p.phi[zb + t] * p.il2;
-      float p2 = 0.f;
-      for (int t2 = r; t2 < tend; ++t2) p2 += ex2(a2 - csh[t2]) * rsh[t2];
-      p.dphi2[zb + t] = p2;
+      const int mid = r + ((tend - r + 1) >> 1);
+      const int lo = grp == 0 ? r : mid, hi = grp == 0 ? mid : tend;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      int t2 = lo;
+      for (; t2 + 4 <= hi; t2 += 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = fmaf(ex2(a2_t - csh[t2 + e]), rsh[t2 + e], acc[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 3; ++e)
+        if (t2 + e < hi) acc[e] = fmaf(ex2(a2_t - csh[t2 + e]), rsh[t2 + e], acc[e]);
+      p2 = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
+    if (grp == 1) rx[r] = p2;
+    rows_sync();
+    if (grp == 0 && t_ok) p.dphi2[zb + t] = p2 + rx[r];
   }
   tc_fence_before();
   __syncthreads();
