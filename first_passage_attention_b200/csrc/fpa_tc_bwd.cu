@@ -80,10 +80,10 @@ struct TcBwdCfg : TileLayout<D> {
   static constexpr int OFF_G = OFF_RED + (32 + 4 * kBT) * 4;
   // a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full, g_full
   static constexpr int NBAR = 1 + 2 * NS + 2 * NSLOT + 2 + 1 + 1;
-  // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions stay in shared memory, where warps
-  // 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
+  // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions (with 2^{a2 - max}) stay in shared
+  // memory, where warps 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
   static constexpr int GLD = kBT + 1;
-  static constexpr int GBYTES = (kBT * GLD + kBT) * 4;
+  static constexpr int GBYTES = (kBT * GLD + 2 * kBT + 4) * 4;  // g, a2, 2^{a2 - M}, max / min
   static constexpr bool FUSEDIAG = KV && OFF_G + GBYTES + NBAR * 8 + 16 + 1024 <= 227 * 1024;
   static constexpr int OFF_BAR = OFF_G + (FUSEDIAG ? GBYTES : 0);
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
@@ -374,26 +374,97 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 114);
   } else if (C::FUSEDIAG && (warp == 2 || warp == 3)) {
-    // ---- In-tile soft-min of the diagonal tile (DPHI4), concurrent with the row groups. For key s and
-    // Z_{s,t} = sum_{s<u<=t} 2^{a2_u} (kernel.py:269-283 evaluates the same sums with scans), with
-    // w_t = 2^{a2_t} / Z_{s,t} in (0, 1]:
-    //   H(t) = g_ts + (1 - w_{t+1}) H(t+1),  contribution to u = t: w_t H(t)   (Z_{s,t} / Z_{s,t+1} = 1 - w_{t+1}).
-    // g_ts sits at G[s][t] (t >= s); w_t of key s is kept at G[t][s] (below the diagonal, unused by g). Each of
-    // the 64 threads takes keys wt and 127 - wt (equal work), then positions wt and 127 - wt for the column sums.
+    // ---- In-tile soft-min of the diagonal tile (DPHI4), concurrent with the row groups (kernel.py:269-283
+    // evaluates the same sums with scans). For key s, Z_{s,t} = sum_{s<u<=t} 2^{a2_u}, and g_ts at G[s][t]
+    // (t > s), the contribution to position u is
+    //   2^{a2_u} K_s(u),  K_s(u) = sum_{t>=u} g_ts / Z_{s,t}.
+    // Fast path, when the tile's a2 spans at most kSpan: with E_u = 2^{a2_u - M} (M the tile maximum, so
+    // E_u >= 2^-kSpan stays a normal float), S_{s,t} = Z_{s,t} 2^-M is a running sum, one reciprocal per pair
+    // gives R_ts = g_ts / S_{s,t} (in place of g), a suffix sum along t gives K (in place of R), and the column sums
+    // times E_u give DPHI4_u. Every term E_u g_ts / S_{s,t} is at most |g_ts| (u lies in the window).
+    // Otherwise the running-maximum form: w_t = 2^{a2_t} / Z_{s,t} in (0, 1] and
+    //   H(t) = g_ts + (1 - w_{t+1}) H(t+1),  contribution to u = t: w_t H(t)   (Z_{s,t} / Z_{s,t+1} = 1 - w_{t+1}),
+    // with w_t of key s kept at G[t][s] (below the diagonal, unused by g).
+    // Each of the 64 threads takes keys wt and 127 - wt (equal work), then positions wt and 127 - wt for the column
+    // sums. Both passes run in blocks of kRun positions whose shared-memory operands are loaded into registers
+    // first, so only the add/FMA chain is serial; positions past the end of a chain load neutral values and store
+    // nothing.
     constexpr int LD = C::GLD;
+    constexpr int kRun = 8;
+    constexpr float kSpan = 64.f;
     float* G = reinterpret_cast<float*>(smem + C::OFF_G);
     float* a2s = G + kBT * LD;
+    float* es = a2s + kBT;
+    float* mm = es + kBT;  // per-warp maximum and minimum of a2 over the tile's positions
     const int wt = threadIdx.x - 64;
     const int tend = min(kBT, p.T - j * kBT);
-    for (int t = wt; t < kBT; t += 64) a2s[t] = -p.phi[zb + size_t(j) * kBT + t] * p.il2;  // phi = +inf beyond T
+    float vmax = -kInf, vmin = kInf;
+    for (int t = wt; t < kBT; t += 64) {
+      const float a = -p.phi[zb + size_t(j) * kBT + t] * p.il2;  // phi = +inf beyond T
+      a2s[t] = a;
+      if (t < tend) {
+        vmax = fmaxf(vmax, a);
+        vmin = fminf(vmin, a);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+      vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
+    }
+    if (lane == 0) {
+      mm[2 * (warp - 2)] = vmax;
+      mm[2 * (warp - 2) + 1] = vmin;
+    }
     asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+    const float M = fmaxf(mm[0], mm[2]);
+    const bool fast = M - fminf(mm[1], mm[3]) <= kSpan;  // the same for all 64 threads
+    if (fast) {
+      for (int t = wt; t < kBT; t += 64) es[t] = t < tend ? ex2(a2s[t] - M) : 0.f;
+      asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+    }
     bool ok = mbar_wait(g_full, 0, p.status, 130);
-    if (ok) {
-      // Both recurrences run in blocks of kRun positions: the block's shared-memory operands are loaded into
-      // registers first, so only the FMA/select chain is serial (the exponentials and reciprocals of a block
-      // overlap). Positions past the end of the chain load neutral values (a2 = -inf: e = 0, zz unchanged) and
-      // store nothing.
-      constexpr int kRun = 8;
+    if (ok && fast) {
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        const int s = q == 0 ? wt : kBT - 1 - wt;
+        float* row = G + s * LD;
+        float S = 0.f;
+#pragma unroll 1
+        for (int t0 = s + 1; t0 < tend; t0 += kRun) {
+          float ev[kRun], gv[kRun];
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            const bool in = t0 + e < tend;
+            ev[e] = in ? es[t0 + e] : 0.f;
+            gv[e] = in ? row[t0 + e] : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            S += ev[e];
+            gv[e] *= rcp_approx(S);
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e)
+            if (t0 + e < tend) row[t0 + e] = gv[e];
+        }
+        float K = 0.f;
+#pragma unroll 1
+        for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
+          float rv[kRun];
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) rv[e] = t1 - e > s ? row[t1 - e] : 0.f;
+#pragma unroll
+          for (int e = 0; e < kRun; ++e) {
+            K += rv[e];
+            rv[e] = K;
+          }
+#pragma unroll
+          for (int e = 0; e < kRun; ++e)
+            if (t1 - e > s) row[t1 - e] = rv[e];
+        }
+      }
+    } else if (ok) {
 #pragma unroll 1
       for (int q = 0; q < 2; ++q) {
         const int s = q == 0 ? wt : kBT - 1 - wt;
@@ -408,8 +479,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             const float dd = at[e] - mz;
             const bool up = dd > 0.f;
             const float ee = ex2(-fabsf(dd));
-            zz = up ? fmaf(zz, ee, 1.f) : zz + ee;
-            mz = up ? at[e] : mz;
+            zz = fmaf(zz, up ? ee : 1.f, up ? 1.f : ee);
+            mz = fmaxf(mz, at[e]);
             wv[e] = (up ? 1.f : ee) * rcp_approx(zz);
           }
 #pragma unroll
@@ -453,7 +524,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 #pragma unroll
           for (int e = 0; e < 3; ++e)
             if (s2 + e < u) acc[e] += G[(s2 + e) * LD + u];
-          p.dphi4[zb + size_t(j) * kBT + u] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          const float col = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          p.dphi4[zb + size_t(j) * kBT + u] = fast ? es[u] * col : col;
         }
       }
     }
