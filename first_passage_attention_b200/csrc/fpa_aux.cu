@@ -67,7 +67,10 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.y;
-  if (j == 0 && z == 0 && tid == 0 && status) *status = 0;
+  if (j == 0 && z == 0 && tid == 0) {
+    if (status) *status = 0;
+    if (fact.sched) fact.sched[0] = fact.sched[1] = 0;
+  }
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
   const float p = t < T ? phi[size_t(z) * T + t] : kInf;
@@ -165,7 +168,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
                          const Fact* fact) {
-  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
+  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
                                                    cols_scaled, beta, d.H, f, status);
   return cudaGetLastError();

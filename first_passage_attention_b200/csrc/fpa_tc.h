@@ -14,6 +14,9 @@ constexpr int kTcTbParts = 8;  // per-warp partial sums of each tile-pair total 
 
 bool tc_supports(int D);
 
+// Streaming multiprocessors of the current device (the grid of the persistent kernels).
+int sm_count();
+
 // True if a [B, H, T, D] fp16 operand with these element strides can be read by TMA as it is (innermost stride 1,
 // 16-byte aligned base and strides).
 bool tma_layout_ok(const void* p, const int64_t st[4]);

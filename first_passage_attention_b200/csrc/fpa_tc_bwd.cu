@@ -6,9 +6,10 @@
 //                     TMEM over S^T and dP^T), then dV += P^T dO and dK += dS^T Q on the tensor cores. Also dpsi,
 //                     the dbeta partial, the soft-min sums W (u in the key's tile) and TB (u strictly between the
 //                     tiles), and g of the diagonal tile (stored for diag_dphi_kernel).
-//   tc_bwd_q_kernel   one CTA per query tile i, key tiles j = i .. 0: S = Q K^T, dP = dO V^T; thread = query
-//                     computes dS (fp16, into its own TMEM columns) and dQ += dS K; also r_t and from it the
-//                     soft-min part with u in the query's tile (DPHI2).
+//   tc_bwd_q_kernel   persistent, one CTA per SM taking query tiles i of one head as work units; per unit, key
+//                     tiles j = i .. 0: S = Q K^T, dP = dO V^T; thread = query computes dS (fp16, into its own TMEM
+//                     columns) and dQ += dS K; also r_t and from it the soft-min part with u in the query's tile
+//                     (DPHI2).
 //
 // Warp roles (384 threads): warp 0 issues the MMAs (whole warp, one elected lane issues), warp 1 is the TMA
 // producer (streamed tiles and their per-row vectors through a ring of stages), warps 2-3 only hand their
@@ -40,6 +41,7 @@ constexpr int kGroupThreads = 128;
 constexpr int kHalf = kBT / 2;      // columns of one row group
 constexpr int kNamedBarRows = 1;    // bar.sync id used by the 256 row threads
 constexpr int kNamedBarDiag = 2;    // bar.sync id used by the 64 threads of warps 2-3 (diagonal soft-min)
+constexpr int kUQ = 4;              // persistent passes: depth of the ring of work-unit ids
 
 // Shared-memory layout of one [128 x D] fp16 tile as TMA writes it: boxes of 128 rows x min(64, D) columns with
 // the swizzle of the box row width.
@@ -75,18 +77,21 @@ struct TcBwdCfg : TileLayout<D> {
   static constexpr int OFF_B = L::TILEB;                // stationary operand 2 (when !AT)
   static constexpr int OFF_S1 = NSTAT * L::TILEB;       // streamed operand 1 [NS]
   static constexpr int OFF_S2 = OFF_S1 + NS * L::TILEB;  // streamed operand 2 [NS]
-  static constexpr int OFF_VEC = OFF_S2 + NS * L::TILEB;  // [NS][VECSTAGE]
+  static constexpr int OFF_X = OFF_S2 + NS * L::TILEB;   // q-pass: the next unit's Q and dO tiles (TMA staging)
+  static constexpr int OFF_VEC = OFF_X + (KV ? 0 : 2 * L::TILEB);  // [NS][VECSTAGE]
   static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
   static constexpr int OFF_G = OFF_RED + (32 + 4 * kBT) * 4;
-  // a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full, g_full
-  static constexpr int NBAR = 1 + 2 * NS + 2 * NSLOT + 2 + 1 + 1;
+  // kv: a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full, g_full;
+  // q: st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, acc_free, drain, at_full, x_full,
+  // x_empty, u_full[kUQ], u_empty[kUQ]
+  static constexpr int NBAR = 2 * NS + 2 * NSLOT + 6 + 2 * kUQ;
   // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions (with 2^{a2 - max}) stay in shared
   // memory, where warps 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
   static constexpr int GLD = kBT + 1;
   static constexpr int GBYTES = (kBT * GLD + 2 * kBT + 4) * 4;  // g, a2, 2^{a2 - M}, max / min
-  static constexpr bool FUSEDIAG = KV && OFF_G + GBYTES + NBAR * 8 + 16 + 1024 <= 227 * 1024;
+  static constexpr bool FUSEDIAG = KV && OFF_G + GBYTES + NBAR * 8 + 64 + 1024 <= 227 * 1024;
   static constexpr int OFF_BAR = OFF_G + (FUSEDIAG ? GBYTES : 0);
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;  // + the TMEM address and the unit ring
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(KV || AT, "the q-pass keeps Q and dO in TMEM");
 };
@@ -129,6 +134,7 @@ struct TcBwdParams {
   float* dphi4;        // [BH][TP]
   float* dphi2;        // [BH][TP]
   int* status;
+  int* sched;          // [2] work-unit counters (kv-pass, q-pass), zero before the launch
   int B, H, T, NB, TP;
   float scale, scale2, il2;
 };
@@ -775,6 +781,50 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 }
 
 // ------------------------------------------------------------------------------------------------- q-pass ----
+// Persistent: one CTA per SM takes work units (query tile i of one head; longest first) from a counter in the
+// workspace until none is left. The producer stages each unit's Q and dO tiles by TMA while the previous unit runs;
+// at a unit boundary the row threads read dQ out of TMEM, copy the next unit's Q and dO rows from the staging buffer
+// into TMEM, and only then store dQ and DPHI2 of the finished unit, so the next unit's first products are computed
+// meanwhile. Jobs, tiles and units are numbered across units, which sets every slot, stage and barrier phase.
+template <int D>
+__device__ __forceinline__ void stage_row_to_tmem(uint32_t taddr, const uint8_t* tile, int r) {
+  using L = TileLayout<D>;
+  constexpr int CPB = L::SWB / 16;  // 16-byte chunks per box row; the TMA swizzle permutes them by row
+  uint32_t u[D / 2];
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    const uint32_t o = uint32_t(r * L::SWB + (c % CPB) * 16);
+    const uint32_t sw = o ^ (((o >> 7) & uint32_t(CPB - 1)) << 4);
+    const uint4 x = *reinterpret_cast<const uint4*>(tile + (c / CPB) * L::BOXB + sw);
+    u[4 * c] = x.x;
+    u[4 * c + 1] = x.y;
+    u[4 * c + 2] = x.z;
+    u[4 * c + 3] = x.w;
+  }
+  if constexpr (D == 16) {
+    tmem_st8(taddr, u);
+  } else if constexpr (D == 32) {
+    tmem_st16(taddr, u);
+  } else {
+#pragma unroll
+    for (int c = 0; c < D / 2; c += 32) tmem_st32(taddr + c, u + c);
+  }
+}
+
+// AND of `v` over the 256 row threads (named barrier kNamedBarRows).
+__device__ __forceinline__ bool rows_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(kNamedBarRows)
+      : "memory");
+  return r != 0;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -784,27 +834,29 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* a_full = bars;
-  uint64_t* st_full = bars + 1;
+  uint64_t* st_full = bars;
   uint64_t* st_empty = st_full + C::NS;
   uint64_t* s_full = st_empty + C::NS;  // [NSLOT] S and dP of the job in the slot are ready
-  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT] the group of the job in the slot has written its P / dS
-  uint64_t* acc_done = p_full + C::NSLOT;
-  uint64_t* drain = acc_done + 1;
-  uint64_t* at_full = drain + 1;        // stationary operands written into TMEM by the row threads
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(at_full + 1);
+  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT] the group of the job in the slot has written its dS
+  uint64_t* acc_done = p_full + C::NSLOT;  // every MMA of the unit has completed (dQ final)
+  uint64_t* acc_free = acc_done + 1;       // the row threads have read dQ out of TMEM
+  uint64_t* drain = acc_free + 1;
+  uint64_t* at_full = drain + 1;  // the unit's Q and dO rows are in TMEM
+  uint64_t* x_full = at_full + 1;  // the unit's Q and dO tiles are in the staging buffer
+  uint64_t* x_empty = x_full + 1;  // the row threads have copied the staging buffer
+  uint64_t* u_full = x_empty + 1;  // [kUQ] unit ids handed from the producer to the MMA warp and the rows
+  uint64_t* u_empty = u_full + kUQ;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + kUQ);
+  int* uq = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbh = p.B * p.H;
-  const int i = p.NB - 1 - int(blockIdx.x) / nbh;  // longest query tiles first
-  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
-  const int nsteps = i + 1;                         // key tiles j = i, i-1, ..., 0
+  const int nunits = p.NB * nbh;
   // Q and dO (stationary) as TMEM operands of S and dP.
   constexpr int COL_Q = C::COL_X, COL_DO = COL_Q + D / 2;
 
   if (threadIdx.x == 0) {
-    mbar_init(a_full, 1);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
@@ -814,8 +866,15 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       mbar_init(p_full + x, kGroupThreads);
     }
     mbar_init(acc_done, 1);
+    mbar_init(acc_free, kRowThreads);
     mbar_init(drain, 1);
     mbar_init(at_full, kRowThreads);
+    mbar_init(x_full, 1);
+    mbar_init(x_empty, kRowThreads);
+    for (int x = 0; x < kUQ; ++x) {
+      mbar_init(u_full + x, 1);
+      mbar_init(u_empty + x, 1 + kRowThreads / 32);  // the MMA warp and each row warp
+    }
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -823,7 +882,6 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const size_t zb = size_t(z) * p.TP;
   // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
   // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
   if (warp < kRowWarp0) regs_producer();
@@ -837,271 +895,391 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     }
     __syncwarp();
     bool ok = true;
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS, j = i - k;
-      if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 201);
+    int gk = 0, nx = 0;  // tiles and staged units issued so far
+    for (int u = 0; ok; ++u) {
+      const int us = u % kUQ;
+      if (u >= kUQ) ok = mbar_wait(u_empty + us, ((u / kUQ) - 1) & 1, p.status, 230);
+      if (!ok) break;
+      int x = 0;
+      if (lane == 0) {
+        x = atomicAdd(p.sched + 1, 1);
+        uq[us] = x;
+        mbar_arrive(u_full + us);
+      }
+      x = __shfl_sync(0xffffffffu, x, 0);
+      if (x >= nunits) break;
+      const int i = p.NB - 1 - x / nbh, z = x % nbh, b = z / p.H, h = z % p.H;
+      const size_t zb = size_t(z) * p.TP;
+      if (nx > 0) ok = mbar_wait(x_empty, (nx - 1) & 1, p.status, 231);
       if (!ok) break;
       if (elect_one()) {
-        uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
-        mbar_expect_tx(st_full + st, 2 * C::TILEB + 5 * C::VECB);
+        mbar_expect_tx(x_full, 2 * C::TILEB);
         for (int bx = 0; bx < C::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, st_full + st);
-          tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, st_full + st);
+          tma_load_4d(smem + C::OFF_X + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, x_full);
+          tma_load_4d(smem + C::OFF_X + C::TILEB + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b, x_full);
         }
-        const size_t off = zb + size_t(j) * kBT;
-        bulk_load(vec, p.kv4 + off, 4 * C::VECB, st_full + st);
-        bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
       }
       __syncwarp();
-    }
-    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
-      mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 203);
-  } else if (warp == kWarpMma) {
-    // Jobs n = 2 k + g in order (key tile k, row group g = key columns [64 g, 64 g + 64)). S and dP of job n go
-    // into slot n % NSLOT; once the group has written dS there, dQ += dS K over its 64 keys, then the products of
-    // job n + NSLOT into the same slot (in issue order, so the read of dS comes first).
-    const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
-    const int njobs = 2 * nsteps;
-    auto issue_s = [&](int n) {
-      const int g = n & 1, st = (n >> 1) % C::NS;
-      const uint32_t dcol = tmem + (n % C::NSLOT) * 128;
-      issue_ts_k<D>(dcol, tmem + COL_Q, s1 + st * C::TILEB + g * kHalf * C::SWB);           // S  = Q K^T
-      issue_ts_k<D>(dcol + kHalf, tmem + COL_DO, s2 + st * C::TILEB + g * kHalf * C::SWB);  // dP = dO V^T
-      mma_commit_w(s_full + n % C::NSLOT);
-    };
-    bool ok = mbar_wait(at_full, 0, p.status, 210);
-    int loaded = -1;  // streamed tiles known to be in shared memory: 0 .. loaded
-    auto need_tile = [&](int kt) {
-      if (ok && kt > loaded) {
-        ok = mbar_wait(st_full + kt % C::NS, (kt / C::NS) & 1, p.status, 211);
-        loaded = kt;
-        tc_fence_after();
+      ++nx;
+      for (int k = 0; k <= i && ok; ++k, ++gk) {
+        const int st = gk % C::NS, j = i - k;
+        if (gk >= C::NS) ok = mbar_wait(st_empty + st, ((gk / C::NS) - 1) & 1, p.status, 201);
+        if (!ok) break;
+        if (elect_one()) {
+          uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
+          mbar_expect_tx(st_full + st, 2 * C::TILEB + 5 * C::VECB);
+          for (int bx = 0; bx < C::NBOX; ++bx) {
+            tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b,
+                        st_full + st);
+            tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b,
+                        st_full + st);
+          }
+          const size_t off = zb + size_t(j) * kBT;
+          bulk_load(vec, p.kv4 + off, 4 * C::VECB, st_full + st);
+          bulk_load(vec + 4 * C::VECB, p.phi + off, C::VECB, st_full + st);
+        }
+        __syncwarp();
       }
-      return ok;
-    };
-    tc_fence_after();
-    for (int n = 0; n < C::NSLOT && n < njobs; ++n)
-      if (need_tile(n >> 1)) issue_s(n);
-    for (int n = 0; n < njobs && ok; ++n) {
-      const int g = n & 1, k = n >> 1, st = k % C::NS;
-      ok = mbar_wait(p_full + n % C::NSLOT, (n / C::NSLOT) & 1, p.status, 212);
-      if (!ok) break;
-      tc_fence_after();
-      issue_ts_half<D>(tmem + C::COL_A1, tmem + (n % C::NSLOT) * 128 + kHalf, s1 + st * C::TILEB, g, n > 0);
-      if (g == 1) mma_commit_w(st_empty + st);
-      const int m = n + C::NSLOT;
-      if (m < njobs && need_tile(m >> 1)) issue_s(m);
     }
-    mma_commit_w(acc_done);
+    // Nothing may land in shared memory after the CTA exits: wait for the last copies issued.
+    for (int q = (gk > C::NS ? gk - C::NS : 0); q < gk; ++q) mbar_wait(st_full + q % C::NS, (q / C::NS) & 1, p.status, 203);
+    if (nx > 0) mbar_wait(x_full, (nx - 1) & 1, p.status, 204);
+  } else if (warp == kWarpMma) {
+    // Jobs n = 2 k + g of a unit in order (key tile k, row group g = key columns [64 g, 64 g + 64)); with gn jobs
+    // before the unit, S and dP of job n go into slot (gn + n) % NSLOT; once the group has written dS there,
+    // dQ += dS K over its 64 keys, then the products of job n + NSLOT into the same slot (in issue order, so the
+    // read of dS comes first). The first dQ product of a unit overwrites dQ, so it waits until the rows have read
+    // the previous unit's.
+    const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
+    bool ok = true;
+    int gn = 0, gk = 0, loaded = -1;
+    for (int u = 0; ok; ++u) {
+      const int us = u % kUQ;
+      ok = mbar_wait(u_full + us, (u / kUQ) & 1, p.status, 232);
+      if (!ok) break;
+      const int x = uq[us];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(u_empty + us);
+      if (x >= nunits) break;
+      const int i = p.NB - 1 - x / nbh;
+      const int njobs = 2 * (i + 1);
+      auto need_tile = [&](int kt) {
+        const int gt = gk + kt;
+        if (ok && gt > loaded) {
+          ok = mbar_wait(st_full + gt % C::NS, (gt / C::NS) & 1, p.status, 211);
+          loaded = gt;
+          tc_fence_after();
+        }
+        return ok;
+      };
+      auto issue_s = [&](int n) {
+        const int g = n & 1, st = (gk + (n >> 1)) % C::NS, sl = (gn + n) % C::NSLOT;
+        const uint32_t dcol = tmem + sl * 128;
+        issue_ts_k<D>(dcol, tmem + COL_Q, s1 + st * C::TILEB + g * kHalf * C::SWB);           // S  = Q K^T
+        issue_ts_k<D>(dcol + kHalf, tmem + COL_DO, s2 + st * C::TILEB + g * kHalf * C::SWB);  // dP = dO V^T
+        mma_commit_w(s_full + sl);
+      };
+      ok = mbar_wait(at_full, u & 1, p.status, 210);
+      tc_fence_after();
+      for (int n = 0; n < C::NSLOT && n < njobs; ++n)
+        if (need_tile(n >> 1)) issue_s(n);
+      for (int n = 0; n < njobs && ok; ++n) {
+        const int g = n & 1, st = (gk + (n >> 1)) % C::NS, sl = (gn + n) % C::NSLOT;
+        ok = mbar_wait(p_full + sl, ((gn + n) / C::NSLOT) & 1, p.status, 212);
+        if (ok && n == 0 && u > 0) ok = mbar_wait(acc_free, (u - 1) & 1, p.status, 215);
+        if (!ok) break;
+        tc_fence_after();
+        issue_ts_half<D>(tmem + C::COL_A1, tmem + sl * 128 + kHalf, s1 + st * C::TILEB, g, n > 0);
+        if (g == 1) mma_commit_w(st_empty + st);
+        const int m = n + C::NSLOT;
+        if (m < njobs && need_tile(m >> 1)) issue_s(m);
+      }
+      mma_commit_w(acc_done);
+      gn += njobs;
+      gk += njobs / 2;
+    }
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 214);
   } else if (warp >= kRowWarp0) {
     regs_rows();
     const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
-    const int r = wr * 32 + (threadIdx.x & 31);  // query within the tile = TMEM lane
-    const int cb = grp * kHalf;                  // this group's key columns [cb, cb + 64)
-    const int t = i * kBT + r;
-    const bool t_ok = t < p.T;
+    const int r = wr * 32 + lane;  // query within the tile = TMEM lane
+    const int cb = grp * kHalf;    // this group's key columns [cb, cb + 64)
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
-    {
-      // Group 0 writes the query's row of Q, group 1 its row of dO, into TMEM.
-      const __half* row = grp == 0 ? p.q + b * p.q_s[0] + h * p.q_s[1] + int64_t(t_ok ? t : 0) * p.q_s[2]
-                                   : p.dout + b * p.do_s[0] + h * p.do_s[1] + int64_t(t_ok ? t : 0) * p.do_s[2];
-      row_to_tmem<D>(tl + (grp == 0 ? COL_Q : COL_DO), row, t_ok);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(at_full);
-    }
-    const float betal = p.beta[h] * kLog2e;
-    const float* own = reinterpret_cast<const float*>(p.qv4 + zb + (t & ~1));  // (-lse, -delta) pair of t
-    const float nlse = own[t & 1];   // -inf beyond T
-    const float ndel = own[2 + (t & 1)];
-    const float pre_t = p.pre[zb + t];
-    const float prel_t = p.prel[zb + t];
-    const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
-    const float bpre = t_ok ? ex2(prel_t - c2_t) : 1.f;
-    const float* bmin = p.bmin + size_t(z) * p.NB;
-    const float* bl = p.bl + size_t(z) * p.NB;
-    const float2 sc2 = make_float2(p.scale2, p.scale2), bet2 = make_float2(betal, betal);
-    const float2 nlse2 = make_float2(nlse, nlse), ndel2 = make_float2(ndel, ndel);
-    float2 racc2 = make_float2(0.f, 0.f);
-    float mid = kInf, midl = -kInf;
-    bool ok = true;
-    // Per-tile scalars of key tile j, loaded one tile ahead so their latency hides behind the element work.
-    const float* sufr = p.sufr + size_t(z) * p.NB;
-    float bl_n = bl[i], bmin_n = bmin[i], sufr_n = sufr[i], sufl0_n = p.sufl[zb + size_t(i) * kBT];
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS, j = i - k;
-      const float blj = bl_n, bminj = bmin_n, sufrj = sufr_n, sufl0 = sufl0_n;
-      if (j > 0) {
-        bl_n = bl[j - 1];
-        bmin_n = bmin[j - 1];
-        sufr_n = sufr[j - 1];
-        sufl0_n = p.sufl[zb + size_t(j - 1) * kBT];
-      }
-      const int n = 2 * k + grp, slot = n % C::NSLOT;
-      ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 220);
-      if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 221);
-      if (!ok) break;
-      tc_fence_after();
-      // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
-      // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
-      const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
-      const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
-      const float4* KV = reinterpret_cast<const float4*>(vbase);  // key pairs: (SUF - psi, -psi), (sufy, SUFL)
-      const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
-      const bool diag = k == 0;
-      const float cap = fminf(mid, pre_t);
-      const float mterm = ex2(midl - c2_t) + bpre;
-      // 2^{SUFL_s - c2_t} = sufy_s * 2^{SUFL_first - c2_t} when both factors stay in range.
-      // Warp-uniform (the chunk body holds warp-collective TMEM loads and stores). Rows beyond T take either path.
-      const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (sufrj <= 120.f && sufl0 - c2_t <= 120.f)));
-      const float yfac = (fact && t_ok) ? ex2(sufl0 - c2_t) : 0.f;
-      const float2 cap2 = make_float2(cap, cap), yf2 = make_float2(yfac, yfac), mt2 = make_float2(mterm, mterm);
-      const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
-      // Diagonal tile, keys descending: rr = min phi over (key, query]; the first group starts from the minimum
-      // over the second group's keys up to the query, [64, query].
-      float rr = kInf;
-      if (diag && grp == 0)
-        for (int c = kHalf; c < kBT; ++c)
-          if (c <= r) rr = fminf(rr, vphi[c]);
-      // 16 key columns per chunk: load S and dP, compute dS (fp16) and write it over the first 8 of those 16 dP
-      // columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal two keys
-      // are handled per step with packed f32x2 arithmetic.
-      auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
-        constexpr bool DIAG = decltype(diag_tag)::value;
-        constexpr bool FACT = decltype(fact_tag)::value;
-        uint32_t dpk[8];
-        if constexpr (DIAG) {
-#pragma unroll
-          for (int e = 15; e >= 0; --e) {
-            const int c = c0 + e;
-            const float4 va = KV[c0 + (e & ~1)];
-            const float npsi = (e & 1) ? va.w : va.z;
-            const float x = rr + npsi;  // +inf at c == r
-            rr = c <= r ? fminf(rr, vphi[c]) : rr;
-            const float xm = fminf(x, 0.f);
-            const float sv = fmaf(sS[e], p.scale2, betal * xm);
-            const bool valid = c <= r && c < kvalid;
-            sP[e] = valid ? ex2(sv + nlse) * (sP[e] + ndel) : 0.f;
-          }
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float4 va = KV[c0 + e];      // (SUF_c - psi_c, SUF_c1 - psi_c1, -psi_c, -psi_c1)
-            const float4 vb = KV[c0 + e + 1];  // (sufy_c, sufy_c1, SUFL_c, SUFL_c1)
-            const float2 dd = __fadd2_rn(cap2, make_float2(va.z, va.w));
-            const float2 x = make_float2(fminf(va.x, dd.x), fminf(va.y, dd.y));
-            const float2 xm = make_float2(fminf(x.x, 0.f), fminf(x.y, 0.f));
-            float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
-            sv = __fadd2_rn(sv, nlse2);
-            const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
-            const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), ndel2));
-            const float2 g = make_float2(x.x <= 0.f ? ds.x : 0.f, x.y <= 0.f ? ds.y : 0.f);
-            float2 den;
-            if constexpr (FACT)
-              den = __ffma2_rn(make_float2(vb.x, vb.y), yf2, mt2);
-            else
-              den = make_float2(ex2(vb.z - c2_t) + mterm, ex2(vb.w - c2_t) + mterm);
-            racc2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), racc2);
-            dpk[e / 2] = pack_half2(ds.x, ds.y);
-          }
-        }
-        tmem_st8(tP + c0, dpk);
-      };
-      // The group's four chunks, descending, with the TMEM loads of the next chunk in flight during the current one.
-      auto tile = [&](auto diag_tag, auto fact_tag) {
-        float sA[16], pA[16], sB[16], pB[16];
-        const int top = cb + kHalf - 16;
-        tmem_ld16(tS + top, sA);
-        tmem_ld16(tP + top, pA);
-        tmem_ld_wait_regs(sA, pA);
-#pragma unroll
-        for (int q = 0; q < kHalf / 16; q += 2) {
-          const int c0 = top - 16 * q;
-          tmem_ld16(tS + c0 - 16, sB);
-          tmem_ld16(tP + c0 - 16, pB);
-          chunk(c0, sA, pA, diag_tag, fact_tag);
-          tmem_ld_wait_regs(sB, pB);
-          if (q + 2 < kHalf / 16) {
-            tmem_ld16(tS + c0 - 32, sA);
-            tmem_ld16(tP + c0 - 32, pA);
-          }
-          chunk(c0 - 16, sB, pB, diag_tag, fact_tag);
-          if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
-        }
-      };
-      if (diag)
-        tile(std::true_type{}, std::false_type{});
-      else if (fact)
-        tile(std::false_type{}, std::true_type{});
-      else
-        tile(std::false_type{}, std::false_type{});
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full + slot);
-      if (!diag) {
-        mid = fminf(mid, bminj);
-        midl = lse2(midl, blj);
-      }
-    }
-    const float racc = racc2.x + racc2.y;
-    const float a2_t = t_ok ? -p.phi[zb + t] * p.il2 : 0.f;  // for DPHI2 below; loaded while dQ drains
-    if (ok) ok = mbar_wait(acc_done, 0, p.status, 222);
-    if (ok) {
-      tc_fence_after();
-      __half* dqrow = p.dq + b * p.dq_s[0] + h * p.dq_s[1] + int64_t(t_ok ? t : 0) * p.dq_s[2];
-      constexpr int DH = D >= 32 ? D / 2 : D;
-      if (D >= 32 || grp == 0) {
-#pragma unroll
-        for (int c = grp * DH; c < grp * DH + DH; c += 16) {
-          float a1[16];
-          tmem_ld16(tl + C::COL_A1 + c, a1);
-          tmem_ld_wait();
-          if (t_ok) {
-            uint32_t u[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) u[e] = pack_half2(a1[2 * e] * p.scale, a1[2 * e + 1] * p.scale);
-            reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(u[0], u[1], u[2], u[3]);
-            reinterpret_cast<uint4*>(dqrow + c)[1] = make_uint4(u[4], u[5], u[6], u[7]);
-          }
-        }
-      }
-    }
-    // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile); r_t joins the two
-    // groups' partial sums in a fixed order. The two groups split each position's range of t in halves (group 0
-    // the lower one), each with four accumulators joined in a fixed order.
+    constexpr int DH = D >= 32 ? D / 2 : D;  // head-dim columns of dQ stored by each group
+    const float2 sc2 = make_float2(p.scale2, p.scale2);
     float* rx = red + 32;
     float* rsh = red + 32 + kBT;
     float* csh = red + 32 + 2 * kBT;
-    if (grp == 1) rx[r] = racc;
-    rows_sync();
-    if (grp == 0) {
-      rsh[r] = racc + rx[r];
-      csh[r] = c2_t;
-    }
-    rows_sync();
-    float p2 = 0.f;
-    if (t_ok) {
-      const int tend = min(kBT, p.T - i * kBT);
-      const int mid = r + ((tend - r + 1) >> 1);
-      const int lo = grp == 0 ? r : mid, hi = grp == 0 ? mid : tend;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      int t2 = lo;
-      for (; t2 + 4 <= hi; t2 += 4) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(ex2(a2_t - csh[t2 + e]), rsh[t2 + e], acc[e]);
+    bool ok = true;
+    int gn = 0, gk = 0;
+    // The finished unit, written out after the next unit's Q and dO rows are in TMEM.
+    bool have_prev = false;
+    float dqv[DH];
+    int pv_t = 0, pv_i = 0, pv_b = 0, pv_h = 0;
+    size_t pv_zb = 0;
+    bool pv_ok = false;
+    float pv_racc = 0.f, pv_c2 = 0.f, pv_a2 = 0.f;
+    for (int u = 0;; ++u) {
+      const int us = u % kUQ;
+      int x = nunits;
+      if (ok) ok = mbar_wait(u_full + us, (u / kUQ) & 1, p.status, 233);
+      if (ok) x = uq[us];
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(u_empty + us);
+      const bool more = rows_all(ok && x < nunits);
+      const int i = more ? p.NB - 1 - x / nbh : 0;
+      const int z = more ? x % nbh : 0, b = z / p.H, h = z % p.H;
+      const size_t zb = size_t(z) * p.TP;
+      const int t = i * kBT + r;
+      const bool t_ok = more && t < p.T;
+      // The unit's per-query and per-tile scalars, loaded first so that their latency passes during the copy below
+      // and the previous unit's write-out.
+      float2 nl_nd = make_float2(0.f, 0.f);
+      float pre_t = 0.f, prel_t = 0.f, phi_t = 0.f, beta_h = 0.f, bl_n = 0.f, bmin_n = 0.f, sufr_n = 0.f,
+            sufl0_n = 0.f;
+      if (more) {
+        const float* own = reinterpret_cast<const float*>(p.qv4 + zb + (t & ~1));  // (-lse, -delta) pair of t
+        nl_nd = make_float2(own[t & 1], own[2 + (t & 1)]);  // -lse is -inf beyond T
+        pre_t = p.pre[zb + t];
+        prel_t = p.prel[zb + t];
+        phi_t = p.phi[zb + t];
+        beta_h = p.beta[h];
+        bl_n = p.bl[size_t(z) * p.NB + i];
+        bmin_n = p.bmin[size_t(z) * p.NB + i];
+        sufr_n = p.sufr[size_t(z) * p.NB + i];
+        sufl0_n = p.sufl[zb + size_t(i) * kBT];
       }
+      if (more) {
+        // Group 0 copies the query's row of Q, group 1 its row of dO, into TMEM. Every MMA of the previous unit
+        // has completed (acc_done), so nothing reads those columns any more.
+        ok = mbar_wait(x_full, u & 1, p.status, 234);
+        if (ok) {
+          stage_row_to_tmem<D>(tl + (grp == 0 ? COL_Q : COL_DO), smem + C::OFF_X + grp * C::TILEB, r);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(at_full);
+        mbar_arrive(x_empty);
+      }
+      if (have_prev) {
+        if (pv_ok && (D >= 32 || grp == 0)) {
+          __half* dqrow = p.dq + pv_b * p.dq_s[0] + pv_h * p.dq_s[1] + int64_t(pv_t) * p.dq_s[2] + grp * DH;
 #pragma unroll
-      for (int e = 0; e < 3; ++e)
-        if (t2 + e < hi) acc[e] = fmaf(ex2(a2_t - csh[t2 + e]), rsh[t2 + e], acc[e]);
-      p2 = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          for (int c = 0; c < DH; c += 8) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w4[e] = pack_half2(dqv[c + 2 * e] * p.scale, dqv[c + 2 * e + 1] * p.scale);
+            reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+        // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile), with r_t joining
+        // the two groups' partial sums in a fixed order. PRE is non-increasing within the tile, so
+        //   DPHI2_u = 2^{a2_u - c2_u} Q_u,  Q_u = r_u + f_u Q_{u+1},  f_u = 2^{c2_u - c2_{u+1}} <= 1,
+        // a linear recurrence that contracts; the first row warp solves it: four positions per lane, then a suffix
+        // scan of the lanes' affine maps Q_{4l} = A + B Q_{4l+4}.
+        if (grp == 1) rx[r] = pv_racc;
+        rows_sync();
+        if (grp == 0) {
+          rsh[r] = pv_racc + rx[r];
+          csh[r] = pv_c2;
+        }
+        rows_sync();
+        if (warp == kRowWarp0) {
+          const int tend = min(kBT, p.T - pv_i * kBT);
+          float rv[4], fv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int u = 4 * lane + e;
+            rv[e] = u < tend ? rsh[u] : 0.f;
+            fv[e] = u + 1 < tend ? ex2(csh[u] - csh[u + 1]) : 0.f;
+          }
+          float A = rv[3], Bm = fv[3];
+#pragma unroll
+          for (int e = 2; e >= 0; --e) {
+            A = fmaf(fv[e], A, rv[e]);
+            Bm *= fv[e];
+          }
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float A2 = __shfl_down_sync(0xffffffffu, A, o), B2 = __shfl_down_sync(0xffffffffu, Bm, o);
+            if (lane + o < 32) {
+              A = fmaf(Bm, A2, A);
+              Bm *= B2;
+            }
+          }
+          float qn = __shfl_down_sync(0xffffffffu, A, 1);  // Q_{4l+4}
+          if (lane == 31) qn = 0.f;
+#pragma unroll
+          for (int e = 3; e >= 0; --e) {
+            qn = fmaf(fv[e], qn, rv[e]);
+            rsh[4 * lane + e] = qn;
+          }
+        }
+        rows_sync();
+        // rsh, csh and rx are next written after the rows_all of the next unit.
+        if (grp == 0 && pv_ok) p.dphi2[pv_zb + pv_t] = ex2(pv_a2 - pv_c2) * rsh[r];
+      }
+      if (!more) break;
+
+      const int nsteps = i + 1;
+      const float betal = beta_h * kLog2e;
+      const float nlse = nl_nd.x, ndel = nl_nd.y;
+      const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
+      const float bpre = t_ok ? ex2(prel_t - c2_t) : 1.f;
+      const float a2_t = t_ok ? -phi_t * p.il2 : 0.f;  // for DPHI2 of this unit
+      const float* bmin = p.bmin + size_t(z) * p.NB;
+      const float* bl = p.bl + size_t(z) * p.NB;
+      const float2 bet2 = make_float2(betal, betal);
+      const float2 nlse2 = make_float2(nlse, nlse), ndel2 = make_float2(ndel, ndel);
+      float2 racc2 = make_float2(0.f, 0.f);
+      float mid = kInf, midl = -kInf;
+      // Per-tile scalars of key tile j (those of the first tile were loaded above), loaded one tile ahead so their
+      // latency hides behind the element work.
+      const float* sufr = p.sufr + size_t(z) * p.NB;
+      for (int k = 0; k < nsteps && ok; ++k) {
+        const int gt = gk + k, st = gt % C::NS, j = i - k;
+        const float blj = bl_n, bminj = bmin_n, sufrj = sufr_n, sufl0 = sufl0_n;
+        if (j > 0) {
+          bl_n = bl[j - 1];
+          bmin_n = bmin[j - 1];
+          sufr_n = sufr[j - 1];
+          sufl0_n = p.sufl[zb + size_t(j - 1) * kBT];
+        }
+        const int n = gn + 2 * k + grp, slot = n % C::NSLOT;
+        ok = mbar_wait(st_full + st, (gt / C::NS) & 1, p.status, 220);
+        if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 221);
+        if (!ok) break;
+        tc_fence_after();
+        // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
+        // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
+        const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
+        const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
+        const float4* KV = reinterpret_cast<const float4*>(vbase);  // key pairs: (SUF - psi, -psi), (sufy, SUFL)
+        const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
+        const bool diag = k == 0;
+        const float cap = fminf(mid, pre_t);
+        const float mterm = ex2(midl - c2_t) + bpre;
+        // 2^{SUFL_s - c2_t} = sufy_s * 2^{SUFL_first - c2_t} when both factors stay in range.
+        // Warp-uniform (the chunk body holds warp-collective TMEM loads and stores). Rows beyond T take either path.
+        const bool fact = __all_sync(0xffffffffu, !diag && (!t_ok || (sufrj <= 120.f && sufl0 - c2_t <= 120.f)));
+        const float yfac = (fact && t_ok) ? ex2(sufl0 - c2_t) : 0.f;
+        const float2 cap2 = make_float2(cap, cap), yf2 = make_float2(yfac, yfac), mt2 = make_float2(mterm, mterm);
+        const int kvalid = p.T - j * kBT;  // keys c < kvalid exist
+        // Diagonal tile, keys descending: rr = min phi over (key, query]; the first group starts from the minimum
+        // over the second group's keys up to the query, [64, query].
+        float rr = kInf;
+        if (diag && grp == 0)
+          for (int c = kHalf; c < kBT; ++c)
+            if (c <= r) rr = fminf(rr, vphi[c]);
+        // 16 key columns per chunk: load S and dP, compute dS (fp16) and write it over the first 8 of those 16 dP
+        // columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal two keys
+        // are handled per step with packed f32x2 arithmetic.
+        auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
+          constexpr bool DIAG = decltype(diag_tag)::value;
+          constexpr bool FACT = decltype(fact_tag)::value;
+          uint32_t dpk[8];
+          if constexpr (DIAG) {
+#pragma unroll
+            for (int e = 15; e >= 0; --e) {
+              const int c = c0 + e;
+              const float4 va = KV[c0 + (e & ~1)];
+              const float npsi = (e & 1) ? va.w : va.z;
+              const float x = rr + npsi;  // +inf at c == r
+              rr = c <= r ? fminf(rr, vphi[c]) : rr;
+              const float xm = fminf(x, 0.f);
+              const float sv = fmaf(sS[e], p.scale2, betal * xm);
+              const bool valid = c <= r && c < kvalid;
+              sP[e] = valid ? ex2(sv + nlse) * (sP[e] + ndel) : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float4 va = KV[c0 + e];      // (SUF_c - psi_c, SUF_c1 - psi_c1, -psi_c, -psi_c1)
+              const float4 vb = KV[c0 + e + 1];  // (sufy_c, sufy_c1, SUFL_c, SUFL_c1)
+              const float2 dd = __fadd2_rn(cap2, make_float2(va.z, va.w));
+              const float2 x = make_float2(fminf(va.x, dd.x), fminf(va.y, dd.y));
+              const float2 xm = make_float2(fminf(x.x, 0.f), fminf(x.y, 0.f));
+              float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
+              sv = __fadd2_rn(sv, nlse2);
+              const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
+              const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), ndel2));
+              const float2 g = make_float2(x.x <= 0.f ? ds.x : 0.f, x.y <= 0.f ? ds.y : 0.f);
+              float2 den;
+              if constexpr (FACT)
+                den = __ffma2_rn(make_float2(vb.x, vb.y), yf2, mt2);
+              else
+                den = make_float2(ex2(vb.z - c2_t) + mterm, ex2(vb.w - c2_t) + mterm);
+              racc2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), racc2);
+              dpk[e / 2] = pack_half2(ds.x, ds.y);
+            }
+          }
+          tmem_st8(tP + c0, dpk);
+        };
+        // The group's four chunks, descending, with the TMEM loads of the next chunk in flight during the current
+        // one.
+        auto tile = [&](auto diag_tag, auto fact_tag) {
+          float sA[16], pA[16], sB[16], pB[16];
+          const int top = cb + kHalf - 16;
+          tmem_ld16(tS + top, sA);
+          tmem_ld16(tP + top, pA);
+          tmem_ld_wait_regs(sA, pA);
+#pragma unroll
+          for (int q = 0; q < kHalf / 16; q += 2) {
+            const int c0 = top - 16 * q;
+            tmem_ld16(tS + c0 - 16, sB);
+            tmem_ld16(tP + c0 - 16, pB);
+            chunk(c0, sA, pA, diag_tag, fact_tag);
+            tmem_ld_wait_regs(sB, pB);
+            if (q + 2 < kHalf / 16) {
+              tmem_ld16(tS + c0 - 32, sA);
+              tmem_ld16(tP + c0 - 32, pA);
+            }
+            chunk(c0 - 16, sB, pB, diag_tag, fact_tag);
+            if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
+          }
+        };
+        if (diag)
+          tile(std::true_type{}, std::false_type{});
+        else if (fact)
+          tile(std::false_type{}, std::true_type{});
+        else
+          tile(std::false_type{}, std::false_type{});
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full + slot);
+        if (!diag) {
+          mid = fminf(mid, bminj);
+          midl = lse2(midl, blj);
+        }
+      }
+      // dQ of the unit out of TMEM; the MMA warp may then start the next unit's dQ.
+      if (ok) ok = mbar_wait(acc_done, u & 1, p.status, 222);
+      if (ok) {
+        tc_fence_after();
+        if (D >= 32 || grp == 0) {
+#pragma unroll
+          for (int c = 0; c < DH; c += 16) tmem_ld16(tl + C::COL_A1 + grp * DH + c, dqv + c);
+          tmem_ld_wait();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_free);
+      have_prev = true;
+      pv_t = t;
+      pv_i = i;
+      pv_b = b;
+      pv_h = h;
+      pv_zb = zb;
+      pv_ok = t_ok && ok;
+      pv_racc = racc2.x + racc2.y;
+      pv_c2 = c2_t;
+      pv_a2 = a2_t;
+      gn += 2 * nsteps;
+      gk += nsteps;
     }
-    if (grp == 1) rx[r] = p2;
-    rows_sync();
-    if (grp == 0 && t_ok) p.dphi2[zb + t] = p2 + rx[r];
   }
   tc_fence_before();
   __syncthreads();
@@ -1113,7 +1291,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
-               const Fact& fact, float* gd, const float4* qv4, int* status, cudaStream_t s, std::string* err) {
+               const Fact& fact, float* gd, const float4* qv4, int* sched, int* status, cudaStream_t s,
+               std::string* err) {
   using CK = TcBwdCfg<D, true>;
   using CQ = TcBwdCfg<D, false>;
   CUtensorMap mq, mk, mv, mdo;
@@ -1165,6 +1344,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.dphi4 = sc.dphi4;
   p.dphi2 = sc.dphi2;
   p.status = status;
+  p.sched = sched;
   p.B = d.B;
   p.H = d.H;
   p.T = d.T;
@@ -1182,6 +1362,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     return FPA_ERR_CUDA;
   }
   const int grid = d.NB * d.BH();
+  const int qgrid = std::min(grid, sm_count());  // persistent; the stats kernel zeroed the unit counters
   prof_mark(s, "bwd_kv_tc");
   kv<<<grid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
@@ -1191,7 +1372,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   }
   if (e == cudaSuccess) {
     prof_mark(s, "bwd_q_tc");
-    qk<<<grid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
+    qk<<<qgrid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -1221,7 +1402,7 @@ size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
   return keycols_bytes(d) + gd_bytes(d) +
          2 * align256(bh * d.TP * sizeof(float4)) + 2 * align256(bh * d.TP * sizeof(float)) +
-         2 * align256(bh * d.NB * sizeof(float));
+         2 * align256(bh * d.NB * sizeof(float)) + align256(2 * sizeof(int));
 }
 
 int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
@@ -1258,6 +1439,8 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   fact.prer = reinterpret_cast<float*>(q);
   q += align256(bh * d.NB * 4);
   fact.sufr = reinterpret_cast<float*>(q);
+  q += align256(bh * d.NB * 4);
+  fact.sched = reinterpret_cast<int*>(q);  // work-unit counters of the persistent passes
   // Raw key vectors, the factorisation arrays and the padded lse copy (filled by the stats and delta kernels).
   prof_mark(s, "stats");
   cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
@@ -1283,10 +1466,10 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   }
   int rc;
   switch (d.D) {
-    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
-    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
-    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
-    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status, s, err); break;
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
   if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, delta (+ pack), kv, [diag], q

@@ -1,4 +1,4 @@
-// Host-side TMA tensor maps for the tensor-core kernels.
+// Host-side TMA tensor maps and device queries for the tensor-core kernels.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -22,6 +22,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 }  // namespace
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
 
 bool tma_layout_ok(const void* p, const int64_t st[4]) {
   if (reinterpret_cast<uintptr_t>(p) % 16) return false;
