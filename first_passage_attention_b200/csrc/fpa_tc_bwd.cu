@@ -1,19 +1,22 @@
 // Tensor-core backward pass of FPA for sm_100a (fp16 operands, fp32 accumulation), in two deterministic passes
 // with the decomposition of the reference's backward (kernel.py:178-265 kv-pass, 287-340 q-pass):
 //
-//   tc_bwd_kv_kernel  one CTA per key tile j (128 keys) of one head, query tiles i = j .. NB-1:
+//   tc_bwd_kv_kernel  persistent, one CTA per SM taking key tiles j (128 keys) of one head as work units; per
+//                     unit, query tiles i = j .. NB-1:
 //                     S^T = K Q^T and dP^T = V dO^T into TMEM; thread = key computes P^T, dS^T (fp16, back into
 //                     TMEM over S^T and dP^T), then dV += P^T dO and dK += dS^T Q on the tensor cores. Also dpsi,
 //                     the dbeta partial, the soft-min sums W (u in the key's tile) and TB (u strictly between the
-//                     tiles), and g of the diagonal tile (stored for diag_dphi_kernel).
+//                     tiles), and the in-tile soft-min of the diagonal tile (warps 2-3; for D = 128 its g is stored
+//                     for diag_dphi_kernel).
 //   tc_bwd_q_kernel   persistent, one CTA per SM taking query tiles i of one head as work units; per unit, key
 //                     tiles j = i .. 0: S = Q K^T, dP = dO V^T; thread = query computes dS (fp16, into its own TMEM
 //                     columns) and dQ += dS K; also r_t and from it the soft-min part with u in the query's tile
 //                     (DPHI2).
 //
 // Warp roles (384 threads): warp 0 issues the MMAs (whole warp, one elected lane issues), warp 1 is the TMA
-// producer (streamed tiles and their per-row vectors through a ring of stages), warps 2-3 only hand their
-// registers to the row groups (setmaxnreg). Warps 4-7 and 8-11 are two row groups (thread = TMEM lane); group g
+// producer (work-unit ids, the stationary tiles, streamed tiles and their per-row vectors through a ring of
+// stages), warps 2-3 run the kv-pass's diagonal soft-min and otherwise hand registers to the row groups
+// (setmaxnreg). Warps 4-7 and 8-11 are two row groups (thread = TMEM lane); group g
 // owns columns [64 g, 64 g + 64) of every S / dP tile and runs on its own barriers; S and dP live in TMEM slots
 // that rotate over the jobs (tile, group), so the products of a group's next tile are computed while it works on
 // the current one. Every mbarrier wait is bounded (fpa::sm100::mbar_wait).
@@ -77,14 +80,13 @@ struct TcBwdCfg : TileLayout<D> {
   static constexpr int OFF_B = L::TILEB;                // stationary operand 2 (when !AT)
   static constexpr int OFF_S1 = NSTAT * L::TILEB;       // streamed operand 1 [NS]
   static constexpr int OFF_S2 = OFF_S1 + NS * L::TILEB;  // streamed operand 2 [NS]
-  static constexpr int OFF_X = OFF_S2 + NS * L::TILEB;   // q-pass: the next unit's Q and dO tiles (TMA staging)
-  static constexpr int OFF_VEC = OFF_X + (KV ? 0 : 2 * L::TILEB);  // [NS][VECSTAGE]
+  static constexpr int OFF_X = OFF_S2 + NS * L::TILEB;   // the next unit's stationary tiles (TMA staging; AT)
+  static constexpr int OFF_VEC = OFF_X + (AT ? 2 * L::TILEB : 0);  // [NS][VECSTAGE]
   static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
   static constexpr int OFF_G = OFF_RED + (32 + 4 * kBT) * 4;
-  // kv: a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, drain, at_full, g_full;
-  // q: st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, acc_free, drain, at_full, x_full,
-  // x_empty, u_full[kUQ], u_empty[kUQ]
-  static constexpr int NBAR = 2 * NS + 2 * NSLOT + 6 + 2 * kUQ;
+  // kv: a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, acc_free, drain, at_full,
+  // x_full, x_empty, g_full, g_free, u_full[kUQ], u_empty[kUQ] (the q-pass uses a subset)
+  static constexpr int NBAR = 2 * NS + 2 * NSLOT + 10 + 2 * kUQ;
   // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions (with 2^{a2 - max}) stay in shared
   // memory, where warps 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
   static constexpr int GLD = kBT + 1;
@@ -164,8 +166,23 @@ __device__ __forceinline__ float rows_sum(float v, float* red) {
   return r;
 }
 
-__device__ __forceinline__ void regs_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory"); }
-__device__ __forceinline__ void regs_rows() { asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory"); }
+// Register split per warpgroup (the launch gives 168 per thread): the producer/MMA warpgroup keeps 88 (96 for
+// D = 128, whose MMA warp issues from shared-memory descriptors) and the two row groups take the rest,
+// 128 * 88 + 256 * 208 = 128 * 96 + 256 * 200 = 384 * 168.
+template <int D>
+__device__ __forceinline__ void regs_producer() {
+  if constexpr (D == 128)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
+  else
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+}
+template <int D>
+__device__ __forceinline__ void regs_rows() {
+  if constexpr (D == 128)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
+  else
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+}
 
 // The descriptor of the same operand layout `off` bytes further on: the start address is the low 14-bit field
 // (address >> 4) and shared-memory addresses stay below 2^18, so the offset adds to the low word without a carry.
@@ -212,18 +229,22 @@ __device__ __forceinline__ void issue_ts_k(uint32_t d, uint32_t a_tmem, uint32_t
   }
 }
 
-// One row of a stationary operand (D fp16 values, zeros when !ok) into this thread's TMEM lane, D/2 columns from
-// `taddr` (the packing issue_ts_k expects). Warp-collective.
+// One row of a staged [128 x D] fp16 tile (as TMA wrote it) into this thread's TMEM lane, D/2 columns from `taddr`
+// (the packing issue_ts_k expects: two fp16 per 32-bit column in K order). Warp-collective.
 template <int D>
-__device__ __forceinline__ void row_to_tmem(uint32_t taddr, const __half* row, bool ok) {
+__device__ __forceinline__ void stage_row_to_tmem(uint32_t taddr, const uint8_t* tile, int r) {
+  using L = TileLayout<D>;
+  constexpr int CPB = L::SWB / 16;  // 16-byte chunks per box row; the TMA swizzle permutes them by row
   uint32_t u[D / 2];
 #pragma unroll
-  for (int q = 0; q < D / 8; ++q) {
-    const uint4 x = ok ? reinterpret_cast<const uint4*>(row)[q] : make_uint4(0u, 0u, 0u, 0u);
-    u[4 * q] = x.x;
-    u[4 * q + 1] = x.y;
-    u[4 * q + 2] = x.z;
-    u[4 * q + 3] = x.w;
+  for (int c = 0; c < D / 8; ++c) {
+    const uint32_t o = uint32_t(r * L::SWB + (c % CPB) * 16);
+    const uint32_t sw = o ^ (((o >> 7) & uint32_t(CPB - 1)) << 4);
+    const uint4 x = *reinterpret_cast<const uint4*>(tile + (c / CPB) * L::BOXB + sw);
+    u[4 * c] = x.x;
+    u[4 * c + 1] = x.y;
+    u[4 * c + 2] = x.z;
+    u[4 * c + 3] = x.w;
   }
   if constexpr (D == 16) {
     tmem_st8(taddr, u);
@@ -235,7 +256,29 @@ __device__ __forceinline__ void row_to_tmem(uint32_t taddr, const __half* row, b
   }
 }
 
+// AND of `v` over the `n` threads of named barrier `id` (all of them call it).
+__device__ __forceinline__ bool bar_all(bool v, int id, int n) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ bool rows_all(bool v) { return bar_all(v, kNamedBarRows, kRowThreads); }  // 256 row threads
+__device__ __forceinline__ bool diag_all(bool v) { return bar_all(v, kNamedBarDiag, 64); }  // warps 2-3
+
 // ------------------------------------------------------------------------------------------------ kv-pass ----
+// Persistent, like the q-pass: work units are key tiles j of one head (longest first) taken from a counter. The
+// producer stages each unit's K and V tiles by TMA (or, when K and V stay in shared memory, loads them there once
+// the previous unit's products are complete); at a unit boundary the row threads copy the next unit's K and V rows
+// into TMEM and then read the finished unit's dV and dK out, so the next unit's first products are computed
+// meanwhile. The diagonal tile comes first in each unit; its soft-min runs on warps 2-3 during the rest of the
+// unit, and the next unit's diagonal tile waits until they are done with G.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -245,23 +288,28 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* a_full = bars;
+  uint64_t* a_full = bars;  // K and V of the unit in shared memory (when they do not fit in TMEM)
   uint64_t* st_full = bars + 1;
   uint64_t* st_empty = st_full + C::NS;
-  uint64_t* s_full = st_empty + C::NS;  // [NSLOT] S and dP of the job in the slot are ready
-  uint64_t* p_full = s_full + C::NSLOT;  // [NSLOT] the group of the job in the slot has written its P / dS
-  uint64_t* acc_done = p_full + C::NSLOT;
-  uint64_t* drain = acc_done + 1;
-  uint64_t* at_full = drain + 1;        // stationary operands written into TMEM by the row threads
-  uint64_t* g_full = at_full + 1;       // the diagonal tile's g is in shared memory (fused diagonal soft-min)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
+  uint64_t* s_full = st_empty + C::NS;     // [NSLOT] S and dP of the job in the slot are ready
+  uint64_t* p_full = s_full + C::NSLOT;    // [NSLOT] the group of the job in the slot has written its P / dS
+  uint64_t* acc_done = p_full + C::NSLOT;  // every MMA of the unit has completed (dV, dK final)
+  uint64_t* acc_free = acc_done + 1;       // the row threads have read dV and dK out of TMEM
+  uint64_t* drain = acc_free + 1;
+  uint64_t* at_full = drain + 1;  // K and V rows of the unit in TMEM
+  uint64_t* x_full = at_full + 1;  // K and V tiles of the unit in the staging buffer
+  uint64_t* x_empty = x_full + 1;  // the row threads have copied the staging buffer
+  uint64_t* g_full = x_empty + 1;  // the diagonal tile's g is in shared memory (fused diagonal soft-min)
+  uint64_t* g_free = g_full + 1;   // warps 2-3 are done with it
+  uint64_t* u_full = g_free + 1;   // [kUQ] unit ids handed from the producer to the other warps
+  uint64_t* u_empty = u_full + kUQ;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + kUQ);
+  int* uq = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbh = p.B * p.H;
-  const int j = int(blockIdx.x) / nbh;  // key tile 0 has the most query tiles: first in launch order
-  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
-  const int nsteps = p.NB - j;
+  const int nunits = p.NB * nbh;
   // K and V as TMEM operands of S^T and dP^T (both stationary) when the columns fit.
   constexpr bool AT = C::AT;
   constexpr int COL_K = C::COL_X, COL_V = COL_K + D / 2;
@@ -277,9 +325,17 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       mbar_init(p_full + x, kGroupThreads);
     }
     mbar_init(acc_done, 1);
+    mbar_init(acc_free, kRowThreads);
     mbar_init(drain, 1);
     mbar_init(at_full, kRowThreads);
+    mbar_init(x_full, 1);
+    mbar_init(x_empty, kRowThreads);
     mbar_init(g_full, kRowThreads);
+    mbar_init(g_free, 64);
+    for (int x = 0; x < kUQ; ++x) {
+      mbar_init(u_full + x, 1);
+      mbar_init(u_empty + x, 1 + kRowThreads / 32 + (C::FUSEDIAG ? 2 : 0));  // MMA, row and soft-min warps
+    }
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -287,10 +343,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const size_t zb = size_t(z) * p.TP;
-  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
-  // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
-  if (warp < kRowWarp0) regs_producer();
+  if (warp < kRowWarp0) regs_producer<D>();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -298,85 +351,142 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
-      if constexpr (!AT) {
-        mbar_expect_tx(a_full, 2 * C::TILEB);
-        for (int bx = 0; bx < C::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
-          tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
-        }
-      }
     }
     __syncwarp();
     bool ok = true;
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS, i = j + k;
-      if (k >= C::NS) ok = mbar_wait(st_empty + st, ((k / C::NS) - 1) & 1, p.status, 101);
+    int gk = 0, nx = 0;  // tiles and staged units issued so far
+    for (int u = 0; ok; ++u) {
+      const int us = u % kUQ;
+      if (u >= kUQ) ok = mbar_wait(u_empty + us, ((u / kUQ) - 1) & 1, p.status, 134);
       if (!ok) break;
-      if (elect_one()) {
-        uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
-        mbar_expect_tx(st_full + st, 2 * C::TILEB + 6 * C::VECB);
-        for (int bx = 0; bx < C::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, st_full + st);
-          tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b,
-                      st_full + st);
-        }
-        const size_t off = zb + size_t(i) * kBT;
-        bulk_load(vec, p.qv4 + off, 4 * C::VECB, st_full + st);
-        bulk_load(vec + 4 * C::VECB, p.prel + off, C::VECB, st_full + st);
-        bulk_load(vec + 5 * C::VECB, p.phi + off, C::VECB, st_full + st);
+      int x = 0;
+      if (lane == 0) {
+        x = atomicAdd(p.sched, 1);
+        uq[us] = x;
+        mbar_arrive(u_full + us);
       }
-      __syncwarp();
+      x = __shfl_sync(0xffffffffu, x, 0);
+      if (x >= nunits) break;
+      const int j = x / nbh, z = x % nbh, b = z / p.H, h = z % p.H;
+      const size_t zb = size_t(z) * p.TP;
+      const int nsteps = p.NB - j;
+      if constexpr (AT) {
+        if (nx > 0) ok = mbar_wait(x_empty, (nx - 1) & 1, p.status, 131);
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_expect_tx(x_full, 2 * C::TILEB);
+          for (int bx = 0; bx < C::NBOX; ++bx) {
+            tma_load_4d(smem + C::OFF_X + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, x_full);
+            tma_load_4d(smem + C::OFF_X + C::TILEB + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, x_full);
+          }
+        }
+        __syncwarp();
+        ++nx;
+      }
+      // Without room in TMEM, K and V go to shared memory, after the unit's first tiles and once every MMA of the
+      // previous unit (the last readers of that memory) has completed.
+      const int kst = nsteps < C::NS ? nsteps : C::NS;
+      for (int k = 0; k <= nsteps && ok; ++k) {
+        if (!AT && k == kst) {
+          if (u > 0) ok = mbar_wait(acc_done, (u - 1) & 1, p.status, 102);
+          if (!ok) break;
+          if (elect_one()) {
+            mbar_expect_tx(a_full, 2 * C::TILEB);
+            for (int bx = 0; bx < C::NBOX; ++bx) {
+              tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
+              tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
+            }
+          }
+          __syncwarp();
+          ++nx;
+        }
+        if (k == nsteps) break;
+        const int st = gk % C::NS, i = j + k;
+        if (gk >= C::NS) ok = mbar_wait(st_empty + st, ((gk / C::NS) - 1) & 1, p.status, 101);
+        if (!ok) break;
+        if (elect_one()) {
+          uint8_t* vec = smem + C::OFF_VEC + st * C::VECSTAGE;
+          mbar_expect_tx(st_full + st, 2 * C::TILEB + 6 * C::VECB);
+          for (int bx = 0; bx < C::NBOX; ++bx) {
+            tma_load_4d(smem + C::OFF_S1 + st * C::TILEB + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b,
+                        st_full + st);
+            tma_load_4d(smem + C::OFF_S2 + st * C::TILEB + bx * C::BOXB, &tdo, bx * C::BOXC, i * kBT, h, b,
+                        st_full + st);
+          }
+          const size_t off = zb + size_t(i) * kBT;
+          bulk_load(vec, p.qv4 + off, 4 * C::VECB, st_full + st);
+          bulk_load(vec + 4 * C::VECB, p.prel + off, C::VECB, st_full + st);
+          bulk_load(vec + 5 * C::VECB, p.phi + off, C::VECB, st_full + st);
+        }
+        __syncwarp();
+        ++gk;
+      }
     }
-    if constexpr (!AT) mbar_wait(a_full, 0, p.status, 102);
-    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k)
-      mbar_wait(st_full + k % C::NS, (k / C::NS) & 1, p.status, 103);
+    // Nothing may land in shared memory after the CTA exits: wait for the last copies issued.
+    for (int q = (gk > C::NS ? gk - C::NS : 0); q < gk; ++q) mbar_wait(st_full + q % C::NS, (q / C::NS) & 1, p.status, 103);
+    if (nx > 0) mbar_wait(AT ? x_full : a_full, (nx - 1) & 1, p.status, 104);
   } else if (warp == kWarpMma) {
-    // Jobs n = 2 k + g in order (query tile k, row group g = query columns [64 g, 64 g + 64)). S^T and dP^T of job
-    // n go into slot n % NSLOT; once the group has written P^T and dS^T there, dV += P^T dO and dK += dS^T Q over
-    // its 64 queries, then the products of job n + NSLOT into the same slot (tcgen05.mma from one thread execute
-    // in order, so the reads come first).
+    // Jobs n = 2 k + g of a unit in order (query tile k, row group g = query columns [64 g, 64 g + 64)); with gn
+    // jobs before the unit, S^T and dP^T of job n go into slot (gn + n) % NSLOT; once the group has written P^T and
+    // dS^T there, dV += P^T dO and dK += dS^T Q over its 64 queries, then the products of job n + NSLOT into the
+    // same slot (tcgen05.mma from one thread execute in order, so the reads come first). The first products of a
+    // unit overwrite dV and dK, so they wait until the rows have read the previous unit's.
     const uint32_t sa = smem_u32(smem + C::OFF_A), sb = smem_u32(smem + C::OFF_B);
     const uint32_t s1 = smem_u32(smem + C::OFF_S1), s2 = smem_u32(smem + C::OFF_S2);
-    const int njobs = 2 * nsteps;
-    auto issue_s = [&](int n) {
-      const int g = n & 1, st = (n >> 1) % C::NS;
-      const uint32_t dcol = tmem + (n % C::NSLOT) * 128;
-      const uint32_t bq = s1 + st * C::TILEB + g * kHalf * C::SWB, bdo = s2 + st * C::TILEB + g * kHalf * C::SWB;
-      if constexpr (AT) {
-        issue_ts_k<D>(dcol, tmem + COL_K, bq);              // S^T  = K Q^T
-        issue_ts_k<D>(dcol + kHalf, tmem + COL_V, bdo);     // dP^T = V dO^T
-      } else {
-        issue_ss_half<D>(dcol, sa, bq);
-        issue_ss_half<D>(dcol + kHalf, sb, bdo);
-      }
-      mma_commit_w(s_full + n % C::NSLOT);
-    };
-    bool ok = AT ? mbar_wait(at_full, 0, p.status, 115) : mbar_wait(a_full, 0, p.status, 110);
-    int loaded = -1;  // streamed tiles known to be in shared memory: 0 .. loaded
-    auto need_tile = [&](int kt) {
-      if (ok && kt > loaded) {
-        ok = mbar_wait(st_full + kt % C::NS, (kt / C::NS) & 1, p.status, 111);
-        loaded = kt;
-        tc_fence_after();
-      }
-      return ok;
-    };
-    tc_fence_after();
-    for (int n = 0; n < C::NSLOT && n < njobs; ++n)
-      if (need_tile(n >> 1)) issue_s(n);
-    for (int n = 0; n < njobs && ok; ++n) {
-      const int g = n & 1, k = n >> 1, st = k % C::NS;
-      ok = mbar_wait(p_full + n % C::NSLOT, (n / C::NSLOT) & 1, p.status, 112);
+    bool ok = true;
+    int gn = 0, gk = 0, loaded = -1;
+    for (int u = 0; ok; ++u) {
+      const int us = u % kUQ;
+      ok = mbar_wait(u_full + us, (u / kUQ) & 1, p.status, 132);
       if (!ok) break;
+      const int x = uq[us];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(u_empty + us);
+      if (x >= nunits) break;
+      const int njobs = 2 * (p.NB - x / nbh);
+      auto need_tile = [&](int kt) {
+        const int gt = gk + kt;
+        if (ok && gt > loaded) {
+          ok = mbar_wait(st_full + gt % C::NS, (gt / C::NS) & 1, p.status, 111);
+          loaded = gt;
+          tc_fence_after();
+        }
+        return ok;
+      };
+      auto issue_s = [&](int n) {
+        const int g = n & 1, st = (gk + (n >> 1)) % C::NS, sl = (gn + n) % C::NSLOT;
+        const uint32_t dcol = tmem + sl * 128;
+        const uint32_t bq = s1 + st * C::TILEB + g * kHalf * C::SWB, bdo = s2 + st * C::TILEB + g * kHalf * C::SWB;
+        if constexpr (AT) {
+          issue_ts_k<D>(dcol, tmem + COL_K, bq);              // S^T  = K Q^T
+          issue_ts_k<D>(dcol + kHalf, tmem + COL_V, bdo);     // dP^T = V dO^T
+        } else {
+          issue_ss_half<D>(dcol, sa, bq);
+          issue_ss_half<D>(dcol + kHalf, sb, bdo);
+        }
+        mma_commit_w(s_full + sl);
+      };
+      ok = AT ? mbar_wait(at_full, u & 1, p.status, 115) : mbar_wait(a_full, u & 1, p.status, 110);
       tc_fence_after();
-      const uint32_t acol = tmem + (n % C::NSLOT) * 128;
-      issue_ts_half<D>(tmem + C::COL_A1, acol, s2 + st * C::TILEB, g, n > 0);          // dV += P^T dO
-      issue_ts_half<D>(tmem + C::COL_A2, acol + kHalf, s1 + st * C::TILEB, g, n > 0);  // dK += dS^T Q
-      if (g == 1) mma_commit_w(st_empty + st);
-      const int m = n + C::NSLOT;
-      if (m < njobs && need_tile(m >> 1)) issue_s(m);
+      for (int n = 0; n < C::NSLOT && n < njobs; ++n)
+        if (need_tile(n >> 1)) issue_s(n);
+      for (int n = 0; n < njobs && ok; ++n) {
+        const int g = n & 1, st = (gk + (n >> 1)) % C::NS, sl = (gn + n) % C::NSLOT;
+        ok = mbar_wait(p_full + sl, ((gn + n) / C::NSLOT) & 1, p.status, 112);
+        if (ok && n == 0 && u > 0) ok = mbar_wait(acc_free, (u - 1) & 1, p.status, 116);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t acol = tmem + sl * 128;
+        issue_ts_half<D>(tmem + C::COL_A1, acol, s2 + st * C::TILEB, g, n > 0);          // dV += P^T dO
+        issue_ts_half<D>(tmem + C::COL_A2, acol + kHalf, s1 + st * C::TILEB, g, n > 0);  // dK += dS^T Q
+        if (g == 1) mma_commit_w(st_empty + st);
+        const int m = n + C::NSLOT;
+        if (m < njobs && need_tile(m >> 1)) issue_s(m);
+      }
+      mma_commit_w(acc_done);
+      gn += njobs;
+      gk += njobs / 2;
     }
-    mma_commit_w(acc_done);
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 114);
   } else if (C::FUSEDIAG && (warp == 2 || warp == 3)) {
@@ -403,374 +513,445 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     float* es = a2s + kBT;
     float* mm = es + kBT;  // per-warp maximum and minimum of a2 over the tile's positions
     const int wt = threadIdx.x - 64;
-    const int tend = min(kBT, p.T - j * kBT);
-    float vmax = -kInf, vmin = kInf;
-    for (int t = wt; t < kBT; t += 64) {
-      const float a = -p.phi[zb + size_t(j) * kBT + t] * p.il2;  // phi = +inf beyond T
-      a2s[t] = a;
-      if (t < tend) {
-        vmax = fmaxf(vmax, a);
-        vmin = fminf(vmin, a);
+    bool ok = true;
+    for (int u = 0;; ++u) {
+      const int us = u % kUQ;
+      int x = nunits;
+      if (ok) ok = mbar_wait(u_full + us, (u / kUQ) & 1, p.status, 133);
+      if (ok) x = uq[us];
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(u_empty + us);
+      if (!diag_all(ok && x < nunits)) break;
+      const int j = x / nbh, z = x % nbh;
+      const size_t zb = size_t(z) * p.TP;
+      const int tend = min(kBT, p.T - j * kBT);
+      float vmax = -kInf, vmin = kInf;
+      for (int t = wt; t < kBT; t += 64) {
+        const float a = -p.phi[zb + size_t(j) * kBT + t] * p.il2;  // phi = +inf beyond T
+        a2s[t] = a;
+        if (t < tend) {
+          vmax = fmaxf(vmax, a);
+          vmin = fminf(vmin, a);
+        }
       }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
-      vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
-    }
-    if (lane == 0) {
-      mm[2 * (warp - 2)] = vmax;
-      mm[2 * (warp - 2) + 1] = vmin;
-    }
-    asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
-    const float M = fmaxf(mm[0], mm[2]);
-    const bool fast = M - fminf(mm[1], mm[3]) <= kSpan;  // the same for all 64 threads
-    if (fast) {
-      for (int t = wt; t < kBT; t += 64) es[t] = t < tend ? ex2(a2s[t] - M) : 0.f;
+      for (int o = 16; o > 0; o >>= 1) {
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+        vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
+      }
+      if (lane == 0) {
+        mm[2 * (warp - 2)] = vmax;
+        mm[2 * (warp - 2) + 1] = vmin;
+      }
       asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
-    }
-    bool ok = mbar_wait(g_full, 0, p.status, 130);
-    if (ok && fast) {
+      const float M = fmaxf(mm[0], mm[2]);
+      const bool fast = M - fminf(mm[1], mm[3]) <= kSpan;  // the same for all 64 threads
+      if (fast) {
+        for (int t = wt; t < kBT; t += 64) es[t] = t < tend ? ex2(a2s[t] - M) : 0.f;
+        asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+      }
+      ok = mbar_wait(g_full, u & 1, p.status, 130);
+      if (ok && fast) {
 #pragma unroll 1
-      for (int q = 0; q < 2; ++q) {
-        const int s = q == 0 ? wt : kBT - 1 - wt;
-        float* row = G + s * LD;
-        float S = 0.f;
+        for (int q = 0; q < 2; ++q) {
+          const int s = q == 0 ? wt : kBT - 1 - wt;
+          float* row = G + s * LD;
+          float S = 0.f;
 #pragma unroll 1
-        for (int t0 = s + 1; t0 < tend; t0 += kRun) {
-          float ev[kRun], gv[kRun];
+          for (int t0 = s + 1; t0 < tend; t0 += kRun) {
+            float ev[kRun], gv[kRun];
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            const bool in = t0 + e < tend;
-            ev[e] = in ? es[t0 + e] : 0.f;
-            gv[e] = in ? row[t0 + e] : 0.f;
+            for (int e = 0; e < kRun; ++e) {
+              const bool in = t0 + e < tend;
+              ev[e] = in ? es[t0 + e] : 0.f;
+              gv[e] = in ? row[t0 + e] : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e) {
+              S += ev[e];
+              gv[e] *= rcp_approx(S);
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e)
+              if (t0 + e < tend) row[t0 + e] = gv[e];
           }
+          float K = 0.f;
+#pragma unroll 1
+          for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
+            float rv[kRun];
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            S += ev[e];
-            gv[e] *= rcp_approx(S);
+            for (int e = 0; e < kRun; ++e) rv[e] = t1 - e > s ? row[t1 - e] : 0.f;
+#pragma unroll
+            for (int e = 0; e < kRun; ++e) {
+              K += rv[e];
+              rv[e] = K;
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e)
+              if (t1 - e > s) row[t1 - e] = rv[e];
           }
-#pragma unroll
-          for (int e = 0; e < kRun; ++e)
-            if (t0 + e < tend) row[t0 + e] = gv[e];
         }
-        float K = 0.f;
+      } else if (ok) {
 #pragma unroll 1
-        for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
-          float rv[kRun];
+        for (int q = 0; q < 2; ++q) {
+          const int s = q == 0 ? wt : kBT - 1 - wt;
+          float mz = -kInf, zz = 0.f;
+#pragma unroll 1
+          for (int t0 = s + 1; t0 < tend; t0 += kRun) {
+            float at[kRun], wv[kRun];
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) rv[e] = t1 - e > s ? row[t1 - e] : 0.f;
+            for (int e = 0; e < kRun; ++e) at[e] = t0 + e < tend ? a2s[t0 + e] : -kInf;
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            K += rv[e];
-            rv[e] = K;
+            for (int e = 0; e < kRun; ++e) {
+              const float dd = at[e] - mz;
+              const bool up = dd > 0.f;
+              const float ee = ex2(-fabsf(dd));
+              zz = fmaf(zz, up ? ee : 1.f, up ? 1.f : ee);
+              mz = fmaxf(mz, at[e]);
+              wv[e] = (up ? 1.f : ee) * rcp_approx(zz);
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e)
+              if (t0 + e < tend) G[(t0 + e) * LD + s] = wv[e];
           }
+          float H = 0.f, wn = 0.f;
+#pragma unroll 1
+          for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
+            float w[kRun], g[kRun];
 #pragma unroll
-          for (int e = 0; e < kRun; ++e)
-            if (t1 - e > s) row[t1 - e] = rv[e];
+            for (int e = 0; e < kRun; ++e) {
+              const bool in = t1 - e > s;
+              w[e] = in ? G[(t1 - e) * LD + s] : 0.f;
+              g[e] = in ? G[s * LD + t1 - e] : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e) {
+              H = fmaf(1.f - wn, H, g[e]);
+              g[e] = w[e] * H;
+              wn = w[e];
+            }
+#pragma unroll
+            for (int e = 0; e < kRun; ++e)
+              if (t1 - e > s) G[s * LD + t1 - e] = g[e];
+          }
         }
       }
-    } else if (ok) {
+      asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
+      if (ok) {
 #pragma unroll 1
-      for (int q = 0; q < 2; ++q) {
-        const int s = q == 0 ? wt : kBT - 1 - wt;
-        float mz = -kInf, zz = 0.f;
-#pragma unroll 1
-        for (int t0 = s + 1; t0 < tend; t0 += kRun) {
-          float at[kRun], wv[kRun];
+        for (int q = 0; q < 2; ++q) {
+          const int u = q == 0 ? wt : kBT - 1 - wt;
+          if (u < tend) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};  // keys s = 0, 1, 2, 3 mod 4, joined in a fixed order
+            int s2 = 0;
+            for (; s2 + 4 <= u; s2 += 4) {
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) at[e] = t0 + e < tend ? a2s[t0 + e] : -kInf;
+              for (int e = 0; e < 4; ++e) acc[e] += G[(s2 + e) * LD + u];
+            }
 #pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            const float dd = at[e] - mz;
-            const bool up = dd > 0.f;
-            const float ee = ex2(-fabsf(dd));
-            zz = fmaf(zz, up ? ee : 1.f, up ? 1.f : ee);
-            mz = fmaxf(mz, at[e]);
-            wv[e] = (up ? 1.f : ee) * rcp_approx(zz);
+            for (int e = 0; e < 3; ++e)
+              if (s2 + e < u) acc[e] += G[(s2 + e) * LD + u];
+            const float col = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+            p.dphi4[zb + size_t(j) * kBT + u] = fast ? es[u] * col : col;
           }
-#pragma unroll
-          for (int e = 0; e < kRun; ++e)
-            if (t0 + e < tend) G[(t0 + e) * LD + s] = wv[e];
-        }
-        float H = 0.f, wn = 0.f;
-#pragma unroll 1
-        for (int t1 = tend - 1; t1 > s; t1 -= kRun) {
-          float w[kRun], g[kRun];
-#pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            const bool in = t1 - e > s;
-            w[e] = in ? G[(t1 - e) * LD + s] : 0.f;
-            g[e] = in ? G[s * LD + t1 - e] : 0.f;
-          }
-#pragma unroll
-          for (int e = 0; e < kRun; ++e) {
-            H = fmaf(1.f - wn, H, g[e]);
-            g[e] = w[e] * H;
-            wn = w[e];
-          }
-#pragma unroll
-          for (int e = 0; e < kRun; ++e)
-            if (t1 - e > s) G[s * LD + t1 - e] = g[e];
         }
       }
-    }
-    asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
-    if (ok) {
-#pragma unroll 1
-      for (int q = 0; q < 2; ++q) {
-        const int u = q == 0 ? wt : kBT - 1 - wt;
-        if (u < tend) {
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};  // keys s = 0, 1, 2, 3 mod 4, joined in a fixed order
-          int s2 = 0;
-          for (; s2 + 4 <= u; s2 += 4) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[e] += G[(s2 + e) * LD + u];
-          }
-#pragma unroll
-          for (int e = 0; e < 3; ++e)
-            if (s2 + e < u) acc[e] += G[(s2 + e) * LD + u];
-          const float col = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-          p.dphi4[zb + size_t(j) * kBT + u] = fast ? es[u] * col : col;
-        }
-      }
+      asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");  // G, a2s, es, mm are reused
+      mbar_arrive(g_free);
     }
   } else if (warp >= kRowWarp0) {
-    regs_rows();
+    regs_rows<D>();
     const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
     const int r = wr * 32 + lane;  // key within the tile = TMEM lane
     const int cb = grp * kHalf;    // this group's query columns [cb, cb + 64)
-    const int s = j * kBT + r;
-    const bool s_ok = s < p.T;
     const uint32_t tl = tmem + (uint32_t(wr * 32) << 16);
-    if constexpr (AT) {
-      // Group 0 writes the key's row of K, group 1 its row of V, into TMEM.
-      const __half* row = grp == 0 ? p.k + b * p.k_s[0] + h * p.k_s[1] + int64_t(s_ok ? s : 0) * p.k_s[2]
-                                   : p.v + b * p.v_s[0] + h * p.v_s[1] + int64_t(s_ok ? s : 0) * p.v_s[2];
-      row_to_tmem<D>(tl + (grp == 0 ? COL_K : COL_V), row, s_ok);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(at_full);
-    }
-    const float bh = p.beta[h], betal = bh * kLog2e;
-    const float psi_s = p.psi[zb + s];
-    const float xs_s = p.xs[zb + s];  // SUF_s - psi_s (+inf for the last key of the tile)
-    const float suf_s = p.suf[zb + s];
-    const float sufl_s = p.sufl[zb + s];
-    const float c2_s = suf_s < kInf ? -suf_s * p.il2 : -kInf;
-    const float* bmin = p.bmin + size_t(z) * p.NB;
-    const float* bl = p.bl + size_t(z) * p.NB;
-    const float2 sc2 = make_float2(p.scale2, p.scale2), bet2 = make_float2(betal, betal);
-    const float2 npsi2 = make_float2(-psi_s, -psi_s);
-    float gsum = 0.f, dbsum = 0.f, wsum = 0.f;
-    float2 gsum2 = make_float2(0.f, 0.f), dbsum2 = make_float2(0.f, 0.f);
-    float mid = kInf, midl = -kInf;
-    bool ok = true;
-    // Per-tile scalars of query tile i, loaded one tile ahead so their latency hides behind the element work.
-    const float* prer = p.prer + size_t(z) * p.NB;
-    float bl_n = bl[j], bmin_n = bmin[j], prer_n = prer[j];
-    for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS, i = j + k;
-      const float bli = bl_n, bmini = bmin_n, preri = prer_n;
-      if (i + 1 < p.NB) {
-        bl_n = bl[i + 1];
-        bmin_n = bmin[i + 1];
-        prer_n = prer[i + 1];
-      }
-      const int n = 2 * k + grp, slot = n % C::NSLOT;
-      ok = mbar_wait(st_full + st, (k / C::NS) & 1, p.status, 120);
-      if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 121);
-      if (!ok) break;
-      tc_fence_after();
-      // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
-      // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
-      const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
-      const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
-      const float4* QV = reinterpret_cast<const float4*>(vbase);  // query pairs: (-lse, -delta), (PRE, prey)
-      const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
-      const float* vphi = reinterpret_cast<const float*>(vbase + 5 * C::VECB);
-      const bool diag = k == 0;
-      const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
-      float rs = fmaxf(c2_s, cmid2);
-      const bool vrs = !diag && rs > -kInf;
-      rs = vrs ? rs : 0.f;
-      const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
-      // 2^{PREL_t - rs} = prey_t * 2^{BL_i - rs} when both factors stay in range (no exp2 per element).
-      // Warp-uniform: the chunk body holds warp-collective TMEM loads and stores, so the whole warp takes the
-      // factorised path or none of it does.
-      const bool fact = __all_sync(0xffffffffu, vrs && preri <= 120.f && bli - rs <= 120.f);
-      const float xfac = fact ? ex2(bli - rs) : 0.f;
-      const float2 xf2 = make_float2(xfac, xfac), sv2 = make_float2(sv_, sv_);
-      const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
-      // Off the diagonal x_ts = min(a_s, PRE_t - psi_s) with a_s = min(SUF_s - psi_s, mid - psi_s): x_ts <= 0 iff
-      // a_s <= 0 or PRE_t <= psi_s, and min(x_ts, 0) = min(min(a_s, 0), PRE_t - psi_s).
-      const float a_s = fminf(xs_s, mid - psi_s);
-      const float am = fminf(a_s, 0.f);
-      const bool pa = a_s <= 0.f;
-      // Diagonal tile: rr = min phi over (key, query]; the second group starts from the minimum over (key, 63].
-      float rr = kInf;
-      if (diag && grp == 1)
-        for (int c = 0; c < kHalf; ++c)
-          if (c > r) rr = fminf(rr, vphi[c]);
-      float2 fsum2 = make_float2(0.f, 0.f);
-      float* grow = C::FUSEDIAG ? nullptr : p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
-      // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
-      // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal
-      // two queries are handled per step with packed f32x2 arithmetic.
-      auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
-        constexpr bool DIAG = decltype(diag_tag)::value;
-        constexpr bool FACT = decltype(fact_tag)::value;
-        uint32_t ppk[8], dpk[8];
-        if constexpr (DIAG) {
-          float gb[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int c = c0 + e;
-            const float4 va = QV[c0 + (e & ~1)];
-            const float nl = (e & 1) ? va.y : va.x, nd = (e & 1) ? va.w : va.z;
-            rr = c > r ? fminf(rr, vphi[c]) : rr;
-            const float x = rr - psi_s;  // +inf for c <= r
-            const float xm = fminf(x, 0.f);
-            const float sv = fmaf(sS[e], p.scale2, betal * xm);
-            const bool valid = s_ok && c >= r && c < tvalid;
-            const float pp = valid ? ex2(sv + nl) : 0.f;
-            const float ds = valid ? pp * (sP[e] + nd) : 0.f;
-            const float g = x <= 0.f ? ds : 0.f;
-            gsum += g;
-            dbsum = fmaf(ds, xm, dbsum);
-            gb[e] = g;
-            sS[e] = pp;
-            sP[e] = ds;
-          }
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
-            dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
-          }
-          if constexpr (C::FUSEDIAG) {
-            float* grs = reinterpret_cast<float*>(smem + C::OFF_G) + r * C::GLD + c0;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) grs[e] = gb[e];
-          } else {
-            float4* dst = reinterpret_cast<float4*>(grow + c0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float4 va = QV[c0 + e];      // (-lse_c, -lse_c1, -delta_c, -delta_c1)
-            const float4 vb = QV[c0 + e + 1];  // (PRE_c, PRE_c1, prey_c, prey_c1)
-            const float2 dd = __fadd2_rn(make_float2(vb.x, vb.y), npsi2);
-            const float2 xm = make_float2(fminf(am, dd.x), fminf(am, dd.y));
-            const bool in0 = pa || dd.x <= 0.f, in1 = pa || dd.y <= 0.f;
-            float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
-            sv = __fadd2_rn(sv, make_float2(va.x, va.y));
-            const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
-            const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), make_float2(va.z, va.w)));
-            const float2 g = make_float2(in0 ? ds.x : 0.f, in1 ? ds.y : 0.f);
-            gsum2 = __fadd2_rn(gsum2, g);
-            dbsum2 = __ffma2_rn(ds, xm, dbsum2);
-            float2 den;
-            if constexpr (FACT)
-              den = __ffma2_rn(make_float2(vb.z, vb.w), xf2, sv2);
-            else
-              den = make_float2(sv_ + ex2(vprel[c0 + e] - rs), sv_ + ex2(vprel[c0 + e + 1] - rs));
-            fsum2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), fsum2);
-            ppk[e / 2] = pack_half2(pp.x, pp.y);
-            dpk[e / 2] = pack_half2(ds.x, ds.y);
-          }
-        }
-        tmem_st8(tS + c0, ppk);
-        tmem_st8(tP + c0, dpk);
-      };
-      // The group's four chunks, ascending, with the TMEM loads of the next chunk in flight during the current one.
-      auto tile = [&](auto diag_tag, auto fact_tag) {
-        float sA[16], pA[16], sB[16], pB[16];
-        tmem_ld16(tS + cb, sA);
-        tmem_ld16(tP + cb, pA);
-        tmem_ld_wait_regs(sA, pA);
-#pragma unroll
-        for (int q = 0; q < kHalf / 16; q += 2) {
-          const int c0 = cb + 16 * q;
-          tmem_ld16(tS + c0 + 16, sB);
-          tmem_ld16(tP + c0 + 16, pB);
-          chunk(c0, sA, pA, diag_tag, fact_tag);
-          tmem_ld_wait_regs(sB, pB);
-          if (q + 2 < kHalf / 16) {
-            tmem_ld16(tS + c0 + 32, sA);
-            tmem_ld16(tP + c0 + 32, pA);
-          }
-          chunk(c0 + 16, sB, pB, diag_tag, fact_tag);
-          if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
-        }
-      };
-      if (diag)
-        tile(std::true_type{}, std::false_type{});
-      else if (fact)
-        tile(std::false_type{}, std::true_type{});
-      else
-        tile(std::false_type{}, std::false_type{});
-      if (C::FUSEDIAG && diag) mbar_arrive(g_full);  // release: the g columns written above
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full + slot);
-      if (!diag) {
-        const float fsum = vrs ? fsum2.x + fsum2.y : 0.f;
-        if (vrs) wsum += ex2(c2_s - rs) * fsum;
-        if (i > j + 1) {
-          // Tile-pair total: one partial per warp (8 per pair), summed in a fixed order by the dphi kernel.
-          const float tot = group_sum<32>(vrs ? ex2(cmid2 - rs) * fsum : 0.f);
-          if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + (warp - kRowWarp0)] = tot;
-        }
-        mid = fminf(mid, bmini);
-        midl = lse2(midl, bli);
-      }
-    }
-    gsum += gsum2.x + gsum2.y;
-    dbsum += dbsum2.x + dbsum2.y;
-    // Join the two groups' per-key sums (fixed order: group 0 + group 1).
+    constexpr int DH = D >= 32 ? D / 2 : D;  // head-dim columns of dV and dK stored by each group
+    const float2 sc2 = make_float2(p.scale2, p.scale2);
     float* xg = red + 32;
     float* xw = red + 32 + kBT;
-    if (grp == 1) {
-      xg[r] = gsum;
-      xw[r] = wsum;
-    }
-    rows_sync();
-    if (ok) ok = mbar_wait(acc_done, 0, p.status, 122);
-    if (ok) {
-      tc_fence_after();
-      __half* dvrow = p.dv + b * p.dv_s[0] + h * p.dv_s[1] + int64_t(s_ok ? s : 0) * p.dv_s[2];
-      __half* dkrow = p.dk + b * p.dk_s[0] + h * p.dk_s[1] + int64_t(s_ok ? s : 0) * p.dk_s[2];
-      constexpr int DH = D >= 32 ? D / 2 : D;  // head-dim columns stored by each group
-      if (D >= 32 || grp == 0) {
-#pragma unroll
-        for (int c = grp * DH; c < grp * DH + DH; c += 16) {
-          float a1[16], a2[16];
-          tmem_ld16(tl + C::COL_A1 + c, a1);
-          tmem_ld16(tl + C::COL_A2 + c, a2);
-          tmem_ld_wait();
-          if (s_ok) {
-            uint32_t u1[8], u2[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              u1[e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
-              u2[e] = pack_half2(a2[2 * e] * p.scale, a2[2 * e + 1] * p.scale);
-            }
-            reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(u1[0], u1[1], u1[2], u1[3]);
-            reinterpret_cast<uint4*>(dvrow + c)[1] = make_uint4(u1[4], u1[5], u1[6], u1[7]);
-            reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(u2[0], u2[1], u2[2], u2[3]);
-            reinterpret_cast<uint4*>(dkrow + c)[1] = make_uint4(u2[4], u2[5], u2[6], u2[7]);
+    bool ok = true;
+    int gn = 0, gk = 0;
+    // The finished unit, written out after the next unit's K and V rows are in TMEM.
+    bool have_prev = false, pv_done = false, pv_ok = false;
+    int pv_s = 0, pv_j = 0, pv_b = 0, pv_h = 0, pv_z = 0;
+    float pv_g = 0.f, pv_db = 0.f, pv_w = 0.f, pv_bh = 0.f;
+    for (int u = 0;; ++u) {
+      const int us = u % kUQ;
+      int x = nunits;
+      if (ok) ok = mbar_wait(u_full + us, (u / kUQ) & 1, p.status, 124);
+      if (ok) x = uq[us];
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(u_empty + us);
+      const bool more = rows_all(ok && x < nunits);
+      const int j = more ? x / nbh : 0;
+      const int z = more ? x % nbh : 0, b = z / p.H, h = z % p.H;
+      const size_t zb = size_t(z) * p.TP;
+      const int s = j * kBT + r;
+      const bool s_ok = more && s < p.T;
+      // The unit's per-key and first per-tile scalars, loaded first so that their latency passes during the copy
+      // below and the previous unit's write-out.
+      float bh = 0.f, psi_s = 0.f, xs_s = 0.f, suf_s = 0.f, sufl_s = 0.f, bl_n = 0.f, bmin_n = 0.f, prer_n = 0.f;
+      if (more) {
+        bh = p.beta[h];
+        psi_s = p.psi[zb + s];
+        xs_s = p.xs[zb + s];  // SUF_s - psi_s (+inf for the last key of the tile)
+        suf_s = p.suf[zb + s];
+        sufl_s = p.sufl[zb + s];
+        bl_n = p.bl[size_t(z) * p.NB + j];
+        bmin_n = p.bmin[size_t(z) * p.NB + j];
+        prer_n = p.prer[size_t(z) * p.NB + j];
+      }
+      if constexpr (AT) {
+        if (more) {
+          // Group 0 copies the key's row of K, group 1 its row of V, into TMEM. Every MMA of the previous unit has
+          // completed (acc_done), so nothing reads those columns any more.
+          ok = mbar_wait(x_full, u & 1, p.status, 125);
+          if (ok) {
+            stage_row_to_tmem<D>(tl + (grp == 0 ? COL_K : COL_V), smem + C::OFF_X + grp * C::TILEB, r);
+            tmem_st_wait();
           }
+          tc_fence_before();
+          mbar_arrive(at_full);
+          mbar_arrive(x_empty);
         }
       }
-      if (s_ok && grp == 0) {
-        p.dpsi[size_t(z) * p.T + s] = -bh * (gsum + xg[r]);
-        p.w[zb + s] = wsum + xw[r];
+      if (have_prev) {
+        if (pv_done) {
+          tc_fence_after();
+          __half* dvrow = p.dv + pv_b * p.dv_s[0] + pv_h * p.dv_s[1] + int64_t(pv_s) * p.dv_s[2];
+          __half* dkrow = p.dk + pv_b * p.dk_s[0] + pv_h * p.dk_s[1] + int64_t(pv_s) * p.dk_s[2];
+          if (D >= 32 || grp == 0) {
+#pragma unroll
+            for (int c = grp * DH; c < grp * DH + DH; c += 16) {
+              float a1[16], a2[16];
+              tmem_ld16(tl + C::COL_A1 + c, a1);
+              tmem_ld16(tl + C::COL_A2 + c, a2);
+              tmem_ld_wait();
+              if (pv_ok) {
+                uint32_t u1[8], u2[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  u1[e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
+                  u2[e] = pack_half2(a2[2 * e] * p.scale, a2[2 * e + 1] * p.scale);
+                }
+                reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(u1[0], u1[1], u1[2], u1[3]);
+                reinterpret_cast<uint4*>(dvrow + c)[1] = make_uint4(u1[4], u1[5], u1[6], u1[7]);
+                reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(u2[0], u2[1], u2[2], u2[3]);
+                reinterpret_cast<uint4*>(dkrow + c)[1] = make_uint4(u2[4], u2[5], u2[6], u2[7]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acc_free);
+        // Join the two groups' per-key sums (fixed order: group 0 + group 1).
+        if (grp == 1) {
+          xg[r] = pv_g;
+          xw[r] = pv_w;
+        }
+        rows_sync();
+        if (pv_ok && grp == 0) {
+          p.dpsi[size_t(pv_z) * p.T + pv_s] = -pv_bh * (pv_g + xg[r]);
+          p.w[size_t(pv_z) * p.TP + pv_s] = pv_w + xw[r];
+        }
+        const float db = rows_sum(pv_db, red);  // xg, xw are next written after rows_all
+        if (threadIdx.x == kRowWarp0 * 32) p.dbeta[size_t(pv_z) * p.NB + pv_j] = db;
       }
+      if (!more) break;
+
+      const int nsteps = p.NB - j;
+      const float betal = bh * kLog2e;
+      const float c2_s = suf_s < kInf ? -suf_s * p.il2 : -kInf;
+      const float* bmin = p.bmin + size_t(z) * p.NB;
+      const float* bl = p.bl + size_t(z) * p.NB;
+      const float2 bet2 = make_float2(betal, betal);
+      const float2 npsi2 = make_float2(-psi_s, -psi_s);
+      float gsum = 0.f, dbsum = 0.f, wsum = 0.f;
+      float2 gsum2 = make_float2(0.f, 0.f), dbsum2 = make_float2(0.f, 0.f);
+      float mid = kInf, midl = -kInf;
+      // Per-tile scalars of query tile i (those of the first tile were loaded above), loaded one tile ahead so
+      // their latency hides behind the element work.
+      const float* prer = p.prer + size_t(z) * p.NB;
+      for (int k = 0; k < nsteps && ok; ++k) {
+        const int gt = gk + k, st = gt % C::NS, i = j + k;
+        const float bli = bl_n, bmini = bmin_n, preri = prer_n;
+        if (i + 1 < p.NB) {
+          bl_n = bl[i + 1];
+          bmin_n = bmin[i + 1];
+          prer_n = prer[i + 1];
+        }
+        const int n = gn + 2 * k + grp, slot = n % C::NSLOT;
+        ok = mbar_wait(st_full + st, (gt / C::NS) & 1, p.status, 120);
+        if (ok) ok = mbar_wait(s_full + slot, (n / C::NSLOT) & 1, p.status, 121);
+        if (!ok) break;
+        tc_fence_after();
+        // TMEM addresses of this job's S and dP columns, offset so that column c of the tile (cb <= c < cb + 64)
+        // is at tS + c and tP + c (unsigned wrap-around keeps the sums exact).
+        const uint32_t tS = tl + uint32_t(slot * 128) - uint32_t(cb), tP = tS + kHalf;
+        const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
+        const float4* QV = reinterpret_cast<const float4*>(vbase);  // query pairs: (-lse, -delta), (PRE, prey)
+        const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
+        const float* vphi = reinterpret_cast<const float*>(vbase + 5 * C::VECB);
+        const bool diag = k == 0;
+        const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
+        float rs = fmaxf(c2_s, cmid2);
+        const bool vrs = !diag && rs > -kInf;
+        rs = vrs ? rs : 0.f;
+        const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
+        // 2^{PREL_t - rs} = prey_t * 2^{BL_i - rs} when both factors stay in range (no exp2 per element).
+        // Warp-uniform: the chunk body holds warp-collective TMEM loads and stores, so the whole warp takes the
+        // factorised path or none of it does.
+        const bool fact = __all_sync(0xffffffffu, vrs && preri <= 120.f && bli - rs <= 120.f);
+        const float xfac = fact ? ex2(bli - rs) : 0.f;
+        const float2 xf2 = make_float2(xfac, xfac), sv2 = make_float2(sv_, sv_);
+        const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
+        // Off the diagonal x_ts = min(a_s, PRE_t - psi_s) with a_s = min(SUF_s - psi_s, mid - psi_s): x_ts <= 0 iff
+        // a_s <= 0 or PRE_t <= psi_s, and min(x_ts, 0) = min(min(a_s, 0), PRE_t - psi_s).
+        const float a_s = fminf(xs_s, mid - psi_s);
+        const float am = fminf(a_s, 0.f);
+        const bool pa = a_s <= 0.f;
+        // Diagonal tile: rr = min phi over (key, query]; the second group starts from the minimum over (key, 63].
+        float rr = kInf;
+        if (diag && grp == 1)
+          for (int c = 0; c < kHalf; ++c)
+            if (c > r) rr = fminf(rr, vphi[c]);
+        float2 fsum2 = make_float2(0.f, 0.f);
+        float* grow = C::FUSEDIAG ? nullptr : p.gd + ((size_t(z) * p.NB + j) * kBT + r) * kBT;
+        // 16 query columns per chunk: load S^T and dP^T, compute, write P^T and dS^T (fp16) over the first 8 of
+        // those 16 columns. DIAG and FACT are compile-time so the element loop has no branches; off the diagonal
+        // two queries are handled per step with packed f32x2 arithmetic.
+        auto chunk = [&](int c0, float(&sS)[16], float(&sP)[16], auto diag_tag, auto fact_tag) {
+          constexpr bool DIAG = decltype(diag_tag)::value;
+          constexpr bool FACT = decltype(fact_tag)::value;
+          uint32_t ppk[8], dpk[8];
+          if constexpr (DIAG) {
+            float gb[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int c = c0 + e;
+              const float4 va = QV[c0 + (e & ~1)];
+              const float nl = (e & 1) ? va.y : va.x, nd = (e & 1) ? va.w : va.z;
+              rr = c > r ? fminf(rr, vphi[c]) : rr;
+              const float x = rr - psi_s;  // +inf for c <= r
+              const float xm = fminf(x, 0.f);
+              const float sv = fmaf(sS[e], p.scale2, betal * xm);
+              const bool valid = s_ok && c >= r && c < tvalid;
+              const float pp = valid ? ex2(sv + nl) : 0.f;
+              const float ds = valid ? pp * (sP[e] + nd) : 0.f;
+              const float g = x <= 0.f ? ds : 0.f;
+              gsum += g;
+              dbsum = fmaf(ds, xm, dbsum);
+              gb[e] = g;
+              sS[e] = pp;
+              sP[e] = ds;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              ppk[e / 2] = pack_half2(sS[e], sS[e + 1]);
+              dpk[e / 2] = pack_half2(sP[e], sP[e + 1]);
+            }
+            if constexpr (C::FUSEDIAG) {
+              float* grs = reinterpret_cast<float*>(smem + C::OFF_G) + r * C::GLD + c0;
+#pragma unroll
+              for (int e = 0; e < 16; ++e) grs[e] = gb[e];
+            } else {
+              float4* dst = reinterpret_cast<float4*>(grow + c0);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) dst[q] = make_float4(gb[4 * q], gb[4 * q + 1], gb[4 * q + 2], gb[4 * q + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float4 va = QV[c0 + e];      // (-lse_c, -lse_c1, -delta_c, -delta_c1)
+              const float4 vb = QV[c0 + e + 1];  // (PRE_c, PRE_c1, prey_c, prey_c1)
+              const float2 dd = __fadd2_rn(make_float2(vb.x, vb.y), npsi2);
+              const float2 xm = make_float2(fminf(am, dd.x), fminf(am, dd.y));
+              const bool in0 = pa || dd.x <= 0.f, in1 = pa || dd.y <= 0.f;
+              float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
+              sv = __fadd2_rn(sv, make_float2(va.x, va.y));
+              const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
+              const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), make_float2(va.z, va.w)));
+              const float2 g = make_float2(in0 ? ds.x : 0.f, in1 ? ds.y : 0.f);
+              gsum2 = __fadd2_rn(gsum2, g);
+              dbsum2 = __ffma2_rn(ds, xm, dbsum2);
+              float2 den;
+              if constexpr (FACT)
+                den = __ffma2_rn(make_float2(vb.z, vb.w), xf2, sv2);
+              else
+                den = make_float2(sv_ + ex2(vprel[c0 + e] - rs), sv_ + ex2(vprel[c0 + e + 1] - rs));
+              fsum2 = __ffma2_rn(g, make_float2(rcp_approx(den.x), rcp_approx(den.y)), fsum2);
+              ppk[e / 2] = pack_half2(pp.x, pp.y);
+              dpk[e / 2] = pack_half2(ds.x, ds.y);
+            }
+          }
+          tmem_st8(tS + c0, ppk);
+          tmem_st8(tP + c0, dpk);
+        };
+        // The group's four chunks, ascending, with the TMEM loads of the next chunk in flight during the current one.
+        auto tile = [&](auto diag_tag, auto fact_tag) {
+          float sA[16], pA[16], sB[16], pB[16];
+          tmem_ld16(tS + cb, sA);
+          tmem_ld16(tP + cb, pA);
+          tmem_ld_wait_regs(sA, pA);
+#pragma unroll
+          for (int q = 0; q < kHalf / 16; q += 2) {
+            const int c0 = cb + 16 * q;
+            tmem_ld16(tS + c0 + 16, sB);
+            tmem_ld16(tP + c0 + 16, pB);
+            chunk(c0, sA, pA, diag_tag, fact_tag);
+            tmem_ld_wait_regs(sB, pB);
+            if (q + 2 < kHalf / 16) {
+              tmem_ld16(tS + c0 + 32, sA);
+              tmem_ld16(tP + c0 + 32, pA);
+            }
+            chunk(c0 + 16, sB, pB, diag_tag, fact_tag);
+            if (q + 2 < kHalf / 16) tmem_ld_wait_regs(sA, pA);
+          }
+        };
+        if (diag) {
+          // The diagonal tile writes its g into G: the soft-min warps must be done with the previous unit's.
+          if (C::FUSEDIAG && u > 0) ok = mbar_wait(g_free, (u - 1) & 1, p.status, 123);
+          if (!ok) break;
+          tile(std::true_type{}, std::false_type{});
+        }
+        else if (fact)
+          tile(std::false_type{}, std::true_type{});
+        else
+          tile(std::false_type{}, std::false_type{});
+        if (C::FUSEDIAG && diag) mbar_arrive(g_full);  // release: the g columns written above
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full + slot);
+        if (!diag) {
+          const float fsum = vrs ? fsum2.x + fsum2.y : 0.f;
+          if (vrs) wsum += ex2(c2_s - rs) * fsum;
+          if (i > j + 1) {
+            // Tile-pair total: one partial per warp (8 per pair), summed in a fixed order by the dphi kernel.
+            const float tot = group_sum<32>(vrs ? ex2(cmid2 - rs) * fsum : 0.f);
+            if (lane == 0) p.tb[((size_t(z) * p.NB + i) * p.NB + j) * kTcTbParts + (warp - kRowWarp0)] = tot;
+          }
+          mid = fminf(mid, bmini);
+          midl = lse2(midl, bli);
+        }
+      }
+      gsum += gsum2.x + gsum2.y;
+      dbsum += dbsum2.x + dbsum2.y;
+      if (ok) ok = mbar_wait(acc_done, u & 1, p.status, 122);
+      have_prev = true;
+      pv_done = ok;
+      pv_ok = s_ok && ok;
+      pv_s = s;
+      pv_j = j;
+      pv_b = b;
+      pv_h = h;
+      pv_z = z;
+      pv_g = gsum;
+      pv_db = dbsum;
+      pv_w = wsum;
+      pv_bh = bh;
+      gn += 2 * nsteps;
+      gk += nsteps;
     }
-    const float db = rows_sum(dbsum, red);
-    if (threadIdx.x == kRowWarp0 * 32) p.dbeta[size_t(z) * p.NB + j] = db;
   }
   tc_fence_before();
   __syncthreads();
@@ -786,45 +967,6 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 // at a unit boundary the row threads read dQ out of TMEM, copy the next unit's Q and dO rows from the staging buffer
 // into TMEM, and only then store dQ and DPHI2 of the finished unit, so the next unit's first products are computed
 // meanwhile. Jobs, tiles and units are numbered across units, which sets every slot, stage and barrier phase.
-template <int D>
-__device__ __forceinline__ void stage_row_to_tmem(uint32_t taddr, const uint8_t* tile, int r) {
-  using L = TileLayout<D>;
-  constexpr int CPB = L::SWB / 16;  // 16-byte chunks per box row; the TMA swizzle permutes them by row
-  uint32_t u[D / 2];
-#pragma unroll
-  for (int c = 0; c < D / 8; ++c) {
-    const uint32_t o = uint32_t(r * L::SWB + (c % CPB) * 16);
-    const uint32_t sw = o ^ (((o >> 7) & uint32_t(CPB - 1)) << 4);
-    const uint4 x = *reinterpret_cast<const uint4*>(tile + (c / CPB) * L::BOXB + sw);
-    u[4 * c] = x.x;
-    u[4 * c + 1] = x.y;
-    u[4 * c + 2] = x.z;
-    u[4 * c + 3] = x.w;
-  }
-  if constexpr (D == 16) {
-    tmem_st8(taddr, u);
-  } else if constexpr (D == 32) {
-    tmem_st16(taddr, u);
-  } else {
-#pragma unroll
-    for (int c = 0; c < D / 2; c += 32) tmem_st32(taddr + c, u + c);
-  }
-}
-
-// AND of `v` over the 256 row threads (named barrier kNamedBarRows).
-__device__ __forceinline__ bool rows_all(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, 256, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(v)), "r"(kNamedBarRows)
-      : "memory");
-  return r != 0;
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -882,9 +1024,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA warpgroup keeps 88 (the MMA
-  // issue code needs them) and the two row groups take 208 each (128*88 + 256*208 = 384*168).
-  if (warp < kRowWarp0) regs_producer();
+  if (warp < kRowWarp0) regs_producer<D>();
 
   if (warp == kWarpProducer) {
     if (elect_one()) {
@@ -1001,7 +1141,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 214);
   } else if (warp >= kRowWarp0) {
-    regs_rows();
+    regs_rows<D>();
     const int grp = (warp - kRowWarp0) >> 2, wr = warp & 3;
     const int r = wr * 32 + lane;  // query within the tile = TMEM lane
     const int cb = grp * kHalf;    // this group's key columns [cb, cb + 64)
@@ -1362,9 +1502,9 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     return FPA_ERR_CUDA;
   }
   const int grid = d.NB * d.BH();
-  const int qgrid = std::min(grid, sm_count());  // persistent; the stats kernel zeroed the unit counters
+  const int pgrid = std::min(grid, sm_count());  // persistent; the stats kernel zeroed the unit counters
   prof_mark(s, "bwd_kv_tc");
-  kv<<<grid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
+  kv<<<pgrid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
   if (e == cudaSuccess && !CK::FUSEDIAG) {
     prof_mark(s, "diag_dphi");
@@ -1372,7 +1512,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   }
   if (e == cudaSuccess) {
     prof_mark(s, "bwd_q_tc");
-    qk<<<qgrid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
+    qk<<<pgrid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
