@@ -867,8 +867,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
               const float2 dd = __fadd2_rn(make_float2(vb.x, vb.y), npsi2);
               const float2 xm = make_float2(fminf(am, dd.x), fminf(am, dd.y));
               const bool in0 = pa || dd.x <= 0.f, in1 = pa || dd.y <= 0.f;
-              float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
-              sv = __fadd2_rn(sv, make_float2(va.x, va.y));
+              const float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2,
+                                           __ffma2_rn(bet2, xm, make_float2(va.x, va.y)));
               const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
               const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), make_float2(va.z, va.w)));
               const float2 g = make_float2(in0 ? ds.x : 0.f, in1 ? ds.y : 0.f);
@@ -1342,8 +1342,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
               const float2 dd = __fadd2_rn(cap2, make_float2(va.z, va.w));
               const float2 x = make_float2(fminf(va.x, dd.x), fminf(va.y, dd.y));
               const float2 xm = make_float2(fminf(x.x, 0.f), fminf(x.y, 0.f));
-              float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __fmul2_rn(bet2, xm));
-              sv = __fadd2_rn(sv, nlse2);
+              const float2 sv = __ffma2_rn(make_float2(sS[e], sS[e + 1]), sc2, __ffma2_rn(bet2, xm, nlse2));
               const float2 pp = make_float2(ex2(sv.x), ex2(sv.y));
               const float2 ds = __fmul2_rn(pp, __fadd2_rn(make_float2(sP[e], sP[e + 1]), ndel2));
               const float2 g = make_float2(x.x <= 0.f ? ds.x : 0.f, x.y <= 0.f ? ds.y : 0.f);
