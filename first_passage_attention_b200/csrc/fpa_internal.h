@@ -31,6 +31,7 @@ inline Dims make_dims(int B, int H, int T, int D, int BT) {
 // Profiling mark (fpa_profile.cu): when profiling is on, records an event on `s` that starts the timing of the
 // kernel `name` launched next; name = nullptr ends the last kernel of a call. A no-op otherwise.
 void prof_mark(cudaStream_t s, const char* name);
+bool prof_on();  // per-kernel timing enabled (the library then launches everything on the caller's stream)
 
 // Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
 void set_last_error(const std::string& msg);

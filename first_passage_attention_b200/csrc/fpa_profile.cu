@@ -23,6 +23,8 @@ std::vector<cudaEvent_t> g_pool;
 
 }  // namespace
 
+bool prof_on() { return g_on.load(std::memory_order_relaxed) != 0; }
+
 void prof_mark(cudaStream_t s, const char* name) {
   if (!g_on.load(std::memory_order_relaxed)) return;
   std::lock_guard<std::mutex> lock(g_mu);

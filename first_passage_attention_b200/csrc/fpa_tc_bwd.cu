@@ -22,6 +22,8 @@
 // the current one. Every mbarrier wait is bounded (fpa::sm100::mbar_wait).
 #include <cuda.h>
 
+#include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "fpa_sm100.cuh"
@@ -1428,6 +1430,51 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   }
 }
 
+// The q-pass depends on nothing the kv-pass writes, so it runs on an auxiliary stream forked from the caller's
+// stream: its persistent CTAs take over the SMs that the kv-pass's last units leave idle. One auxiliary stream and
+// pair of events per calling stream and device, created on first use (under stream capture with the thread's
+// capture mode relaxed for the creation calls, which touch no captured work); when none can be had, both passes
+// run on the caller's stream.
+struct Fork {
+  cudaStream_t caller;
+  int dev;
+  cudaStream_t aux;
+  cudaEvent_t fork, join;
+};
+
+bool fork_of(cudaStream_t s, Fork* out) {
+  static std::mutex mu;
+  static Fork table[32];
+  static int n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (table[i].caller == s && table[i].dev == dev) {
+      *out = table[i];
+      return true;
+    }
+  if (n == 32) return false;
+  Fork f{s, dev, nullptr, nullptr, nullptr};
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  bool ok = cudaStreamCreateWithFlags(&f.aux, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming) == cudaSuccess;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (!ok) {
+    cudaGetLastError();
+    return false;
+  }
+  table[n++] = f;
+  *out = f;
+  return true;
+}
+
+// Persistent kernels ask for at least this much shared memory, so that two of them (the kv- and q-pass running
+// concurrently) never share an SM and wait for each other's 512 TMEM columns.
+constexpr int kPersistentMinSmem = 116 * 1024;
+
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
                const Fact& fact, float* gd, const float4* qv4, int* sched, int* status, cudaStream_t s,
@@ -1494,16 +1541,29 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   p.il2 = kLog2e / a.tau;
   auto kv = tc_bwd_kv_kernel<D>;
   auto qk = tc_bwd_q_kernel<D>;
-  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK::SMEM);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, CQ::SMEM);
+  const int smem_kv = std::max(CK::SMEM, kPersistentMinSmem), smem_q = std::max(CQ::SMEM, kPersistentMinSmem);
+  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
   const int grid = d.NB * d.BH();
   const int pgrid = std::min(grid, sm_count());  // persistent; the stats kernel zeroed the unit counters
+  Fork f;
+  const bool forked = !prof_on() && fork_of(s, &f);  // per-kernel timing needs one stream
+  cudaStream_t sq = s;
+  if (forked) {
+    e = cudaEventRecord(f.fork, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(f.aux, f.fork, 0);
+    if (e != cudaSuccess) {
+      *err = std::string("tensor-core backward fork: ") + cudaGetErrorString(e);
+      return FPA_ERR_CUDA;
+    }
+    sq = f.aux;
+  }
   prof_mark(s, "bwd_kv_tc");
-  kv<<<pgrid, kThreads, CK::SMEM, s>>>(mq, mk, mv, mdo, p);
+  kv<<<pgrid, kThreads, smem_kv, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
   if (e == cudaSuccess && !CK::FUSEDIAG) {
     prof_mark(s, "diag_dphi");
@@ -1511,8 +1571,13 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   }
   if (e == cudaSuccess) {
     prof_mark(s, "bwd_q_tc");
-    qk<<<pgrid, kThreads, CQ::SMEM, s>>>(mq, mk, mv, mdo, p);
+    qk<<<pgrid, kThreads, smem_q, sq>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
+  }
+  if (forked) {  // join even after a failed launch, so that no capture is left with a dangling fork
+    const cudaError_t e2 = cudaEventRecord(f.join, f.aux);
+    const cudaError_t e3 = e2 == cudaSuccess ? cudaStreamWaitEvent(s, f.join, 0) : e2;
+    if (e == cudaSuccess) e = e3;
   }
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward launch: ") + cudaGetErrorString(e);
