@@ -87,7 +87,7 @@ struct TcBwdCfg : TileLayout<D> {
   static constexpr int OFF_RED = OFF_VEC + NS * VECSTAGE;  // 32 + 4 * 128 floats of row-group scratch
   static constexpr int OFF_G = OFF_RED + (32 + 4 * kBT) * 4;
   // kv: a_full, st_full[NS], st_empty[NS], s_full[NSLOT], p_full[NSLOT], acc_done, acc_free, drain, at_full,
-  // x_full, x_empty, g_full, g_free, u_full[kUQ], u_empty[kUQ] (the q-pass uses a subset)
+  // x_full, x_empty, g_full, g_free, u_full[kUQ], u_empty[kUQ], s_last (the q-pass uses a subset)
   static constexpr int NBAR = 2 * NS + 2 * NSLOT + 10 + 2 * kUQ;
   // kv-pass: the diagonal tile's g ([128][129] fp32) and a2 of its positions (with 2^{a2 - max}) stay in shared
   // memory, where warps 2-3 run the in-tile soft-min while the row groups go on, when that fits (all D but 128).
@@ -305,7 +305,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   uint64_t* g_free = g_full + 1;   // warps 2-3 are done with it
   uint64_t* u_full = g_free + 1;   // [kUQ] unit ids handed from the producer to the other warps
   uint64_t* u_empty = u_full + kUQ;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + kUQ);
+  uint64_t* s_last = u_empty + kUQ;  // once per unit: its last S^T / dP^T products are complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_last + 1);
   int* uq = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
@@ -338,6 +339,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       mbar_init(u_full + x, 1);
       mbar_init(u_empty + x, 1 + kRowThreads / 32 + (C::FUSEDIAG ? 2 : 0));  // MMA, row and soft-min warps
     }
+    mbar_init(s_last, 1);
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -385,12 +387,14 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         __syncwarp();
         ++nx;
       }
-      // Without room in TMEM, K and V go to shared memory, after the unit's first tiles and once every MMA of the
-      // previous unit (the last readers of that memory) has completed.
+      // Without room in TMEM, K and V go to shared memory, after the unit's first tiles and once the previous
+      // unit's last S^T / dP^T products (the last readers of that memory) are complete. s_last completes once per
+      // unit and is waited here in unit order, and its next phase needs this unit's K and V, so the parity test
+      // cannot see an older phase.
       const int kst = nsteps < C::NS ? nsteps : C::NS;
       for (int k = 0; k <= nsteps && ok; ++k) {
         if (!AT && k == kst) {
-          if (u > 0) ok = mbar_wait(acc_done, (u - 1) & 1, p.status, 102);
+          if (u > 0) ok = mbar_wait(s_last, (u - 1) & 1, p.status, 102);
           if (!ok) break;
           if (elect_one()) {
             mbar_expect_tx(a_full, 2 * C::TILEB);
@@ -467,6 +471,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
           issue_ss_half<D>(dcol + kHalf, sb, bdo);
         }
         mma_commit_w(s_full + sl);
+        if (n == njobs - 1) mma_commit_w(s_last);
       };
       ok = AT ? mbar_wait(at_full, u & 1, p.status, 115) : mbar_wait(a_full, u & 1, p.status, 110);
       tc_fence_after();
@@ -704,10 +709,12 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         prer_n = p.prer[size_t(z) * p.NB + j];
       }
       if constexpr (AT) {
+        // The previous unit's last S^T / dP^T products (the last readers of the K and V columns) are complete:
+        // s_last is waited in unit order, and its next phase needs this unit's K and V.
+        if (have_prev && ok) ok = mbar_wait(s_last, (u - 1) & 1, p.status, 127);
         if (more) {
-          // Group 0 copies the key's row of K, group 1 its row of V, into TMEM. Every MMA of the previous unit has
-          // completed (acc_done), so nothing reads those columns any more.
-          ok = mbar_wait(x_full, u & 1, p.status, 125);
+          // Group 0 copies the key's row of K, group 1 its row of V, into TMEM.
+          ok = ok && mbar_wait(x_full, u & 1, p.status, 125);
           if (ok) {
             stage_row_to_tmem<D>(tl + (grp == 0 ? COL_K : COL_V), smem + C::OFF_X + grp * C::TILEB, r);
             tmem_st_wait();
@@ -718,6 +725,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         }
       }
       if (have_prev) {
+        // dV and dK of the finished unit out of TMEM (its MMAs have completed); the MMA warp may then start this
+        // unit's.
+        if (pv_done && !mbar_wait(acc_done, (u - 1) & 1, p.status, 122)) pv_done = pv_ok = ok = false;
         if (pv_done) {
           tc_fence_after();
           __half* dvrow = p.dv + pv_b * p.dv_s[0] + pv_h * p.dv_s[1] + int64_t(pv_s) * p.dv_s[2];
@@ -938,7 +948,6 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       }
       gsum += gsum2.x + gsum2.y;
       dbsum += dbsum2.x + dbsum2.y;
-      if (ok) ok = mbar_wait(acc_done, u & 1, p.status, 122);
       have_prev = true;
       pv_done = ok;
       pv_ok = s_ok && ok;
@@ -990,7 +999,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   uint64_t* x_empty = x_full + 1;  // the row threads have copied the staging buffer
   uint64_t* u_full = x_empty + 1;  // [kUQ] unit ids handed from the producer to the MMA warp and the rows
   uint64_t* u_empty = u_full + kUQ;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + kUQ);
+  uint64_t* s_last = u_empty + kUQ;  // once per unit: its last S / dP products are complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_last + 1);
   int* uq = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
@@ -1019,6 +1029,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       mbar_init(u_full + x, 1);
       mbar_init(u_empty + x, 1 + kRowThreads / 32);  // the MMA warp and each row warp
     }
+    mbar_init(s_last, 1);
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, 512);
@@ -1120,6 +1131,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         issue_ts_k<D>(dcol, tmem + COL_Q, s1 + st * C::TILEB + g * kHalf * C::SWB);           // S  = Q K^T
         issue_ts_k<D>(dcol + kHalf, tmem + COL_DO, s2 + st * C::TILEB + g * kHalf * C::SWB);  // dP = dO V^T
         mma_commit_w(s_full + sl);
+        if (n == njobs - 1) mma_commit_w(s_last);
       };
       ok = mbar_wait(at_full, u & 1, p.status, 210);
       tc_fence_after();
@@ -1155,9 +1167,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     float* csh = red + 32 + 2 * kBT;
     bool ok = true;
     int gn = 0, gk = 0;
-    // The finished unit, written out after the next unit's Q and dO rows are in TMEM.
-    bool have_prev = false;
-    float dqv[DH];
+    // The finished unit, read out and written after the next unit's Q and dO rows are in TMEM.
+    bool have_prev = false, pv_done = false;
     int pv_t = 0, pv_i = 0, pv_b = 0, pv_h = 0;
     size_t pv_zb = 0;
     bool pv_ok = false;
@@ -1192,10 +1203,12 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         sufr_n = p.sufr[size_t(z) * p.NB + i];
         sufl0_n = p.sufl[zb + size_t(i) * kBT];
       }
+      // The previous unit's last S / dP products (the last readers of the Q and dO columns) are complete: s_last
+      // is waited in unit order, and its next phase needs this unit's Q and dO.
+      if (have_prev && ok) ok = mbar_wait(s_last, (u - 1) & 1, p.status, 235);
       if (more) {
-        // Group 0 copies the query's row of Q, group 1 its row of dO, into TMEM. Every MMA of the previous unit
-        // has completed (acc_done), so nothing reads those columns any more.
-        ok = mbar_wait(x_full, u & 1, p.status, 234);
+        // Group 0 copies the query's row of Q, group 1 its row of dO, into TMEM.
+        ok = ok && mbar_wait(x_full, u & 1, p.status, 234);
         if (ok) {
           stage_row_to_tmem<D>(tl + (grp == 0 ? COL_Q : COL_DO), smem + C::OFF_X + grp * C::TILEB, r);
           tmem_st_wait();
@@ -1205,7 +1218,21 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         mbar_arrive(x_empty);
       }
       if (have_prev) {
-        if (pv_ok && (D >= 32 || grp == 0)) {
+        // dQ of the finished unit out of TMEM (its MMAs have completed); the MMA warp may then start this unit's.
+        float dqv[DH];
+        bool done = pv_done && mbar_wait(acc_done, (u - 1) & 1, p.status, 222);
+        if (done) {
+          tc_fence_after();
+          if (D >= 32 || grp == 0) {
+#pragma unroll
+            for (int c = 0; c < DH; c += 16) tmem_ld16(tl + C::COL_A1 + grp * DH + c, dqv + c);
+            tmem_ld_wait();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acc_free);
+        if (!done) ok = false;
+        if (done && pv_ok && (D >= 32 || grp == 0)) {
           __half* dqrow = p.dq + pv_b * p.dq_s[0] + pv_h * p.dq_s[1] + int64_t(pv_t) * p.dq_s[2] + grp * DH;
 #pragma unroll
           for (int c = 0; c < DH; c += 8) {
@@ -1396,19 +1423,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
           midl = lse2(midl, blj);
         }
       }
-      // dQ of the unit out of TMEM; the MMA warp may then start the next unit's dQ.
-      if (ok) ok = mbar_wait(acc_done, u & 1, p.status, 222);
-      if (ok) {
-        tc_fence_after();
-        if (D >= 32 || grp == 0) {
-#pragma unroll
-          for (int c = 0; c < DH; c += 16) tmem_ld16(tl + C::COL_A1 + grp * DH + c, dqv + c);
-          tmem_ld_wait();
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(acc_free);
       have_prev = true;
+      pv_done = ok;
       pv_t = t;
       pv_i = i;
       pv_b = b;
