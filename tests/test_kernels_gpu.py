@@ -125,6 +125,21 @@ def test_kernel_deterministic(dtype):
     assert all(torch.equal(x, y) for x, y in zip(*runs))
 
 
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_persistent_passes_with_several_units_per_cta(D):
+    """More work units (a head's 128-row tile) than SMs: B2 H48 T384 gives 288 units per backward pass, a third of
+    them one tile long, so each persistent CTA takes two units in a row and the unit-boundary hand-overs (staged or
+    shared-memory stationary operands, accumulator read-out, the diagonal soft-min buffer) all run. D = 32 keeps
+    K and V in TMEM, D = 64 in shared memory, D = 128 also has the separate diagonal kernel. Against the oracle, and
+    bit-identical twice."""
+    need_gpu()
+    inp = make_inputs(2, 48, 384, D, seed=500 + D)
+    kern = run_kernel(*inp, path="tensor")
+    check(kern, run_oracle(*inp), torch.float16)
+    again = run_kernel(*inp, path="tensor")
+    assert all(torch.equal(x, y) for x, y in zip(kern, again))
+
+
 def config3_inputs(D, dtype, seed):
     """Benchmark configuration 3: B2 H8 T1000; phi = cumsum N(-0.05, 1); psi = phi + N(0,1); beta = softplus(N)."""
     g = torch.Generator().manual_seed(seed)
