@@ -67,10 +67,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.y;
-  if (j == 0 && z == 0 && tid == 0) {
-    if (status) *status = 0;
-    if (fact.sched) fact.sched[0] = fact.sched[1] = 0;
-  }
+  if (j == 0 && z == 0 && tid < 4 && status) status[tid] = 0;  // status word and the work-unit counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
   const float p = t < T ? phi[size_t(z) * T + t] : kInf;
@@ -168,7 +165,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
                          const Fact* fact) {
-  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
                                                    cols_scaled, beta, d.H, f, status);
   return cudaGetLastError();
@@ -360,8 +357,9 @@ __device__ float block_sum(float v, float* red) {
 //   dphi4_u                                                            (u in the diagonal tile with both)
 //   part3_u = 2^{a2_u - c_U} sum_{j<U<i} 2^{c_U - cmid_ij} TB[i][j]     (u in a tile strictly between)
 // dphi_u = beta * (part1 + dphi2 + dphi4 + part3). Block: BT threads (one per position of the tile).
-__global__ void dphi_kernel(const float* __restrict__ phi, const float* __restrict__ beta, int H, int T, int BT,
-                            int NB, float il2, Stats st, BwdScratch sc, float* __restrict__ dphi) {
+__global__ void dphi_kernel(const float* __restrict__ phi, const float* __restrict__ beta, int B, int H, int T,
+                            int BT, int NB, float il2, Stats st, BwdScratch sc, float* __restrict__ dphi,
+                            float* __restrict__ dbeta) {
   extern __shared__ float sm[];
   float* cb = sm;           // [NB] max of a2 per tile
   float* A = cb + NB;       // [NB] A[j] = max cb over (j, U]
@@ -462,17 +460,27 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     size_t p = size_t(z) * TP + u;
     dphi[size_t(z) * T + u] = beta[h] * (part1 + sc.dphi2[p] + sc.dphi4[p] + part3);
   }
+  // dbeta[h]: the kv-pass's parts summed over the batch and the key tiles, by the first warp of the blocks
+  // (U = 0, b = 0), strided over the lanes and then a fixed shuffle tree (kernel.py:450: dbeta.sum((0, 2))).
+  if (U == 0 && z < H && tid < 32) {
+    const int n = B * NB;
+    float acc = 0.f;
+    for (int e = tid; e < n; e += 32) acc += sc.dbeta[(size_t(e / NB) * H + h) * NB + e % NB];
+    acc = group_sum<32>(acc);
+    if (tid == 0) dbeta[h] = acc;
+  }
 }
 
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
-                        const BwdScratch& sc, float* dphi, cudaStream_t s) {
+                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s) {
   int threads = d.BT < 32 ? 32 : d.BT;
   size_t smem = (3 * size_t(d.NB) + 2 * d.BT + 32) * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc, dphi);
+  dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
+                                                        dphi, dbeta);
   return cudaGetLastError();
 }
 
@@ -576,21 +584,5 @@ cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, f
   return cudaGetLastError();
 }
 
-// dbeta_h = sum over batch b and key tiles j of the per-tile partials (kernel.py:450). One warp per head: lane l
-// sums the partials l, l + 32, ... in order, then a fixed shuffle tree joins the lanes (deterministic).
-__global__ void dbeta_kernel(int B, int H, int NB, const float* __restrict__ part, float* __restrict__ dbeta) {
-  const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (h >= H) return;  // whole warps leave together
-  const int n = B * NB;
-  float acc = 0.f;
-  for (int e = lane; e < n; e += 32) acc += part[(size_t(e / NB) * H + h) * NB + e % NB];
-  acc = group_sum<32>(acc);
-  if (lane == 0) dbeta[h] = acc;
-}
-
-cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s) {
-  dbeta_kernel<<<(d.H + 3) / 4, 128, 0, s>>>(d.B, d.H, d.NB, sc.dbeta, dbeta);
-  return cudaGetLastError();
-}
 
 }  // namespace fpa

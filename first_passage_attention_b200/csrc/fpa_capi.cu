@@ -178,12 +178,8 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
     ++n;
   }
   fpa::prof_mark(s, "dphi");
-  e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, s);
+  e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, a->dbeta, s);  // also reduces dbeta
   if (e != cudaSuccess) return cuda_fail(e, "dphi kernel");
-  ++n;
-  fpa::prof_mark(s, "dbeta");
-  e = fpa::launch_dbeta(d, sc, a->dbeta, s);
-  if (e != cudaSuccess) return cuda_fail(e, "dbeta kernel");
   ++n;
   fpa::prof_mark(s, nullptr);
   a->kernels_launched = n;

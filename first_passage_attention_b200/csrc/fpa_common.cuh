@@ -96,7 +96,6 @@ struct Fact {
   // [BH][TP] per key, two keys c, c+1 (c even) per pair of float4 for packed f32x2 arithmetic:
   // kv4[c] = (SUF_c - psi_c, SUF_c1 - psi_c1, -psi_c, -psi_c1), kv4[c + 1] = (sufy_c, sufy_c1, SUFL_c, SUFL_c1)
   float4* kv4;
-  int* sched;  // [2] work-unit counters of the persistent backward passes, zeroed by the stats kernel
 };
 
 // Scratch of the backward pass (all float32, per head z = b*H + h).

@@ -60,8 +60,7 @@ cudaError_t launch_qv_delta(const void* o, Str4 so, const void* dout, Str4 sdo, 
                             const float* prey, const Dims& d, float4* qv4, cudaStream_t s);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
-                        const BwdScratch& sc, float* dphi, cudaStream_t s);
-cudaError_t launch_dbeta(const Dims& d, const BwdScratch& sc, float* dbeta, cudaStream_t s);
+                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s);
 
 // fpa_simt.cu (FFMA kernels, tiles of 64 positions, any supported D, fp16 or fp32 inputs)
 constexpr int kSimtBT = 64;

@@ -17,6 +17,14 @@ bool tc_supports(int D);
 // Streaming multiprocessors of the current device (the grid of the persistent kernels).
 int sm_count();
 
+// Persistent kernels ask for at least this much shared memory, so that two of them (the kv- and q-pass running
+// concurrently) never share an SM and wait for each other's 512 TMEM columns.
+constexpr int kPersistentMinSmem = 116 * 1024;
+
+// The 256-byte status block at the head of a workspace: word 0 is the status word, words 1-2 are the work-unit
+// counters of the persistent kv-pass and q-pass; the stats kernel that precedes them zeroes words 0-3.
+constexpr int kSchedKv = 1;
+
 // True if a [B, H, T, D] fp16 operand with these element strides can be read by TMA as it is (innermost stride 1,
 // 16-byte aligned base and strides).
 bool tma_layout_ok(const void* p, const int64_t st[4]);

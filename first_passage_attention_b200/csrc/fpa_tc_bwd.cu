@@ -138,7 +138,7 @@ struct TcBwdParams {
   float* dphi4;        // [BH][TP]
   float* dphi2;        // [BH][TP]
   int* status;
-  int* sched;          // [2] work-unit counters (kv-pass, q-pass), zero before the launch
+  int* sched;          // [2] work-unit counters (kv-pass, q-pass), zeroed by the stats kernel
   int B, H, T, NB, TP;
   float scale, scale2, il2;
 };
@@ -1487,10 +1487,6 @@ bool fork_of(cudaStream_t s, Fork* out) {
   return true;
 }
 
-// Persistent kernels ask for at least this much shared memory, so that two of them (the kv- and q-pass running
-// concurrently) never share an SM and wait for each other's 512 TMEM columns.
-constexpr int kPersistentMinSmem = 116 * 1024;
-
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
                const Fact& fact, float* gd, const float4* qv4, int* sched, int* status, cudaStream_t s,
@@ -1622,7 +1618,7 @@ size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
   return keycols_bytes(d) + gd_bytes(d) +
          2 * align256(bh * d.TP * sizeof(float4)) + 2 * align256(bh * d.TP * sizeof(float)) +
-         2 * align256(bh * d.NB * sizeof(float)) + align256(2 * sizeof(int));
+         2 * align256(bh * d.NB * sizeof(float));
 }
 
 int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
@@ -1659,8 +1655,6 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   fact.prer = reinterpret_cast<float*>(q);
   q += align256(bh * d.NB * 4);
   fact.sufr = reinterpret_cast<float*>(q);
-  q += align256(bh * d.NB * 4);
-  fact.sched = reinterpret_cast<int*>(q);  // work-unit counters of the persistent passes
   // Raw key vectors, the factorisation arrays and the padded lse copy (filled by the stats and delta kernels).
   prof_mark(s, "stats");
   cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
@@ -1686,10 +1680,10 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   }
   int rc;
   switch (d.D) {
-    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
-    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
-    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
-    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, fact.sched, status, s, err); break;
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
   if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, delta (+ pack), kv, [diag], q
