@@ -63,13 +63,47 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
-                             const float* __restrict__ beta, int H, Fact fact, int* status) {
+                             const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.y;
   if (j == 0 && z == 0 && tid < 4 && status) status[tid] = 0;  // status word and the work-unit counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
+  // Tensor-core backward: delta_t = sum_d dO[t, d] O[t, d] (kernel.py:166-174) in float32, read coalesced: each warp
+  // covers its 32 rows with groups of G = D/8 lanes, one 16-byte load of O and of dO per lane per row, a fixed
+  // shuffle tree over the group, and the row's owner thread picks the sum up from shared memory. The loads are
+  // issued before the scans below, so their latency passes meanwhile. Packed with -lse, PRE and prey at the end.
+  __shared__ float sdelta[1024];
+  float delta = 0.f, nlse = -kInf;
+  if (qv.qv4) {
+    const int G = qv.D / 8, rpi = 32 / G, sub = lane / G, part = lane % G;
+    const int b = z / H, h = z % H;
+    const __half* ob = qv.o + b * qv.so.b + h * qv.so.h + part * 8;
+    const __half* db = qv.dout + b * qv.sdo.b + h * qv.sdo.h + part * 8;
+#pragma unroll 4
+    for (int it = 0; it < G; ++it) {
+      const int rr = w * 32 + it * rpi + sub, tt = j * BT + rr;
+      float acc = 0.f;
+      if (tt < T) {
+        const uint4 x = *reinterpret_cast<const uint4*>(ob + int64_t(tt) * qv.so.t);
+        const uint4 y = *reinterpret_cast<const uint4*>(db + int64_t(tt) * qv.sdo.t);
+        const __half2* xh = reinterpret_cast<const __half2*>(&x);
+        const __half2* yh = reinterpret_cast<const __half2*>(&y);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a2 = __half22float2(xh[e]), b2 = __half22float2(yh[e]);
+          acc = fmaf(a2.x, b2.x, acc);
+          acc = fmaf(a2.y, b2.y, acc);
+        }
+      }
+      for (int o = G >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (part == 0) sdelta[rr] = acc;
+    }
+    __syncwarp();
+    delta = sdelta[tid];  // this warp's rows only
+    if (t < T) nlse = -qv.lse[size_t(z) * T + t];
+  }
   const float p = t < T ? phi[size_t(z) * T + t] : kInf;
   const float a = t < T ? -p * il2 : -kInf;
   // inclusive prefix: PRE, PREL
@@ -145,6 +179,14 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
       kv[4] = ex2(sufl - sufl0);
       kv[6] = sufl;
     }
+    if (qv.qv4) {
+      // Pair layout: queries c, c+1 (c even) share qv4[c] = (-lse, -delta) and qv4[c + 1] = (PRE, prey).
+      float* qa = reinterpret_cast<float*>(qv.qv4 + base + (tid & ~1)) + (tid & 1);
+      qa[0] = nlse;  // -inf beyond T
+      qa[2] = t < T ? -delta : 0.f;
+      qa[4] = pm;
+      qa[6] = t < T ? ex2(pl - blj) : 1.f;
+    }
   }
   if (cols.a) {
     const bool ok = t < T;
@@ -164,10 +206,11 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
-                         const Fact* fact) {
+                         const Fact* fact, const QvIn* qv) {
   const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
+  const QvIn q = qv ? *qv : QvIn{nullptr, Str4{0, 0, 0, 0}, nullptr, Str4{0, 0, 0, 0}, nullptr, nullptr, 0};
   stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
-                                                   cols_scaled, beta, d.H, f, status);
+                                                   cols_scaled, beta, d.H, f, status, q);
   return cudaGetLastError();
 }
 
@@ -274,62 +317,11 @@ __global__ void qv_pack_kernel(const float* __restrict__ lse, const float* __res
   qv4[idx + 1] = make_float4(pre[idx], pre[idx + 1], ok0 ? prey[idx] : 1.f, ok1 ? prey[idx + 1] : 1.f);
 }
 
-// delta fused with the pair packing above, for fp16 O and dO with unit innermost stride and 16-byte aligned rows:
-// G = D / 8 lanes per row (16-byte loads) over all BH * TP padded rows (rows beyond T read nothing: delta = 0);
-// rows t and t+1 of a pair sit in adjacent lane groups of one warp, and the even row's first lane writes the pair.
-template <int G>
-__global__ void qv_delta_f16_kernel(const __half* __restrict__ o, Str4 so, const __half* __restrict__ dout, Str4 sdo,
-                                    const float* __restrict__ lse, const float* __restrict__ pre,
-                                    const float* __restrict__ prey, int H, int T, int TP, int rows,
-                                    float4* __restrict__ qv4) {
-  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
-  const int row = gid / G, part = gid % G;
-  const bool in = row < rows;
-  const int z = in ? row / TP : 0, t = in ? row % TP : 0;
-  const bool ok = in && t < T;
-  float acc = 0.f;
-  if (ok) {
-    const int b = z / H, h = z % H;
-    const uint4 a = *reinterpret_cast<const uint4*>(o + b * so.b + h * so.h + int64_t(t) * so.t + part * 8);
-    const uint4 c = *reinterpret_cast<const uint4*>(dout + b * sdo.b + h * sdo.h + int64_t(t) * sdo.t + part * 8);
-    const __half2* ah = reinterpret_cast<const __half2*>(&a);
-    const __half2* ch = reinterpret_cast<const __half2*>(&c);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 x = __half22float2(ah[q]), y = __half22float2(ch[q]);
-      acc = fmaf(x.x, y.x, acc);
-      acc = fmaf(x.y, y.y, acc);
-    }
-  }
-  acc = group_sum<G>(acc);
-  const float acc1 = __shfl_down_sync(0xffffffffu, acc, G);  // row t + 1
-  if (in && part == 0 && (t & 1) == 0) {
-    const bool ok1 = t + 1 < T;
-    const size_t lz = size_t(z) * T;
-    qv4[row] = make_float4(ok ? -lse[lz + t] : -kInf, ok1 ? -lse[lz + t + 1] : -kInf, ok ? -acc : 0.f,
-                           ok1 ? -acc1 : 0.f);
-    qv4[row + 1] = make_float4(pre[row], pre[row + 1], ok ? prey[row] : 1.f, ok1 ? prey[row + 1] : 1.f);
-  }
-}
 
 bool qv_delta_fusable(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d) {
   return dtype == FPA_DTYPE_F16 && d.D >= 16 && d.D <= 128 && vec16_ok(o, so) && vec16_ok(dout, sdo);
 }
 
-cudaError_t launch_qv_delta(const void* o, Str4 so, const void* dout, Str4 sdo, const float* lse, const float* pre,
-                            const float* prey, const Dims& d, float4* qv4, cudaStream_t s) {
-  const int rows = d.BH() * d.TP, G = d.D / 8;
-  const int blocks = int((int64_t(rows) * G + 255) / 256);
-  auto a = static_cast<const __half*>(o);
-  auto c = static_cast<const __half*>(dout);
-  switch (G) {
-    case 2: qv_delta_f16_kernel<2><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
-    case 4: qv_delta_f16_kernel<4><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
-    case 8: qv_delta_f16_kernel<8><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
-    default: qv_delta_f16_kernel<16><<<blocks, 256, 0, s>>>(a, so, c, sdo, lse, pre, prey, d.H, d.T, d.TP, rows, qv4); break;
-  }
-  return cudaGetLastError();
-}
 
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
                            float4* qv4, cudaStream_t s) {

@@ -16,6 +16,19 @@ struct Str4 {
 
 inline Str4 str4(const int64_t s[4]) { return Str4{s[0], s[1], s[2], s[3]}; }
 
+// Inputs of the per-query pairs of the tensor-core backward when the stats kernel builds them itself:
+// qv4[t] = (-lse, -delta, PRE, prey) in the pair layout, delta_t = sum_d dO[t, d] O[t, d] (fp16 O and dO with
+// unit innermost stride and 16-byte aligned rows).
+struct QvIn {
+  const __half* o;
+  Str4 so;
+  const __half* dout;
+  Str4 sdo;
+  const float* lse;
+  float4* qv4;
+  int D;
+};
+
 // Sizes shared by every kernel of one call. Tiles are BT positions; NB = ceil(T / BT); TP = NB * BT.
 struct Dims {
   int B, H, T, D, BT, NB, TP;
@@ -48,16 +61,14 @@ KeyCols carve_keycols(char* base, const Dims& d);
 // cols_scaled = 1: the forward's b'-scaled key vectors; 0: raw (a = SUF - psi, psi, phi) for the backward.
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
-                         const Fact* fact = nullptr);
+                         const Fact* fact = nullptr, const QvIn* qv = nullptr);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          const float* lse, float* lsep, cudaStream_t s);
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,
                            float4* qv4, cudaStream_t s);
-// delta fused with the pair packing (one launch) when O and dO are fp16 with unit innermost stride and 16-byte
-// aligned rows and D <= 128; otherwise launch_delta + launch_qv_pack.
+// The stats kernel builds the per-query pairs itself (QvIn) when O and dO are fp16 with unit innermost stride and
+// 16-byte aligned rows and D <= 128; otherwise launch_delta + launch_qv_pack.
 bool qv_delta_fusable(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d);
-cudaError_t launch_qv_delta(const void* o, Str4 so, const void* dout, Str4 sdo, const float* lse, const float* pre,
-                            const float* prey, const Dims& d, float4* qv4, cudaStream_t s);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
                         const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s);

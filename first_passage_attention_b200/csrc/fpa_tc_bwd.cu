@@ -1655,15 +1655,16 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
   fact.prer = reinterpret_cast<float*>(q);
   q += align256(bh * d.NB * 4);
   fact.sufr = reinterpret_cast<float*>(q);
-  // Raw key vectors, the factorisation arrays and the padded lse copy (filled by the stats and delta kernels).
+  // Raw key vectors, the factorisation arrays and the per-query pairs (filled by the stats kernel; with O and dO
+  // not fp16 and vector-aligned, the pairs by the delta and packing kernels).
+  const bool fused = qv_delta_fusable(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d);
+  const QvIn qin{static_cast<const __half*>(a.o), str4(a.o_stride), static_cast<const __half*>(a.dout),
+                 str4(a.dout_stride), a.lse, qv4, d.D};
   prof_mark(s, "stats");
-  cudaError_t e = launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact);
+  cudaError_t e =
+      launch_stats(a.phi, a.psi, a.beta, d, a.tau, st, cols, 0, status, s, &fact, fused ? &qin : nullptr);
   int nprep = 1;
-  if (e == cudaSuccess && qv_delta_fusable(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d)) {
-    prof_mark(s, "qv_delta");
-    e = launch_qv_delta(a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), a.lse, st.pre, fact.prey, d, qv4, s);
-    nprep += 1;
-  } else {
+  if (!fused) {
     if (e == cudaSuccess) {
       prof_mark(s, "delta");
       e = launch_delta(a.dtype, a.o, str4(a.o_stride), a.dout, str4(a.dout_stride), d, sc.delta, nullptr, nullptr, s);
@@ -1686,7 +1687,7 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
     case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, delta (+ pack), kv, [diag], q
+  if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, [delta, pack], kv, [diag], q
   return rc;
 }
 
