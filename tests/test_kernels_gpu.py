@@ -140,6 +140,63 @@ def test_persistent_passes_with_several_units_per_cta(D):
     assert all(torch.equal(x, y) for x, y in zip(kern, again))
 
 
+def test_backward_calls_on_two_streams_at_once():
+    """Two forward + backward calls issued on two streams without synchronising in between (each call's q-pass runs
+    on an auxiliary stream of its own calling stream) give bit-identical results to the same calls run one after
+    the other."""
+    need_gpu()
+    inputs = [make_inputs(2, 8, 640, 64, seed=700 + n) for n in range(2)]
+    seq = [run_kernel(*inp, path="tensor") for inp in inputs]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    os.environ["FPA_B200_PATH"] = "tensor"
+    try:
+        outs = []
+        for inp, st in zip(inputs, streams):
+            with torch.cuda.stream(st):
+                a = [t.cuda(non_blocking=False).clone().requires_grad_() for t in inp[:6]]
+                o = first_passage_attention(*a, impl="triton")
+                g = torch.autograd.grad(o, a, inp[6].cuda())
+                outs.append([o.detach()] + list(g))
+        torch.cuda.synchronize()
+    finally:
+        os.environ.pop("FPA_B200_PATH", None)
+    for got, want in zip(outs, seq):
+        assert all(torch.equal(x.cpu(), y) for x, y in zip(got, want))
+
+
+def test_forward_backward_replayed_from_a_cuda_graph():
+    """Forward + backward captured into a CUDA graph (the forked q-pass becomes graph edges) and replayed give the
+    eager call's gradients bit for bit."""
+    need_gpu()
+    inp = [t.cuda() for t in make_inputs(2, 6, 512, 64, seed=800)]
+    leaves = [t.clone().requires_grad_() for t in inp[:6]]
+    do = inp[6]
+
+    def step():
+        for x in leaves:
+            x.grad = None
+        first_passage_attention(*leaves, impl="triton").backward(do)
+
+    os.environ["FPA_B200_PATH"] = "tensor"
+    try:
+        step()
+        want = [x.grad.clone() for x in leaves]
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        assert all(torch.equal(x.grad, w) for x, w in zip(leaves, want))
+    finally:
+        os.environ.pop("FPA_B200_PATH", None)
+
+
 def config3_inputs(D, dtype, seed):
     """Benchmark configuration 3: B2 H8 T1000; phi = cumsum N(-0.05, 1); psi = phi + N(0,1); beta = softplus(N)."""
     g = torch.Generator().manual_seed(seed)
