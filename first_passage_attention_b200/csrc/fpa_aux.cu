@@ -1,5 +1,7 @@
 // Small kernels around the attention passes: field statistics, delta = rowsum(dO * O), the final combination of
 // the soft-min gradient of phi, and the batch/tile reduction of dbeta. All are deterministic (fixed summation order).
+#include <cstdlib>
+
 #include "fpa_internal.h"
 
 namespace fpa {
@@ -12,7 +14,7 @@ size_t stats_bytes(const Dims& d) {
 size_t bwd_scratch_bytes(const Dims& d, int tb_parts) {
   size_t bh = size_t(d.BH());
   return 4 * align256(bh * d.TP * sizeof(float)) + align256(bh * d.NB * d.NB * tb_parts * sizeof(float)) +
-         align256(bh * d.NB * sizeof(float));
+         2 * align256(bh * d.NB * sizeof(float));
 }
 
 static float* take(char*& p, size_t n_floats) {
@@ -37,12 +39,14 @@ BwdScratch carve_bwd(char* base, const Dims& d, int tb_parts) {
   size_t bh = size_t(d.BH());
   BwdScratch s;
   s.tb_parts = tb_parts;
+  s.tb_sum = tb_parts == 2 ? 1 : tb_parts;  // the FFMA kv-pass writes one total per pair into a 2-float slot
   s.delta = take(base, bh * d.TP);
   s.w = take(base, bh * d.TP);
   s.dphi2 = take(base, bh * d.TP);
   s.dphi4 = take(base, bh * d.TP);
   s.tb = take(base, bh * d.NB * d.NB * tb_parts);
   s.dbeta = take(base, bh * d.NB);
+  s.part3 = take(base, bh * d.NB);
   return s;
 }
 
@@ -343,6 +347,97 @@ __device__ float block_sum(float v, float* red) {
   return r;  // valid in thread 0
 }
 
+// Part 3 of the dphi combination, u strictly between the key's tile j and the query's tile i (kernel.py:352-364),
+// for every tile U of one head in O(NB^2) work, for long contexts (dphi_kernel sums all pairs j < U < i for each U,
+// O(NB^3) per head, which is cheaper up to a few hundred tiles because it spreads over NB blocks per head):
+//   S_U = sum_{j < U < i} 2^{c_U - M(j, i)} TB[i][j],   M(j, i) = max_{j < n < i} c_n,   c_n = -BMIN_n * il2,
+// so that part3_u = 2^{a2_u - c_U} S_U (dphi_kernel). With X[i][j] = TB[i][j] at scale 2^{-M(j, i)}, three passes
+// in one block per head, each over many independent items:
+//   pass 1, every pair (i, j), i >= j + 2: the pair's partial sums (fixed order) and -M(j, i) (two lookups in a
+//           sparse table of range maxima) go into the pair's first two floats;
+//   pass 2, one warp per key tile j: the suffix sums C_j(U) = sum_{i > U} X[i][j] (a warp scan per 32 pairs with a
+//           carry), stored at pair (U + 1, j);
+//   pass 3, one warp per tile U: S_U 2^{-c_U} = sum_{j < U} C_j(U), lane-strided and then a fixed shuffle tree.
+// Sums of terms at different scales are kept as (m, v) = v 2^m with a running maximum; c_U - M(j, i) <= 0, so
+// nothing overflows. Fixed orders throughout: deterministic.
+constexpr int kPart3CubicMaxNB = 256;
+
+__device__ __forceinline__ void join_mv(float& m, float& v, float m2, float v2) {
+  const float mm = fmaxf(m, m2);
+  v = mm == -kInf ? 0.f : v * ex2(m - mm) + v2 * ex2(m2 - mm);
+  m = mm;
+}
+
+__global__ void dphi_part3_kernel(const float* __restrict__ bmin, int NB, int LV, float il2, BwdScratch sc) {
+  extern __shared__ float rmq[];  // [LV][NB]: rmq[l][n] = max c over tiles n .. n + 2^l - 1
+  const int z = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nwarps = blockDim.x >> 5;
+  for (int n = tid; n < NB; n += blockDim.x) rmq[n] = -bmin[size_t(z) * NB + n] * il2;
+  __syncthreads();
+  for (int l = 1; l < LV; ++l) {
+    for (int n = tid; n + (1 << l) <= NB; n += blockDim.x)
+      rmq[l * NB + n] = fmaxf(rmq[(l - 1) * NB + n], rmq[(l - 1) * NB + n + (1 << (l - 1))]);
+    __syncthreads();
+  }
+  const int np = sc.tb_parts;
+  float* tbz = sc.tb + size_t(z) * NB * NB * np;
+  // pass 1
+  for (int q = tid; q < NB * NB; q += blockDim.x) {
+    const int i = q / NB, j = q % NB;
+    if (i < j + 2) continue;
+    float* pp = tbz + size_t(q) * np;
+    float v = 0.f;
+    if (sc.tb_sum == 8) {
+      const float4 x = reinterpret_cast<const float4*>(pp)[0], y = reinterpret_cast<const float4*>(pp)[1];
+      v = (((x.x + x.y) + x.z) + x.w) + (((y.x + y.y) + y.z) + y.w);
+    } else {
+      for (int k = 0; k < sc.tb_sum; ++k) v += pp[k];
+    }
+    const int lo = j + 1, len = i - 1 - lo + 1, l = 31 - __clz(len);
+    const float mx = fmaxf(rmq[l * NB + lo], rmq[l * NB + i - (1 << l)]);
+    pp[0] = v;
+    pp[1] = -mx;
+  }
+  __syncthreads();
+  // pass 2: column j holds pairs i = NB-1 .. j+2 (descending); lane k of a 32-pair chunk takes i = top - k
+  for (int j = wid; j + 2 < NB; j += nwarps) {
+    float cm = -kInf, cv = 0.f;  // carry: the sum over the pairs above this chunk
+    for (int top = NB - 1; top >= j + 2; top -= 32) {
+      const int i = top - lane;
+      const bool in = i >= j + 2;
+      float* pp = tbz + (size_t(in ? i : j + 2) * NB + j) * np;
+      float m = in ? pp[1] : -kInf, v = in ? pp[0] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive scan over the lanes below (larger i first)
+        const float m2 = __shfl_up_sync(0xffffffffu, m, o), v2 = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) join_mv(m, v, m2, v2);
+      }
+      join_mv(m, v, cm, cv);
+      if (in) {
+        pp[0] = v;  // C_j(i - 1)
+        pp[1] = m;
+      }
+      cm = __shfl_sync(0xffffffffu, m, 31);
+      cv = __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  // pass 3
+  for (int U = wid; U < NB; U += nwarps) {
+    float m = -kInf, v = 0.f;
+    if (U >= 1 && U + 2 <= NB)
+      for (int j = lane; j < U; j += 32) {
+        const float* pp = tbz + (size_t(U + 1) * NB + j) * np;
+        join_mv(m, v, pp[1], pp[0]);
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), v2 = __shfl_xor_sync(0xffffffffu, v, o);
+      join_mv(m, v, m2, v2);
+    }
+    if (lane == 0) sc.part3[size_t(z) * NB + U] = v == 0.f ? 0.f : v * ex2(m + rmq[U]);
+  }
+}
+
 // Final soft-min gradient of phi for tile U of head z (kernel.py:344-370 combines the same four parts):
 //   part1_u = sum_{s<u in U, SUF_s<inf} 2^{a2_u - c_s} W_s            (u in the key's tile)
 //   dphi2_u                                                            (u in the query's tile)
@@ -351,7 +446,7 @@ __device__ float block_sum(float v, float* red) {
 // dphi_u = beta * (part1 + dphi2 + dphi4 + part3). Block: BT threads (one per position of the tile).
 __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restrict__ beta, int B, int H, int T,
                             int BT, int NB, float il2, Stats st, BwdScratch sc, float* __restrict__ dphi,
-                            float* __restrict__ dbeta) {
+                            float* __restrict__ dbeta, int part3_ready) {
   extern __shared__ float sm[];
   float* cb = sm;           // [NB] max of a2 per tile
   float* A = cb + NB;       // [NB] A[j] = max cb over (j, U]
@@ -375,7 +470,7 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     }
   }
   __syncthreads();
-  if (tid == 0) {
+  if (!part3_ready && tid == 0) {
     float m = -kInf;
     for (int j = U - 1; j >= 0; --j) {  // A[j] = max cb over tiles j+1 .. U
       m = fmaxf(m, cb[j + 1]);
@@ -388,27 +483,27 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     }
   }
   __syncthreads();
-  // part3 partial sums over the tile pairs (i, j), j < U < i, spread over the threads (fixed assignment); each
-  // pair's total joins its tb_parts partial sums in order.
+  // part3 (kernel.py:352-364) partial sums over the tile pairs (i, j), j < U < i, spread over the threads (fixed
+  // assignment); each pair's total joins its tb_sum partial sums in order. Long contexts: dphi_part3_kernel.
   float s3 = 0.f;
-  if (U > 0 && U < NB - 1) {
+  if (!part3_ready && U > 0 && U < NB - 1) {
     const float cU = cb[U];
     const int np = sc.tb_parts, npairs = (NB - 1 - U) * U;
     for (int pi = tid; pi < npairs; pi += blockDim.x) {
       const int i = U + 1 + pi / U, j = pi % U;
       const float* part = sc.tb + ((size_t(z) * NB + i) * NB + j) * np;
       float tbij = 0.f;
-      if (np == 8) {
+      if (sc.tb_sum == 8) {
         const float4 u = reinterpret_cast<const float4*>(part)[0], v = reinterpret_cast<const float4*>(part)[1];
         tbij = (((u.x + u.y) + u.z) + u.w) + (((v.x + v.y) + v.z) + v.w);
       } else {
-        for (int q = 0; q < np; ++q) tbij += part[q];
+        for (int q = 0; q < sc.tb_sum; ++q) tbij += part[q];
       }
       s3 += ex2(cU - fmaxf(A[j], Bv[i])) * tbij;
     }
   }
   float S = block_sum(s3, red);
-  if (tid == 0) red[0] = S;
+  if (tid == 0) red[0] = part3_ready ? sc.part3[size_t(z) * NB + U] : S;
   __syncthreads();
   S = red[0];
   // part1 as an exclusive scan over s of W_s 2^{-c_s} kept as (m, v) = v 2^m with a running maximum m (the
@@ -464,7 +559,22 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
 }
 
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
-                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s) {
+                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s, int* launched) {
+  // Beyond kPart3CubicMaxNB tiles (or with FPA_B200_DPHI_QUADRATIC set, which the tests use to reach it at small
+  // sizes) dphi_part3_kernel evaluates the strictly-between part first, in O(NB^2).
+  const bool quadratic = d.NB > kPart3CubicMaxNB || std::getenv("FPA_B200_DPHI_QUADRATIC") != nullptr;
+  *launched = 0;
+  if (quadratic) {
+    int lv = 1;
+    while ((1 << lv) <= d.NB) ++lv;  // levels of the range-maximum table: 2^(lv - 1) <= NB < 2^lv
+    const size_t smem3 = size_t(lv) * d.NB * sizeof(float);
+    if (smem3 > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(dphi_part3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3));
+      if (e != cudaSuccess) return e;
+    }
+    dphi_part3_kernel<<<d.BH(), 1024, smem3, s>>>(st.bmin, d.NB, lv, kLog2e / tau, sc);
+    *launched += 1;
+  }
   int threads = d.BT < 32 ? 32 : d.BT;
   size_t smem = (3 * size_t(d.NB) + 2 * d.BT + 32) * sizeof(float);
   if (smem > 48 * 1024) {
@@ -472,7 +582,8 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
     if (e != cudaSuccess) return e;
   }
   dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
-                                                        dphi, dbeta);
+                                                        dphi, dbeta, quadratic ? 1 : 0);
+  *launched += 1;
   return cudaGetLastError();
 }
 

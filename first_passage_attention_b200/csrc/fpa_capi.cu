@@ -49,7 +49,9 @@ int pick_path(int requested, int dtype, int D) {
 
 int tile_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcBT : fpa::kSimtBT; }
 
-int tb_parts_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcTbParts : 1; }
+// Floats per tile pair of the TB array: the tensor-core kv-pass writes 8 per-warp partial sums, the FFMA one a
+// single total into a slot of 2 (the O(NB^2) part-3 passes of the dphi combination reuse two floats per pair).
+int tb_parts_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcTbParts : 2; }
 
 // The backward follows the same choice as the forward: tensor cores for fp16 with a supported D, FFMA otherwise.
 int bwd_path(int requested, int dtype, int D) { return pick_path(requested, dtype, D); }
@@ -178,9 +180,10 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
     ++n;
   }
   fpa::prof_mark(s, "dphi");
-  e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, a->dbeta, s);  // also reduces dbeta
+  int nd = 0;
+  e = fpa::launch_dphi(a->phi, a->beta, d, a->tau, st, sc, a->dphi, a->dbeta, s, &nd);  // also reduces dbeta
   if (e != cudaSuccess) return cuda_fail(e, "dphi kernel");
-  ++n;
+  n += nd;
   fpa::prof_mark(s, nullptr);
   a->kernels_launched = n;
   a->path_taken = path;

@@ -104,9 +104,11 @@ struct BwdScratch {
   float* w;      // [BH][TP]   soft-min partial sums per key, normalised by 2^{c_s} (part "key tile")
   float* dphi2;  // [BH][TP]   soft-min contribution of u in the query's tile
   float* dphi4;  // [BH][TP]   soft-min contribution of u in the diagonal tile
-  float* tb;     // [BH][NB][NB][tb_parts] tile-pair totals, normalised by 2^{cmid}, as tb_parts partial sums
+  float* tb;     // [BH][NB][NB][tb_parts] tile-pair totals, normalised by 2^{cmid}, as tb_sum partial sums
   float* dbeta;  // [BH][NB]   dbeta partial per key tile
-  int tb_parts;  // partial sums per tile pair (summed in a fixed order by the dphi kernel)
+  float* part3;  // [BH][NB]   long contexts: the strictly-between part of dphi per tile, before 2^{a2_u - c_U}
+  int tb_parts;  // floats per tile pair (at least 2: the O(NB^2) part-3 passes reuse two of them)
+  int tb_sum;    // partial sums per tile pair that the kv-pass writes (summed in a fixed order)
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }

@@ -70,8 +70,9 @@ cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pr
 // 16-byte aligned rows and D <= 128; otherwise launch_delta + launch_qv_pack.
 bool qv_delta_fusable(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d);
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s);
+// dphi_kernel, which also reduces dbeta; for long contexts dphi_part3_kernel first. Sets *launched.
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
-                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s);
+                        const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s, int* launched);
 
 // fpa_simt.cu (FFMA kernels, tiles of 64 positions, any supported D, fp16 or fp32 inputs)
 constexpr int kSimtBT = 64;

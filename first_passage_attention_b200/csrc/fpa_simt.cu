@@ -316,7 +316,7 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
         if (threadIdx.x == 0) {
           float tot = 0.f;
           for (int w = 0; w < nw; ++w) tot += red[w];
-          sc.tb[(size_t(z) * NB + i) * NB + j] = tot;
+          sc.tb[((size_t(z) * NB + i) * NB + j) * sc.tb_parts] = tot;
         }
       }
       mid = fminf(mid, st.bmin[size_t(z) * NB + i]);

@@ -197,6 +197,27 @@ def test_forward_backward_replayed_from_a_cuda_graph():
         os.environ.pop("FPA_B200_PATH", None)
 
 
+@pytest.mark.parametrize("path", ["tensor", "simt"])
+def test_long_context_dphi_combination(path):
+    """The O(NB^2) evaluation of dphi's strictly-between part (dphi_part3_kernel, which runs on its own beyond 256
+    tiles) forced at T = 2048 (16 tiles on the tensor-core path, 32 on the FFMA path): against the oracle and against
+    the O(NB^3) evaluation; every other output is bit-identical."""
+    need_gpu()
+    inp = make_inputs(1, 3, 2048, 64, seed=900)
+    cubic = run_kernel(*inp, path=path)
+    os.environ["FPA_B200_DPHI_QUADRATIC"] = "1"
+    try:
+        quad = run_kernel(*inp, path=path)
+    finally:
+        os.environ.pop("FPA_B200_DPHI_QUADRATIC", None)
+    check(quad, run_oracle(*inp), torch.float16)
+    for name, x, y in zip(NAMES, quad, cubic):
+        if name == "dphi":
+            assert (x - y).abs().max() <= 1e-5 * y.abs().max()
+        else:
+            assert torch.equal(x, y), name
+
+
 def config3_inputs(D, dtype, seed):
     """Benchmark configuration 3: B2 H8 T1000; phi = cumsum N(-0.05, 1); psi = phi + N(0,1); beta = softplus(N)."""
     g = torch.Generator().manual_seed(seed)
