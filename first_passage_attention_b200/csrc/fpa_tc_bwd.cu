@@ -387,26 +387,26 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         __syncwarp();
         ++nx;
       }
-      // Without room in TMEM, K and V go to shared memory, after the unit's first tiles and once the previous
-      // unit's last S^T / dP^T products (the last readers of that memory) are complete. s_last completes once per
+      // Without room in TMEM, K and V go to shared memory as soon as the previous unit's last S^T / dP^T products
+      // (the last readers of that memory) are complete, ahead of the unit's tiles: that happens while the rows
+      // still work on the previous unit's last tiles, so the copy is hidden behind them. s_last completes once per
       // unit and is waited here in unit order, and its next phase needs this unit's K and V, so the parity test
-      // cannot see an older phase.
-      const int kst = nsteps < C::NS ? nsteps : C::NS;
-      for (int k = 0; k <= nsteps && ok; ++k) {
-        if (!AT && k == kst) {
-          if (u > 0) ok = mbar_wait(s_last, (u - 1) & 1, p.status, 102);
-          if (!ok) break;
-          if (elect_one()) {
-            mbar_expect_tx(a_full, 2 * C::TILEB);
-            for (int bx = 0; bx < C::NBOX; ++bx) {
-              tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
-              tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
-            }
+      // cannot see an older phase. The wait needs nothing from this warp: every tile of the previous unit has been
+      // issued.
+      if constexpr (!AT) {
+        if (u > 0) ok = mbar_wait(s_last, (u - 1) & 1, p.status, 102);
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_expect_tx(a_full, 2 * C::TILEB);
+          for (int bx = 0; bx < C::NBOX; ++bx) {
+            tma_load_4d(smem + C::OFF_A + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, a_full);
+            tma_load_4d(smem + C::OFF_B + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, a_full);
           }
-          __syncwarp();
-          ++nx;
         }
-        if (k == nsteps) break;
+        __syncwarp();
+        ++nx;
+      }
+      for (int k = 0; k < nsteps && ok; ++k) {
         const int st = gk % C::NS, i = j + k;
         if (gk >= C::NS) ok = mbar_wait(st_empty + st, ((gk / C::NS) - 1) & 1, p.status, 101);
         if (!ok) break;
