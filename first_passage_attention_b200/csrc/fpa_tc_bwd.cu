@@ -812,9 +812,10 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         const float sv_ = ex2(sufl_s - rs) + ex2(midl - rs);
         // 2^{PREL_t - rs} = prey_t * 2^{BL_i - rs} when both factors stay in range (no exp2 per element).
         // Warp-uniform: the chunk body holds warp-collective TMEM loads and stores, so the whole warp takes the
-        // factorised path or none of it does.
-        const bool fact = __all_sync(0xffffffffu, vrs && preri <= 120.f && bli - rs <= 120.f);
-        const float xfac = fact ? ex2(bli - rs) : 0.f;
+        // factorised path or none of it does. Keys without a soft-min sum on this tile (!vrs: the last key of the
+        // tile on the first tile past the diagonal) discard their denominators, so they take either path.
+        const bool fact = __all_sync(0xffffffffu, !vrs || (preri <= 120.f && bli - rs <= 120.f));
+        const float xfac = (fact && vrs) ? ex2(bli - rs) : 0.f;
         const float2 xf2 = make_float2(xfac, xfac), sv2 = make_float2(sv_, sv_);
         const int tvalid = p.T - i * kBT;  // queries c < tvalid exist (padded ones carry lse = +inf: P = 0)
         // Off the diagonal x_ts = min(a_s, PRE_t - psi_s) with a_s = min(SUF_s - psi_s, mid - psi_s): x_ts <= 0 iff
