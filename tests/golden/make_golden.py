@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this folder from the reference implementation itself.
 
-Run in a container where the reference checkout is available (path in FPA_REFERENCE, default /root/reference):
+Run where the reference checkout is available, with its path in FPA_REFERENCE:
 
-    python tests/golden/make_golden.py
+    FPA_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference ``kernel.py`` and evaluates its float64 PyTorch path (``impl="reference"``,
 ``kernel.py:44-64``) with torch autograd on seeded inputs drawn as the reference tests draw them (``test.py:108-117``)
@@ -16,10 +16,12 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("FPA_REFERENCE", "/root/reference")
+REF = os.environ.get("FPA_REFERENCE")
 
 
 def _reference():
+    if not REF:
+        raise SystemExit("set FPA_REFERENCE to the reference checkout (the folder holding its kernel.py)")
     sys.path.insert(0, REF)
     import kernel  # noqa: E402  (the reference module)
     return kernel
