@@ -130,6 +130,33 @@ def test_reference_layer_matches_golden():
         assert ((g - ref).norm() / ref.norm()).item() < 1e-4, n
 
 
+def _reference_layer_and_input(T=50, seed=0):
+    torch.manual_seed(seed)
+    layer = FirstPassageAttention(64, 4, impl="reference")
+    x = torch.randn(2, T, 64, generator=torch.Generator().manual_seed(seed + 1))
+    return layer, x
+
+
+def test_reference_layer_is_causal():
+    """test.py:184-190: changing the input after position t0 leaves the layer's outputs up to t0 unchanged (the
+    field's cumulative sum and the bias's range minimum only look backwards)."""
+    layer, x = _reference_layer_and_input()
+    t0 = 30
+    x2 = x.clone()
+    x2[:, t0 + 1:] = torch.randn(x2[:, t0 + 1:].shape, generator=torch.Generator().manual_seed(7)) * 5
+    with torch.no_grad():
+        assert torch.allclose(layer(x)[:, :t0 + 1], layer(x2)[:, :t0 + 1], rtol=0, atol=1e-6)
+
+
+def test_reference_layer_gradients_reach_every_parameter():
+    """test.py:193-197: every named parameter (qkv, out, field.proj, field.beta_raw) gets a finite, non-zero
+    gradient through the bias."""
+    layer, x = _reference_layer_and_input()
+    layer(x).square().mean().backward()
+    for name, p in layer.named_parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all() and p.grad.abs().max() > 0, name
+
+
 def test_layer_rejects_bad_head_split():
     with pytest.raises(ValueError, match="multiple of n_heads"):
         FirstPassageAttention(65, 4)
