@@ -43,12 +43,12 @@ def _stream(device):
 
 def _tma_ready(t):
     """True if a [B, H, T, D] fp16 tensor can be described by a TMA tensor map as it is (innermost stride 1,
-    16-byte aligned base and strides)."""
+    16-byte aligned base, positive 16-byte multiple outer strides; a broadcast view has stride 0 and is copied)."""
     if t.dtype != torch.float16 or t.stride(-1) != 1:
         return False
     if t.data_ptr() % 16:
         return False
-    return all((s * 2) % 16 == 0 for s in t.stride()[:3])
+    return all(s > 0 and (s * 2) % 16 == 0 for s in t.stride()[:3])
 
 
 def _prep_qkv(x, path):
@@ -108,6 +108,10 @@ def fpa_backward(q, k, v, o, lse, phi, psi, beta, do, tau, path=None):
     lib = _lib.load()
     path = _path_from_env() if path is None else path
     B, H, T, D = q.shape
+    # q, k, v are the tensors the caller gave the forward (which copied any that TMA cannot describe), and the
+    # gradient of o.sum() arrives as a broadcast view (all strides 0). The reference's backward works on contiguous
+    # copies too: q, k, v padded in its forward and dO padded on entry (kernel.py:380-384, 402, 429).
+    q, k, v, do = (_prep_qkv(x, path) for x in (q, k, v, do))
     dq, dk, dv = (torch.empty((B, H, T, D), dtype=q.dtype, device=q.device) for _ in range(3))
     dphi = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
     dpsi = torch.empty_like(dphi)

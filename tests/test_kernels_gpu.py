@@ -274,6 +274,47 @@ def test_strided_qkv_views():
     check(run_kernel(q, k, v, phi, psi, beta, do), run_oracle(q, k, v, phi, psi, beta, do), torch.float16)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_keys_and_values_shared_across_heads(dtype):
+    """k and v given as one head broadcast over all heads (expand, head stride 0): the result equals the oracle's on
+    the repeated tensors and, bit for bit, the kernels' own result on contiguous copies."""
+    need_gpu()
+    B, H, T, D = 1, 3, 200, 64
+    q, k, v, phi, psi, beta, do = make_inputs(B, H, T, D, seed=61, dtype=dtype)
+    k, v = (x[:, :1].expand(B, H, T, D) for x in (k, v))
+    xs = [t.cuda().requires_grad_() for t in (q, k[:, :1], v[:, :1], phi, psi, beta)]
+    kb, vb = (x.expand(B, H, T, D) for x in xs[1:3])
+    ins = [xs[0], kb, vb] + xs[3:]
+    o = first_passage_attention(*ins, impl="triton")
+    kern = [o.detach().cpu()] + [g.cpu() for g in torch.autograd.grad(o, ins, do.cuda())]
+    torch.cuda.synchronize()
+    check(kern, run_oracle(q, k.contiguous(), v.contiguous(), phi, psi, beta, do), dtype)
+    again = run_kernel(q, k.contiguous(), v.contiguous(), phi, psi, beta, do)
+    for name, a, b in zip(NAMES, kern, again):
+        assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("path", ["auto", "tensor", "simt"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_backward_of_the_sum(dtype, path):
+    """o.sum().backward(), the step of the CPU configuration: autograd hands the backward a broadcast gradient of
+    ones with all strides 0; the result equals the oracle's with grad_o = ones."""
+    need_gpu()
+    if path == "tensor" and dtype != torch.float16:
+        pytest.skip("the tensor-core kernels take fp16")
+    q, k, v, phi, psi, beta, _ = make_inputs(2, 3, 300, 64, seed=51, dtype=dtype)
+    os.environ["FPA_B200_PATH"] = path
+    try:
+        a = [t.cuda().clone().requires_grad_() for t in (q, k, v, phi, psi, beta)]
+        o = first_passage_attention(*a, impl="triton")
+        o.sum().backward()
+        torch.cuda.synchronize()
+        kern = [o.detach().cpu()] + [x.grad.cpu() for x in a]
+    finally:
+        os.environ.pop("FPA_B200_PATH", None)
+    check(kern, run_oracle(q, k, v, phi, psi, beta, torch.ones(q.shape, dtype=dtype)), dtype)
+
+
 def test_long_context_prefix():
     """Configuration 4 (B1 H16 T16383 D128 fp16) at full size. With do = 0 beyond T0 every output and gradient of
     the first T0 positions equals that of the truncated problem (the operator is causal), so the full-size run is
