@@ -70,7 +70,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
                              const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
-  const int j = blockIdx.x, z = blockIdx.y;
+  const int j = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (NB, H, B): z = b * H + h
   if (j == 0 && z == 0 && tid < 4 && status) status[tid] = 0;  // status word and the work-unit counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
@@ -213,7 +213,7 @@ cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, 
                          const Fact* fact, const QvIn* qv) {
   const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   const QvIn q = qv ? *qv : QvIn{nullptr, Str4{0, 0, 0, 0}, nullptr, Str4{0, 0, 0, 0}, nullptr, nullptr, 0};
-  stats_kernel<<<dim3(d.NB, d.BH()), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
+  stats_kernel<<<dim3(d.NB, d.H, d.B), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
                                                    cols_scaled, beta, d.H, f, status, q);
   return cudaGetLastError();
 }
@@ -454,7 +454,7 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
   float* Ws = Bv + NB;      // [BT]
   float* c2s = Ws + BT;     // [BT]
   float* red = c2s + BT;    // [32]
-  const int U = blockIdx.x, z = blockIdx.y, h = z % H;
+  const int U = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y, h = z % H;  // grid (NB, H, B)
   const int tid = threadIdx.x;
   const size_t TP = size_t(NB) * BT;
   for (int n = tid; n < NB; n += blockDim.x) cb[n] = -st.bmin[size_t(z) * NB + n] * il2;
@@ -581,7 +581,7 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
     cudaError_t e = cudaFuncSetAttribute(dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  dphi_kernel<<<dim3(d.NB, d.BH()), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
+  dphi_kernel<<<dim3(d.NB, d.H, d.B), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
                                                         dphi, dbeta, quadratic ? 1 : 0);
   *launched += 1;
   return cudaGetLastError();
@@ -605,7 +605,7 @@ diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, in
   extern __shared__ float dsm[];
   float* G = dsm;           // [BT][BT+1]
   float* a2 = G + BT * LD;  // [BT]
-  const int j = blockIdx.x, z = blockIdx.y, sl = threadIdx.x, wq = sl >> 5;
+  const int j = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y, sl = threadIdx.x, wq = sl >> 5;  // grid (NB, H, B)
   const size_t TP = size_t(NB) * BT;
   const float4* g4 = reinterpret_cast<const float4*>(gd + (size_t(z) * NB + j) * BT * BT);
   // All 32 loads of the thread in flight before the first store (the tile is 64 KB).
@@ -683,7 +683,7 @@ cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, f
   const int smem = (kDiagBT * (kDiagBT + 1) + kDiagBT) * int(sizeof(float));
   cudaError_t e = cudaFuncSetAttribute(diag_dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  diag_dphi_kernel<<<dim3(d.NB, d.BH()), kDiagBT, smem, s>>>(phi, gd, d.T, d.NB, kLog2e / tau, dphi4);
+  diag_dphi_kernel<<<dim3(d.NB, d.H, d.B), kDiagBT, smem, s>>>(phi, gd, d.T, d.NB, kLog2e / tau, dphi4);
   return cudaGetLastError();
 }
 

@@ -28,6 +28,9 @@ int check_common(int dtype, int B, int H, int T, int D, float tau) {
   if (B <= 0 || H <= 0 || T <= 0) return fail(FPA_ERR_INVALID_ARGUMENT, "q, k and v must have the same shape (B, H, T, D)");
   if (!pow2_ge16(D)) return fail(FPA_ERR_INVALID_ARGUMENT, "the head dimension and the block must be powers of two >= 16");
   if (D > 256) return fail(FPA_ERR_UNSUPPORTED, "head dimensions above 256 are not supported");
+  // Per-head kernels run on a (tiles, H, B) grid, whose y and z extents stop at 65535; row indices are 32-bit.
+  if (B > 65535 || H > 65535) return fail(FPA_ERR_UNSUPPORTED, "B and H above 65535 are not supported");
+  if (int64_t(B) * H * T > INT32_MAX) return fail(FPA_ERR_UNSUPPORTED, "B * H * T above 2^31 - 1 is not supported");
   if (!(tau > 0.f)) return fail(FPA_ERR_INVALID_ARGUMENT, "tau must be positive");
   return FPA_OK;
 }

@@ -52,7 +52,7 @@ simt_fwd_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k, S
   float* sufs = phis + BT;
 
   const int i = NB - 1 - blockIdx.x;  // longest query tiles first (kernel.py:108)
-  const int z = blockIdx.y, b = z / H, h = z % H;
+  const int z = blockIdx.z * gridDim.y + blockIdx.y, b = z / H, h = z % H;  // grid (NB, H, B)
   const int tl = threadIdx.x / TPR, sub = threadIdx.x % TPR, c0 = sub * CPT;
   const int t = i * BT + tl;
   const size_t TP = size_t(NB) * BT;
@@ -179,7 +179,7 @@ simt_bwd_kv_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k
   float* red = Ls + BT * LD; // [32]
 
   const int j = blockIdx.x;  // key tile 0 has the most query tiles: launched first
-  const int z = blockIdx.y, b = z / H, h = z % H;
+  const int z = blockIdx.z * gridDim.y + blockIdx.y, b = z / H, h = z % H;  // grid (NB, H, B)
   const int sl = threadIdx.x / TPR, sub = threadIdx.x % TPR, c0 = sub * CPT;
   const int s = j * BT + sl;
   const bool s_ok = s < T;
@@ -372,7 +372,7 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
   float* c2t = rr + BT;
 
   const int i = NB - 1 - blockIdx.x;
-  const int z = blockIdx.y, b = z / H, h = z % H;
+  const int z = blockIdx.z * gridDim.y + blockIdx.y, b = z / H, h = z % H;  // grid (NB, H, B)
   const int tl = threadIdx.x / TPR, sub = threadIdx.x % TPR, c0 = sub * CPT;
   const int t = i * BT + tl;
   const bool t_ok = t < T;
@@ -501,7 +501,7 @@ static cudaError_t simt_fwd_t(const FpaFwdArgs& a, const Dims& d, const Stats& s
   size_t smem = fwd_smem<D>();
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
-  fn<<<dim3(d.NB, d.BH()), SimtShape<D>::THREADS, smem, s>>>(
+  fn<<<dim3(d.NB, d.H, d.B), SimtShape<D>::THREADS, smem, s>>>(
       (const TIn*)a.q, str4(a.q_stride), (const TIn*)a.k, str4(a.k_stride), (const TIn*)a.v, str4(a.v_stride),
       a.phi, a.psi, a.beta, st, (TIn*)a.o, str4(a.o_stride), a.lse, d.H, d.T, d.NB,
       float(1.0 / sqrt(double(D))) * kLog2e);
@@ -515,7 +515,7 @@ static cudaError_t simt_kv_t(const FpaBwdArgs& a, const Dims& d, const Stats& st
   size_t smem = kv_smem<D>();
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
-  fn<<<dim3(d.NB, d.BH()), SimtShape<D>::THREADS, smem, s>>>(
+  fn<<<dim3(d.NB, d.H, d.B), SimtShape<D>::THREADS, smem, s>>>(
       (const TIn*)a.q, str4(a.q_stride), (const TIn*)a.k, str4(a.k_stride), (const TIn*)a.v, str4(a.v_stride),
       (const TIn*)a.dout, str4(a.dout_stride), a.lse, a.phi, a.psi, a.beta, st, sc, (TIn*)a.dk, str4(a.dk_stride),
       (TIn*)a.dv, str4(a.dv_stride), a.dpsi, d.H, d.T, d.NB, float(1.0 / sqrt(double(D))), kLog2e / a.tau);
@@ -529,7 +529,7 @@ static cudaError_t simt_q_t(const FpaBwdArgs& a, const Dims& d, const Stats& st,
   size_t smem = q_smem<D>();
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
-  fn<<<dim3(d.NB, d.BH()), SimtShape<D>::THREADS, smem, s>>>(
+  fn<<<dim3(d.NB, d.H, d.B), SimtShape<D>::THREADS, smem, s>>>(
       (const TIn*)a.q, str4(a.q_stride), (const TIn*)a.k, str4(a.k_stride), (const TIn*)a.v, str4(a.v_stride),
       (const TIn*)a.dout, str4(a.dout_stride), a.lse, a.phi, a.psi, a.beta, st, sc, (TIn*)a.dq, str4(a.dq_stride),
       d.H, d.T, d.NB, float(1.0 / sqrt(double(D))), kLog2e / a.tau);

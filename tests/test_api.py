@@ -47,6 +47,12 @@ def test_workspace_queries_and_argument_errors():
     assert lib.fpa_fwd(ctypes.byref(a), None) == _lib.ERR_INVALID                 # null pointers
     b = _lib.FpaBwdArgs(dtype=_lib.DTYPE_F32, path=0, B=1, H=1, T=64, D=24, tau=1.0)
     assert lib.fpa_bwd(ctypes.byref(b), None) == _lib.ERR_INVALID
+    # Grid limits, as the reference's (tiles, H, B) launches have them: B and H up to 65535 each.
+    assert lib.fpa_fwd_workspace_bytes(_lib.DTYPE_F16, 2, 33000, 20, 16, 0) > 0   # B * H above 65535 is fine
+    assert lib.fpa_bwd_workspace_bytes(_lib.DTYPE_F16, 1, 70000, 20, 16, 0) == 0
+    a = _lib.FpaFwdArgs(dtype=_lib.DTYPE_F32, path=0, B=70000, H=1, T=20, D=16, tau=1.0)
+    assert lib.fpa_fwd(ctypes.byref(a), None) == _lib.ERR_UNSUPPORTED and b"65535" in lib.fpa_last_error()
+    assert lib.fpa_fwd_workspace_bytes(_lib.DTYPE_F16, 65535, 65535, 1, 16, 0) == 0  # B * H * T above 2^31 - 1
     assert lib.fpa_status_string(_lib.ERR_TIMEOUT) == b"device-side wait timed out"
     with pytest.raises(ValueError):
         _lib.check(_lib.ERR_INVALID)

@@ -294,6 +294,26 @@ def test_keys_and_values_shared_across_heads(dtype):
         assert torch.equal(a, b), name
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_more_than_65535_heads(dtype):
+    """B * H = 66000 heads (the per-head kernels' grid is (tiles, H, B), as the reference's is): every head's
+    output and gradients equal, bit for bit, those of a run on a slice of the heads alone, and the oracle's."""
+    need_gpu()
+    B, H, T, D = 2, 33000, 20, 16
+    inp = make_inputs(B, H, T, D, seed=71, dtype=dtype)
+    full = run_kernel(*inp)
+    for sl in (slice(0, 40), slice(H - 40, H)):
+        part_inp = [x[:, sl].contiguous() if x.dim() > 1 else x[sl].contiguous() for x in inp]
+        part = run_kernel(*part_inp)
+        for name, a, b in zip(NAMES, full, part):
+            a = a[sl] if name == "dbeta" else a[:, sl]
+            if name == "dbeta":
+                assert torch.allclose(a, b, rtol=1e-6, atol=0), name
+            else:
+                assert torch.equal(a, b), name
+    check(part, run_oracle(*part_inp), dtype)
+
+
 @pytest.mark.parametrize("path", ["auto", "tensor", "simt"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_backward_of_the_sum(dtype, path):
