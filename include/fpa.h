@@ -56,7 +56,7 @@ enum FpaStatus {
 typedef struct FpaFwdArgs {
   int32_t dtype;            /* FpaDtype */
   int32_t path;             /* FpaPath */
-  int32_t B, H, T, D;       /* D in {16, 32, 64, 128, 256} (kernel.py:476: a power of two >= 16) */
+  int32_t B, H, T, D;       /* D in {16, 32, 64, 128, 256} (kernel.py:476: a power of two >= 16); B, H <= 65535; B*H*T < 2^31 */
   float tau;                /* soft-min temperature, > 0 (enters only the backward pass) */
   const void* q; int64_t q_stride[4];
   const void* k; int64_t k_stride[4];
