@@ -136,6 +136,27 @@ def test_reference_layer_matches_golden():
         assert ((g - ref).norm() / ref.norm()).item() < 1e-4, n
 
 
+def test_layout_preparation_for_the_tensor_core_path():
+    """Which q, k, v, dO views go to the tensor-core kernels as they are (TMA tensor maps need unit innermost
+    stride and positive 16-byte-multiple outer strides) and which are copied first; the FFMA path copies nothing."""
+    from first_passage_attention_b200 import ops
+    B, T, H, D = 2, 130, 4, 32
+    qkv = torch.zeros(B, T, 3, H, D, dtype=torch.float16)
+    q = qkv.permute(2, 0, 3, 1, 4)[0]                     # the layer's view of the fused projection
+    assert ops._tma_ready(q) and ops._prep_qkv(q, _lib.PATH_AUTO) is q
+    k = torch.zeros(B, 1, T, D, dtype=torch.float16).expand(B, H, T, D)    # one head shared by all heads
+    assert not ops._tma_ready(k)
+    kc = ops._prep_qkv(k, _lib.PATH_TENSOR)
+    assert kc.is_contiguous() and kc.shape == k.shape
+    do = torch.ones((), dtype=torch.float16).expand(B, H, T, D)            # the gradient of o.sum()
+    assert not ops._tma_ready(do) and ops._prep_qkv(do, _lib.PATH_AUTO).is_contiguous()
+    assert ops._prep_qkv(do, _lib.PATH_SIMT) is do
+    odd = torch.zeros(B, H, T, D + 1, dtype=torch.float16)[..., :D]          # rows not 16-byte multiples
+    assert not ops._tma_ready(odd) and ops._prep_qkv(odd, _lib.PATH_AUTO).is_contiguous()
+    f32 = torch.zeros(B, 1, T, D).expand(B, H, T, D)
+    assert ops._prep_qkv(f32, _lib.PATH_AUTO) is f32     # fp32 runs on the FFMA kernels, which take any strides
+
+
 def _reference_layer_and_input(T=50, seed=0):
     torch.manual_seed(seed)
     layer = FirstPassageAttention(64, 4, impl="reference")
