@@ -18,7 +18,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE = range(6
 # Exported symbols, in the order include/fpa.h declares them.
 EXPORTS = ("fpa_abi_version", "fpa_struct_size", "fpa_fwd_workspace_bytes", "fpa_bwd_workspace_bytes", "fpa_fwd",
            "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_profile",
-           "fpa_profile_report", "fpa_fwd_noalloc")
+           "fpa_profile_report", "fpa_selftest_wait_timeout", "fpa_fwd_noalloc")
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _c_i64x4 = ctypes.c_int64 * 4
@@ -93,6 +93,8 @@ def load():
         lib.fpa_profile.argtypes = [ctypes.c_int]
         lib.fpa_profile_report.restype = ctypes.c_int
         lib.fpa_profile_report.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+        lib.fpa_selftest_wait_timeout.restype = ctypes.c_int
+        lib.fpa_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
         lib.fpa_fwd_noalloc.restype = ctypes.c_int
         lib.fpa_fwd_noalloc.argtypes = [ctypes.POINTER(FpaFwdArgs), ctypes.c_void_p]
         if lib.fpa_abi_version() != ABI_VERSION:

@@ -569,7 +569,7 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
     while ((1 << lv) <= d.NB) ++lv;  // levels of the range-maximum table: 2^(lv - 1) <= NB < 2^lv
     const size_t smem3 = size_t(lv) * d.NB * sizeof(float);
     if (smem3 > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(dphi_part3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3));
+      cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(dphi_part3_kernel), int(smem3));
       if (e != cudaSuccess) return e;
     }
     dphi_part3_kernel<<<d.BH(), 1024, smem3, s>>>(st.bmin, d.NB, lv, kLog2e / tau, sc);
@@ -578,7 +578,7 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
   int threads = d.BT < 32 ? 32 : d.BT;
   size_t smem = (3 * size_t(d.NB) + 2 * d.BT + 32) * sizeof(float);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(dphi_kernel), int(smem));
     if (e != cudaSuccess) return e;
   }
   dphi_kernel<<<dim3(d.NB, d.H, d.B), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
@@ -681,7 +681,7 @@ diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, in
 cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, float tau, float* dphi4, cudaStream_t s) {
   if (d.BT != kDiagBT) return cudaErrorInvalidValue;
   const int smem = (kDiagBT * (kDiagBT + 1) + kDiagBT) * int(sizeof(float));
-  cudaError_t e = cudaFuncSetAttribute(diag_dphi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(diag_dphi_kernel), smem);
   if (e != cudaSuccess) return e;
   diag_dphi_kernel<<<dim3(d.NB, d.H, d.B), kDiagBT, smem, s>>>(phi, gd, d.T, d.NB, kLog2e / tau, dphi4);
   return cudaGetLastError();

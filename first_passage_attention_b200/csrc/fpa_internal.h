@@ -46,6 +46,11 @@ inline Dims make_dims(int B, int H, int T, int D, int BT) {
 void prof_mark(cudaStream_t s, const char* name);
 bool prof_on();  // per-kernel timing enabled (the library then launches everything on the caller's stream)
 
+// cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, bytes) on the current device, made once per (device,
+// kernel) with the largest size asked for so far; later calls that ask for no more cost a lock and a lookup
+// (fpa_tma.cu). Thread-safe.
+cudaError_t allow_dynamic_smem(const void* fn, int bytes);
+
 // Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
 void set_last_error(const std::string& msg);
 

@@ -492,7 +492,7 @@ static size_t q_smem() { return (2 * size_t(kSimtBT) * D + 6 * kSimtBT) * sizeof
 template <typename F>
 static cudaError_t allow_smem(F* fn, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  return allow_dynamic_smem(reinterpret_cast<const void*>(fn), int(bytes));
 }
 
 template <typename TIn, int D>

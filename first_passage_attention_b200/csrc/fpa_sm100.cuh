@@ -74,17 +74,22 @@ __device__ __forceinline__ uint64_t global_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr uint32_t kSuspendHintNs = 100000;       // 0.1 ms
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, int site,
+                                                uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait_sleep(addr, parity, kSuspendHintNs)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       report_timeout(status, site);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site) {
+  return mbar_wait_limit(bar, parity, status, site, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------------------------------------- TMA ------

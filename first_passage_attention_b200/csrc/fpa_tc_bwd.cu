@@ -1555,8 +1555,8 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
   auto kv = tc_bwd_kv_kernel<D>;
   auto qk = tc_bwd_q_kernel<D>;
   const int smem_kv = std::max(CK::SMEM, kPersistentMinSmem), smem_q = std::max(CQ::SMEM, kPersistentMinSmem);
-  cudaError_t e = cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(kv), smem_kv);
+  if (e == cudaSuccess) e = allow_dynamic_smem(reinterpret_cast<const void*>(qk), smem_q);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core backward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;

@@ -463,7 +463,7 @@ int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
     return FPA_ERR_CUDA;
   }
   auto fn = tc_fwd_kernel<D>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(fn), C::SMEM);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;

@@ -2,6 +2,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <vector>
 
 #include "fpa_tc.h"
 
@@ -24,14 +25,43 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }  // namespace
 
 int sm_count() {
+  static std::mutex mu;
   static int cache[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
-  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && cache[dev] > 0) return cache[dev];
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  std::lock_guard<std::mutex> lock(mu);
   if (dev < 64) cache[dev] = n;
   return n;
+}
+
+cudaError_t allow_dynamic_smem(const void* fn, int bytes) {
+  struct Entry {
+    int dev;
+    const void* fn;
+    int bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (Entry& x : done)
+    if (x.dev == dev && x.fn == fn) {
+      if (x.bytes >= bytes) return cudaSuccess;
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e == cudaSuccess) x.bytes = bytes;
+      return e;
+    }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.push_back(Entry{dev, fn, bytes});
+  return e;
 }
 
 bool tma_layout_ok(const void* p, const int64_t st[4]) {

@@ -199,8 +199,10 @@ def first_passage_attention(q, k, v, phi, psi, beta, tau=1.0, impl=None, block=6
 
 
 class Field(nn.Module):
-    """phi = W + g, psi = W + h with W = cumsum(delta), and beta = softplus(beta_raw), per head, from x (B, T, d_model).
-    delta, g and h are linear maps of x, computed in fp32 (kernel.py:492-509)."""
+    """The per-head field of the layer (kernel.py:492-509). One fp32 projection of x (B, T, d_model) gives three
+    values per head and position: an increment delta, and offsets g and h. The walk W is the running sum of delta
+    along T; the field is phi = W + g and the levels are psi = W + h, both (B, H, T). The strength is
+    beta = softplus(beta_raw) (H,), positive for any parameter value."""
 
     def __init__(self, d_model, n_heads, beta_init=1.0):
         super().__init__()
@@ -220,7 +222,9 @@ class Field(nn.Module):
 
 
 class FirstPassageAttention(nn.Module):
-    """Multi-head causal FPA without positional encoding: x (B, T, d_model) -> (B, T, d_model) (kernel.py:512-530).
+    """Self-attention layer with the first-passage bias in place of a positional encoding (kernel.py:512-530):
+    x (B, T, d_model) goes through one bias-free projection to q, k, v of n_heads heads, a Field gives phi, psi and
+    beta, the operator combines them, and a bias-free output projection maps the heads back to d_model.
 
     The q, k, v views of the fused projection are passed to the kernels with their strides (no copy)."""
 

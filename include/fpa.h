@@ -136,19 +136,29 @@ FPA_API const char* fpa_last_error(void);
 FPA_API int fpa_profile(int enable);
 FPA_API int fpa_profile_report(char* buf, size_t len);
 
+/* Failure-path self-test of the bounded device-side waits. Launches one warp on `stream` that waits, through the
+ * same bounded mbarrier wait every tensor-core kernel uses, on an mbarrier nothing ever arrives on, with a limit of
+ * limit_ns nanoseconds (0 < limit_ns <= 1e9); the wait runs out, records FPA_ERR_TIMEOUT and its site id in the
+ * status word of `workspace` (256 bytes, 256-byte aligned) and the kernel returns. fpa_workspace_status then
+ * reports FPA_ERR_TIMEOUT. It faults and hangs nothing; the context stays usable. No counterpart in the reference
+ * (whose Triton kernels have no bounded waits). */
+FPA_API int fpa_selftest_wait_timeout(void* workspace, unsigned long long limit_ns, void* stream);
+
 /* Size of the scratch array built into the library for fpa_fwd_noalloc (8 MiB per GPU that loads the library). */
 #define FPA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 
 /* Forward pass for callers that cannot allocate device memory (a plugin host that hands over only the input and
  * output buffers, a runtime whose device memory is fully reserved, code that must not allocate after start-up).
  * This entry point has no counterpart in the reference. It runs the same kernels as fpa_fwd, but their scratch
- * lives in a device array that is part of the library image (FPA_NOALLOC_SCRATCH_BYTES, held by every GPU that
- * loads the library until the process exits) instead of a caller workspace: args->workspace and
- * args->workspace_bytes are ignored and overwritten. It allocates nothing. A call whose scratch need
- * (fpa_fwd_workspace_bytes) exceeds FPA_NOALLOC_SCRATCH_BYTES returns FPA_ERR_WORKSPACE with a message and
- * launches nothing. The first call on each device looks up the array's device address (make that first call
- * before any stream capture). All calls share the one array: calls whose kernels overlap on the GPU race and
- * must be serialised by the caller. */
+ * lives in a device array that is part of the library image (FPA_NOALLOC_SCRATCH_BYTES) instead of a caller
+ * workspace: args->workspace and args->workspace_bytes are ignored and overwritten. It calls no allocator. A call
+ * whose scratch need, fpa_fwd_workspace_bytes(dtype, B, H, T, D, path), exceeds FPA_NOALLOC_SCRATCH_BYTES returns
+ * FPA_ERR_WORKSPACE with a message and launches nothing (the need grows with B*H*ceil(T/128)*128, about 28 bytes
+ * per padded query position on the tensor-core path). The array's address is looked up in the current CUDA
+ * context on every call made outside stream capture; CUDA creates the array on the first lookup in a context
+ * (modules load lazily), so a caller that must not allocate later makes that first lookup at start-up with the
+ * set-up call fpa_fwd_noalloc(NULL, stream), which launches nothing, and before any stream capture. All calls
+ * share the one array: calls whose kernels overlap on the GPU race and must be serialised by the caller. */
 FPA_API int fpa_fwd_noalloc(FpaFwdArgs* args, void* stream);
 
 #ifdef __cplusplus

@@ -70,6 +70,22 @@ def forward(q, k, v, phi, psi, beta):
     return p @ v, (m + np.log(l))[..., 0]
 
 
+def forward_row(q, k, v, phi, psi, beta, t):
+    """o[t] of one head (q, k, v [T, D]; phi, psi [T]; beta a scalar) in O(T*D): the same definition as ``forward``
+    (``kernel.py:44-64``) for one query row. For a fixed t, min_{s<u<=t} phi_u as a function of s is the running
+    minimum of phi taken backwards from t, so the row's bias needs no [T, T] table. Lets long contexts (T = 16383)
+    be checked at late rows at full size."""
+    q, k, v, phi, psi = _f64(q), _f64(k), _f64(v), _f64(phi), _f64(psi)
+    D = q.shape[-1]
+    m = np.empty(t + 1)
+    m[t] = np.inf                                                   # empty range on the diagonal
+    if t > 0:
+        m[:t] = np.minimum.accumulate(phi[1:t + 1][::-1])[::-1]     # m[s] = min(phi[s+1 .. t])
+    s = k[:t + 1] @ q[t] * D ** -0.5 + float(beta) * np.minimum(m - psi[:t + 1], 0.0)
+    e = np.exp(s - s.max())
+    return (e / e.sum()) @ v[:t + 1]
+
+
 def _softmin_grad_phi(g, phi, tau):
     """R[u] = sum_{s<u<=t} g[t, s] * exp(a_u) / Z_{s,t}, a = -phi/tau, for one head (g: [T, T] indexed [t, s]).
 

@@ -54,6 +54,10 @@ def test_workspace_queries_and_argument_errors():
     assert lib.fpa_fwd(ctypes.byref(a), None) == _lib.ERR_UNSUPPORTED and b"65535" in lib.fpa_last_error()
     assert lib.fpa_fwd_workspace_bytes(_lib.DTYPE_F16, 65535, 65535, 1, 16, 0) == 0  # B * H * T above 2^31 - 1
     assert lib.fpa_status_string(_lib.ERR_TIMEOUT) == b"device-side wait timed out"
+    # The wait-expiry self-test checks its arguments before any CUDA call.
+    assert lib.fpa_selftest_wait_timeout(None, 1000, None) == _lib.ERR_WORKSPACE
+    assert lib.fpa_selftest_wait_timeout(ctypes.c_void_p(256), 0, None) == _lib.ERR_INVALID
+    assert lib.fpa_selftest_wait_timeout(ctypes.c_void_p(256), 2_000_000_000, None) == _lib.ERR_INVALID
     with pytest.raises(ValueError):
         _lib.check(_lib.ERR_INVALID)
 

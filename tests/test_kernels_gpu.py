@@ -358,6 +358,14 @@ def test_long_context_prefix():
     check(got, ref, torch.float16)
     for x in kern[1:6]:  # dq, dk, dv, dphi, dpsi vanish exactly where do (and so dS) is zero
         assert torch.count_nonzero(x[:, :, T0:]) == 0
+    # Late rows of the full-length forward, where the diagonal-backwards walk carries the running minimum of phi
+    # over 31, 63 and 127 key tiles: each against the float64 one-row evaluation (O(T*D) per row).
+    for h in heads:
+        for t in (4095, 8191, 16382):
+            want = O.forward_row(q[0, h].double().numpy(), k[0, h].double().numpy(), v[0, h].double().numpy(),
+                                 phi[0, h].double().numpy(), psi[0, h].double().numpy(), float(beta[h]), t)
+            err = float(np.abs(kern[0][0, h, t].double().numpy() - want).max() / np.abs(want).max())
+            assert err <= TOL[torch.float16], (h, t, err)
 
 
 @pytest.mark.parametrize("amp", [False, True])

@@ -133,3 +133,18 @@ def test_oracle_stable_for_extreme_fields():
     psi = phi + 300 * torch.randn(B, H, T, generator=g, dtype=torch.float64).numpy()
     grads = O.backward(q, k, v, phi, psi, np.ones(H), do)
     assert all(np.isfinite(x).all() for x in grads)
+
+
+@pytest.mark.parametrize("path", CASE_FILES[:3])
+def test_single_row_forward_matches_the_golden_rows(path):
+    """forward_row (the O(T*D) one-row evaluation the long-context GPU test uses) reproduces the reference's own
+    outputs row by row, including the first and last rows."""
+    z = np.load(path)
+    q, k, v, phi, psi, beta = (z[n] for n in ("q", "k", "v", "phi", "psi", "beta"))
+    B, H, T, D = q.shape
+    beta = np.broadcast_to(np.asarray(beta, dtype=np.float64).reshape(-1), (H,))
+    for b in range(B):
+        for h in range(H):
+            for t in sorted({0, 1, T // 2, T - 1}):
+                row = O.forward_row(q[b, h], k[b, h], v[b, h], phi[b, h], psi[b, h], beta[h], t)
+                assert np.allclose(row, z["o"][b, h, t], rtol=0, atol=1e-10 * max(1.0, np.abs(z["o"]).max()))
