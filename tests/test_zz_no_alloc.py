@@ -20,8 +20,6 @@ from first_passage_attention_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
-TOL_FP16 = 2e-3
-
 
 def _inputs(B, H, T, D, seed):
     g = torch.Generator().manual_seed(seed)
@@ -46,10 +44,6 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def _rel_err(x, ref):
-    return ((x.double() - ref.double()).abs().max() / ref.double().abs().max()).item()
-
-
 def test_noalloc_forward_matches_the_workspace_forward():
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA GPU")
@@ -65,21 +59,21 @@ def test_noalloc_forward_matches_the_workspace_forward():
         _lib.check(lib.fpa_fwd(ctypes.byref(a), _stream()))
         o = torch.full_like(q, float("nan"))
         lse = torch.full((B, H, T), float("nan"), device="cuda")
-        cases.append((a, o_ref, lse_ref, _args(q, k, v, phi, psi, beta, o, lse), o, lse))
+        keep = (q, k, v, phi, psi, beta, ws)   # the argument blocks hold raw pointers: keep the tensors alive
+        cases.append((a, o_ref, lse_ref, _args(q, k, v, phi, psi, beta, o, lse), o, lse, keep))
     _lib.check(lib.fpa_fwd_noalloc(None, _stream()))   # set-up: creates the built-in array, launches nothing
-    torch.cuda.synchronize()
-    free_before = torch.cuda.mem_get_info()[0]
-    for a, o_ref, lse_ref, b, o, lse in cases:
+    for a, o_ref, lse_ref, b, o, lse, _ in cases:
+        # Free device memory right around the call (torch's own allocations for the checks come after).
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         _lib.check(lib.fpa_fwd_noalloc(ctypes.byref(b), _stream()))
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] >= free_before
         assert b.workspace is not None                       # the call reports the built-in array it used
         assert lib.fpa_workspace_status(ctypes.c_void_p(b.workspace), _stream()) == _lib.OK
-        torch.cuda.synchronize()
         assert b.kernels_launched == a.kernels_launched > 0
         assert torch.equal(o, o_ref)
         assert torch.equal(lse, lse_ref)
-        assert _rel_err(o, o_ref) <= TOL_FP16
-    torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info()[0] >= free_before
 
 
 def test_noalloc_refuses_calls_beyond_its_scratch():
