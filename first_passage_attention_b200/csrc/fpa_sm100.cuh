@@ -48,6 +48,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (for a thread that polls several barriers).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // try_wait with a suspend-time hint: the thread sleeps until the phase completes or about `hint_ns` passes, so a
 // waiting warp issues almost nothing while it waits.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity, uint32_t hint_ns) {

@@ -452,6 +452,395 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   }
 }
 
+// ------------------------------------------------------------------------------------------------------------
+// One query tile per CTA, two CTAs per SM (D <= 64).
+//
+// The CTA takes query tile i of one head and walks its key tiles j = i, i - 1, ..., 0 (the diagonal first, as
+// above). It holds 256 TMEM columns: S [0, 128), P [128, 192) (fp16 pairs), O [192, 192 + D). Two CTAs share an
+// SM, so one CTA's prologue, pipeline fill and epilogue run while the other computes, and 768 single-tile CTAs
+// (configuration 2) balance over the SMs better than 384 two-tile ones. S has one slot: the softmax hands it back
+// (s_free) as soon as it has read S, and the MMA warp computes the next S meanwhile; P has columns of its own and is
+// rewritten only after the previous P V has completed (o_ready).
+// Warps (256 threads): 0-3 softmax (thread = row = TMEM lane), 4 TMA producer, 5 MMA issuer, 6-7 only complete
+// the second warpgroup (setmaxnreg acts per warpgroup).
+//
+// Synchronisation (all mbarriers, every wait bounded):
+//   q_full                     producer -> MMA
+//   k_full[s], v_full[s]       producer -> MMA, softmax (K, V tiles and the per-key vectors of stage s)
+//   kv_empty[s]                MMA commit -> producer (stage s free again)
+//   s_full                     MMA commit -> softmax (S of the next key tile ready)
+//   s_free                     softmax (128 arrivals) -> MMA (S read: the slot may take the next S)
+//   p_full                     softmax (128 arrivals) -> MMA (P in TMEM, O corrected)
+//   o_ready                    MMA commit -> softmax (the previous O += P V completed)
+//   o_done                     MMA commit -> softmax (final O complete)
+constexpr int kThreads1 = 256;
+constexpr int kWarpProducer1 = 4;
+constexpr int kWarpMma1 = 5;
+
+template <int D>
+struct Fwd1Cfg {
+  static constexpr int BOXC = D >= 64 ? 64 : D;
+  static constexpr int NBOX = D / BOXC;
+  static constexpr int SWB = BOXC * 2;
+  static constexpr int BOXB = kBT * SWB;
+  static constexpr int TILEB = NBOX * BOXB;
+  static constexpr uint32_t SW = SWB == 128 ? kSwizzle128 : (SWB == 64 ? kSwizzle64 : kSwizzle32);
+  static constexpr int NS = 2;                      // K/V ring stages
+  static constexpr int COLB = kBT * 4;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + TILEB;
+  static constexpr int OFF_V = OFF_K + NS * TILEB;
+  static constexpr int OFF_COL = OFF_V + NS * TILEB;  // per stage: a, psi, phi
+  static constexpr int OFF_BAR = OFF_COL + NS * 3 * COLB;
+  static constexpr int NBAR = 1 + 3 * NS + 6;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int COL_S = 0, COL_P = kBT, COL_O = kBT + kBT / 2;
+  static constexpr int TMEM_COLS = 256;
+  static constexpr uint32_t IDESC_S = idesc_f16(kBT, kBT, 0);
+  static constexpr uint32_t IDESC_O = idesc_f16(kBT, D, 1);
+  static_assert(D <= 64 && COL_O + D <= TMEM_COLS, "TMEM columns");
+  static_assert(2 * SMEM <= 228 * 1024, "two CTAs per SM");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads1, 2)
+tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+               const __grid_constant__ CUtensorMap tv, const TcFwdParams p) {
+  using C = Fwd1Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + C::NS;
+  uint64_t* kv_empty = v_full + C::NS;
+  uint64_t* s_full = kv_empty + C::NS;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* o_ready = p_full + 1;
+  uint64_t* o_done = o_ready + 1;
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1-d grid in longest-first order: every head's last query tile (the most key tiles) first.
+  const int nbh = p.B * p.H;
+  const int i = p.NB - 1 - int(blockIdx.x) / nbh;
+  const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
+  const int nsteps = i + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(o_ready, 1);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Register split: 128 per thread at launch (two CTAs per SM); the softmax warpgroup takes 200, the other 56.
+  if (warp >= 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  if (warp == kWarpProducer1) {
+    if (elect_one()) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+    }
+    __syncwarp();
+    uint8_t* sq = smem + C::OFF_Q;
+    if (elect_one()) {
+      mbar_expect_tx(q_full, C::TILEB);
+      for (int bx = 0; bx < C::NBOX; ++bx) tma_load_4d(sq + bx * C::BOXB, &tq, bx * C::BOXC, i * kBT, h, b, q_full);
+    }
+    __syncwarp();
+    bool ok = true;
+    const size_t colbase = size_t(z) * p.TP;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      const int st = k % C::NS, j = i - k;
+      if (k >= C::NS) ok = mbar_wait(kv_empty + st, ((k / C::NS) - 1) & 1, p.status, 31);
+      if (!ok) break;
+      uint8_t* sk = smem + C::OFF_K + st * C::TILEB;
+      uint8_t* sv = smem + C::OFF_V + st * C::TILEB;
+      uint8_t* sc = smem + C::OFF_COL + st * 3 * C::COLB;
+      if (elect_one()) {
+        mbar_expect_tx(k_full + st, C::TILEB + 3 * C::COLB);
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_4d(sk + bx * C::BOXB, &tk, bx * C::BOXC, j * kBT, h, b, k_full + st);
+        bulk_load(sc, p.cola + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        bulk_load(sc + C::COLB, p.colpsi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        bulk_load(sc + 2 * C::COLB, p.colphi + colbase + size_t(j) * kBT, C::COLB, k_full + st);
+        mbar_expect_tx(v_full + st, C::TILEB);
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_4d(sv + bx * C::BOXB, &tv, bx * C::BOXC, j * kBT, h, b, v_full + st);
+      }
+      __syncwarp();
+    }
+    // Drain: wait (bounded) until the copies this warp issued have landed before the CTA may exit.
+    mbar_wait(q_full, 0, p.status, 32);
+    for (int k = (nsteps > C::NS ? nsteps - C::NS : 0); k < nsteps; ++k) {
+      mbar_wait(k_full + k % C::NS, (k / C::NS) & 1, p.status, 33);
+      mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 34);
+    }
+  } else if (warp == kWarpMma1) {
+    // Whole warp, converged (warp-uniform operands); one elected lane issues each MMA.
+    const uint32_t qa = smem_u32(smem + C::OFF_Q);
+    auto issue_s = [&](int k) {  // S = Q K^T of key step k into the S slot
+      const uint32_t ka = smem_u32(smem + C::OFF_K + (k % C::NS) * C::TILEB);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
+        mma_ss_w(tmem + C::COL_S, smem_desc(qa + off, 16, 8 * C::SWB, C::SW),
+                 smem_desc(ka + off, 16, 8 * C::SWB, C::SW), C::IDESC_S, kk > 0);
+      }
+      mma_commit_w(s_full);
+    };
+    auto issue_pv = [&](int k) {  // O += P V of key step k
+      const uint32_t va = smem_u32(smem + C::OFF_V + (k % C::NS) * C::TILEB);
+#pragma unroll
+      for (int kk = 0; kk < kBT / 16; ++kk)
+        mma_ts_w(tmem + C::COL_O, tmem + C::COL_P + kk * 8,
+                 smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_O, (k > 0 || kk > 0) ? 1u : 0u);
+    };
+    bool ok = mbar_wait(q_full, 0, p.status, 40);
+    if (ok) ok = mbar_wait(k_full, 0, p.status, 41);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+    }
+    for (int k = 0; k < nsteps && ok; ++k) {
+      if (k + 1 < nsteps) {
+        // The next S as soon as the softmax has read this one out of the slot (K of step k + 1 was released by
+        // the P V of step k - 1, already issued).
+        ok = mbar_wait(s_free, k & 1, p.status, 42);
+        if (ok) ok = mbar_wait(k_full + (k + 1) % C::NS, ((k + 1) / C::NS) & 1, p.status, 43);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(k + 1);
+      }
+      ok = mbar_wait(p_full, k & 1, p.status, 44);
+      if (ok) ok = mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 45);
+      if (!ok) break;
+      tc_fence_after();
+      issue_pv(k);
+      mma_commit_w(o_ready);
+      mma_commit_w(kv_empty + k % C::NS);
+    }
+    mma_commit_w(o_done);
+    // Drain: every MMA issued by this warp has completed before TMEM can be released.
+    mma_commit_w(drain);
+    mbar_wait(drain, 0, p.status, 46);
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------------------------------- softmax ----
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
+    const int r = warp * 32 + lane;
+    const int t = i * kBT + r;
+    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const float betal = p.beta[h] * kLog2e;
+    const float pre_t = p.pre[size_t(z) * p.TP + t];
+    const float* bmin = p.bmin + size_t(z) * p.NB;
+    float mrow = -kInf, lrow = 0.f, mid = kInf;
+    bool ok = true;
+    auto run = [&](auto neg_tag) {
+      constexpr bool NEG = decltype(neg_tag)::value;
+      auto ext = [](float a, float b2) { return NEG ? fmaxf(a, b2) : fminf(a, b2); };
+      const float2 sc2 = make_float2(p.scale2, p.scale2);
+      for (int k = 0; k < nsteps && ok; ++k) {
+        const int j = i - k, st = k % C::NS;
+        ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 50);
+        if (ok) ok = mbar_wait(s_full, k & 1, p.status, 51);
+        if (!ok) break;
+        tc_fence_after();
+        float s[kBT];
+#pragma unroll
+        for (int c = 0; c < kBT / 32; ++c) tmem_ld32(tl + C::COL_S + c * 32, s + c * 32);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(s_free);  // the slot may take the next S now
+        const float* cA = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB);  // b'*min(SUF-psi,0)
+        const float* cE = cA + kBT;                                                               // -b'*psi
+        const float* cF = cA + 2 * kBT;                                                           // b'*phi
+        if (j == i) {
+          // Diagonal tile: keys from the row down; rr = extremum of b'*phi over (key, row] (+-inf when empty).
+          float rr = NEG ? -kInf : kInf;
+          const int lim = min(r, p.T - 1 - j * kBT);  // last valid key of this row
+#pragma unroll
+          for (int c = kBT - 1; c >= 0; --c) {
+            const float bias = ext(0.f, rr + cE[c]);
+            const float v = fmaf(s[c], p.scale2, bias);
+            s[c] = c <= lim ? v : -kInf;
+            if (c <= r) rr = ext(rr, cF[c]);
+          }
+        } else {
+          // Off the diagonal: bias = ext(a_s, b' * min(mid, PRE_t) - b' * psi_s), two keys per packed op.
+          const float R = betal * fminf(mid, pre_t);
+          const float2 R2 = make_float2(R, R);
+#pragma unroll
+          for (int c = 0; c < kBT; c += 2) {
+            const float2 e2 = *reinterpret_cast<const float2*>(cE + c);
+            const float2 a2 = *reinterpret_cast<const float2*>(cA + c);
+            const float2 tt = __fadd2_rn(R2, e2);
+            const float2 bias = make_float2(ext(a2.x, tt.x), ext(a2.y, tt.y));
+            const float2 v = __ffma2_rn(make_float2(s[c], s[c + 1]), sc2, bias);
+            s[c] = v.x;
+            s[c + 1] = v.y;
+          }
+          mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
+        }
+        float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int c = 4; c < kBT; c += 4) {
+          m4[0] = fmaxf(m4[0], s[c]);
+          m4[1] = fmaxf(m4[1], s[c + 1]);
+          m4[2] = fmaxf(m4[2], s[c + 2]);
+          m4[3] = fmaxf(m4[3], s[c + 3]);
+        }
+        const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        // Lazy rescaling of the running maximum.
+        const float mnew = fmaxf(mrow, mt);
+        bool need = false;
+        float alpha = 1.f;
+        if (k == 0) {
+          mrow = mnew;
+        } else if (mnew > mrow + kRescaleThreshold) {
+          need = true;
+          alpha = ex2(mrow - mnew);
+          mrow = mnew;
+        }
+        // The previous O += P V must be complete before O is touched and before P is rewritten.
+        if (k > 0) {
+          ok = mbar_wait(o_ready, (k - 1) & 1, p.status, 53);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          lrow *= alpha;
+#pragma unroll
+          for (int c = 0; c < D; c += 16) {
+            float o[16];
+            tmem_ld16(tl + C::COL_O + c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] *= alpha;
+            tmem_st16(tl + C::COL_O + c, reinterpret_cast<const uint32_t*>(o));
+          }
+        }
+        const float2 nm2 = make_float2(-mrow, -mrow);
+        float2 ls = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c0 = 0; c0 < kBT; c0 += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 xx = __fadd2_rn(make_float2(s[c0 + e], s[c0 + e + 1]), nm2);
+            const float2 pp = make_float2(ex2(xx.x), ex2(xx.y));
+            ls = __fadd2_rn(ls, pp);
+            pk[e / 2] = pack_half2(pp.x, pp.y);
+          }
+          tmem_st16(tl + C::COL_P + c0 / 2, pk);
+        }
+        lrow += ls.x + ls.y;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+    };
+    if (betal < 0.f)
+      run(std::true_type{});
+    else
+      run(std::false_type{});
+    if (ok) ok = mbar_wait(o_done, 0, p.status, 52);
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.f / lrow;
+      const bool store = t < p.T;
+      __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(store ? t : 0) * p.o_st;
+#pragma unroll
+      for (int c = 0; c < D; c += 16) {
+        float o[16];
+        tmem_ld16(tl + C::COL_O + c, o);
+        tmem_ld_wait();
+        if (store) {
+          uint4 w0, w1;
+          w0.x = pack_half2(o[0] * inv, o[1] * inv);
+          w0.y = pack_half2(o[2] * inv, o[3] * inv);
+          w0.z = pack_half2(o[4] * inv, o[5] * inv);
+          w0.w = pack_half2(o[6] * inv, o[7] * inv);
+          w1.x = pack_half2(o[8] * inv, o[9] * inv);
+          w1.y = pack_half2(o[10] * inv, o[11] * inv);
+          w1.z = pack_half2(o[12] * inv, o[13] * inv);
+          w1.w = pack_half2(o[14] * inv, o[15] * inv);
+          reinterpret_cast<uint4*>(orow + c)[0] = w0;
+          reinterpret_cast<uint4*>(orow + c)[1] = w1;
+        }
+      }
+      if (store) p.lse[size_t(z) * p.T + t] = mrow + lg2(lrow);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
+            std::string* err) {
+  using C = Fwd1Cfg<D>;
+  CUtensorMap mq, mk, mv;
+  if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
+      !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D)) {
+    *err = "cuTensorMapEncodeTiled failed for q, k or v";
+    return FPA_ERR_CUDA;
+  }
+  auto fn = tc_fwd1_kernel<D>;
+  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(fn), C::SMEM);
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  TcFwdParams p;
+  p.cola = cols.a;
+  p.colpsi = cols.psi;
+  p.colphi = cols.phi;
+  p.pre = st.pre;
+  p.bmin = st.bmin;
+  p.beta = a.beta;
+  p.o = static_cast<__half*>(a.o);
+  p.o_sb = a.o_stride[0];
+  p.o_sh = a.o_stride[1];
+  p.o_st = a.o_stride[2];
+  p.lse = a.lse;
+  p.status = status;
+  p.B = d.B;
+  p.H = d.H;
+  p.T = d.T;
+  p.NB = d.NB;
+  p.TP = d.TP;
+  p.NPAIR = 0;
+  p.scale2 = float(1.0 / sqrt(double(D))) * kLog2e;
+  fn<<<d.NB * d.BH(), kThreads1, C::SMEM, s>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  return FPA_OK;
+}
+
 template <int D>
 int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
            std::string* err) {
@@ -514,9 +903,9 @@ int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
   }
   int rc;
   switch (d.D) {
-    case 16: rc = launch<16>(a, d, st, cols, status, s, err); break;
-    case 32: rc = launch<32>(a, d, st, cols, status, s, err); break;
-    case 64: rc = launch<64>(a, d, st, cols, status, s, err); break;
+    case 16: rc = launch1<16>(a, d, st, cols, status, s, err); break;
+    case 32: rc = launch1<32>(a, d, st, cols, status, s, err); break;
+    case 64: rc = launch1<64>(a, d, st, cols, status, s, err); break;
     case 128: rc = launch<128>(a, d, st, cols, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
