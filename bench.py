@@ -53,6 +53,8 @@ def parse(argv=None):
     ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU reference sample")
     ap.add_argument("--no-config4", action="store_true", help="skip the configuration-4 measurement")
+    ap.add_argument("--no-triton-reference", action="store_true",
+                    help="skip timing the reference's own Triton kernels (installed under baseline/_ref)")
     ap.add_argument("--workload", choices=["operator", "lm"], default="operator",
                     help="operator: configuration 2 (the BASELINE metric); lm: configuration 5, the LM training step")
     ap.add_argument("--lm-layers", type=int, default=12, help="blocks of the LM (configuration 5: 12)")
@@ -423,6 +425,39 @@ def reference_arm(args, B, H, T, D, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def triton_reference(inputs, flush):
+    """The reference's own GPU path (its Triton kernels, impl="triton", from the unmodified reference module installed
+    under baseline/_ref) timed with the reference benchmark's protocol (3 warm-up, median of 15, its bench.py:11-23,
+    46-52) on the same inputs, when that module imports here; otherwise the reason it is unavailable."""
+    import importlib.util
+    path = os.path.join(ROOT, "baseline", "_ref", "kernel.py")
+    if not os.path.exists(path):
+        return {"unavailable": "the reference module is not installed under baseline/_ref"}
+    try:
+        spec = importlib.util.spec_from_file_location("fpa_reference_module", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        q, k, v, phi, psi, beta, do = inputs
+        args = (q, k, v, phi, psi, beta)
+
+        def fwd():
+            with torch.no_grad():
+                mod.first_passage_attention(*args, impl="triton")
+
+        def fwd_bwd():
+            x = [t.clone().requires_grad_() for t in args]
+            mod.first_passage_attention(*x, impl="triton").backward(do)
+        f_ms = reference_protocol(fwd, flush)
+        fb_ms = reference_protocol(fwd_bwd, flush)
+    except Exception as exc:  # a reference that cannot run here is reported, not fatal
+        return {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:200] if str(exc) else ''}"}
+    B, H, T, D = inputs[0].shape
+    return {"fwd_ms": f_ms, "fwd_bwd_ms": fb_ms, "fwd_tflops": flops(B, H, T, D, "fwd") / (f_ms * 1e-3) / 1e12,
+            "fwd_bwd_tflops": flops(B, H, T, D, "fwd_bwd") / (fb_ms * 1e-3) / 1e12,
+            "protocol": "reference bench.py: eager impl='triton', 3 warm-up, median of 15, L2 flushed before each",
+            "source": "unmodified reference kernel.py installed under baseline/_ref"}
+
+
 # ------------------------------------------------------------------------------------------------ native ----
 def e2e_chunks(Bs, Hs):
     """Pieces of a [Bs, Hs] shard the end-to-end step pipelines: each sequence when there are several, else up to
@@ -673,7 +708,13 @@ def main(argv=None):
         del g4f, g4, c4, c4l
         sync_all()
 
-    # 6. Per-kernel device times of the library's launches (CUDA events around each launch, on the call's stream),
+    # 6. The reference's own Triton kernels on this GPU, same inputs and protocol (one GPU only).
+    triton_ref = None
+    if world == 1 and not args.no_triton_reference:
+        triton_ref = triton_reference((q, k, v, phi, psi, beta, do), flush)
+        torch.cuda.synchronize()
+
+    # 7. Per-kernel device times of the library's launches (CUDA events around each launch, on the call's stream),
     # in a separate pass so the event records stay out of the timed regions above.
     from first_passage_attention_b200 import _lib
     lib = _lib.load()
@@ -756,6 +797,7 @@ def main(argv=None):
                                 "streams"},
             "weak_scaling": weak,
             "config4": cfg4,
+            "triton_reference": triton_ref,
             "gpu_launches": launches,
             "step_graph": graph is not None,
             "clocks": sampler.summary(),

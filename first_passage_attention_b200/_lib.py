@@ -17,7 +17,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE = range(6
 
 # Exported symbols, in the order include/fpa.h declares them.
 EXPORTS = ("fpa_abi_version", "fpa_struct_size", "fpa_fwd_workspace_bytes", "fpa_bwd_workspace_bytes", "fpa_fwd",
-           "fpa_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_profile",
+           "fpa_bwd", "fpa_field_fwd", "fpa_field_bwd", "fpa_workspace_status", "fpa_status_string", "fpa_last_error", "fpa_profile",
            "fpa_profile_report", "fpa_selftest_wait_timeout", "fpa_fwd_noalloc")
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
@@ -57,6 +57,14 @@ class FpaBwdArgs(ctypes.Structure):
                 ("kernels_launched", ctypes.c_int32), ("path_taken", ctypes.c_int32)]
 
 
+class FpaFieldArgs(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("T", ctypes.c_int32), ("H", ctypes.c_int32),
+                ("proj", ctypes.c_void_p), ("proj_stride", ctypes.c_int64 * 3),
+                ("phi", ctypes.c_void_p), ("psi", ctypes.c_void_p),
+                ("dphi", ctypes.c_void_p), ("dpsi", ctypes.c_void_p),
+                ("dproj", ctypes.c_void_p), ("dproj_stride", ctypes.c_int64 * 3)]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -84,6 +92,10 @@ def load():
         lib.fpa_fwd.argtypes = [ctypes.POINTER(FpaFwdArgs), ctypes.c_void_p]
         lib.fpa_bwd.restype = ctypes.c_int
         lib.fpa_bwd.argtypes = [ctypes.POINTER(FpaBwdArgs), ctypes.c_void_p]
+        for n in ("fpa_field_fwd", "fpa_field_bwd"):
+            f = getattr(lib, n)
+            f.restype = ctypes.c_int
+            f.argtypes = [ctypes.POINTER(FpaFieldArgs), ctypes.c_void_p]
         lib.fpa_workspace_status.restype = ctypes.c_int
         lib.fpa_workspace_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.fpa_status_string.restype = ctypes.c_char_p
@@ -99,7 +111,8 @@ def load():
         lib.fpa_fwd_noalloc.argtypes = [ctypes.POINTER(FpaFwdArgs), ctypes.c_void_p]
         if lib.fpa_abi_version() != ABI_VERSION:
             raise RuntimeError(f"libfpa_b200 ABI version {lib.fpa_abi_version()} != {ABI_VERSION}; rebuild it")
-        if lib.fpa_struct_size(0) != ctypes.sizeof(FpaFwdArgs) or lib.fpa_struct_size(1) != ctypes.sizeof(FpaBwdArgs):
+        if lib.fpa_struct_size(0) != ctypes.sizeof(FpaFwdArgs) or lib.fpa_struct_size(1) != ctypes.sizeof(FpaBwdArgs) \
+                or lib.fpa_struct_size(2) != ctypes.sizeof(FpaFieldArgs):
             raise RuntimeError("libfpa_b200 argument structs do not match the Python mirror; rebuild it")
         _lib = lib
         return lib

@@ -78,7 +78,9 @@ extern "C" {
 
 int fpa_abi_version(void) { return FPA_ABI_VERSION; }
 
-size_t fpa_struct_size(int which) { return which == 0 ? sizeof(FpaFwdArgs) : which == 1 ? sizeof(FpaBwdArgs) : 0; }
+size_t fpa_struct_size(int which) {
+  return which == 0 ? sizeof(FpaFwdArgs) : which == 1 ? sizeof(FpaBwdArgs) : which == 2 ? sizeof(FpaFieldArgs) : 0;
+}
 
 size_t fpa_fwd_workspace_bytes(int dtype, int B, int H, int T, int D, int path) {
   if (check_common(dtype, B, H, T, D, 1.f) != FPA_OK) return 0;

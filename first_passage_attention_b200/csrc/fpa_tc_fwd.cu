@@ -453,29 +453,38 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// One query tile per CTA, two CTAs per SM (D <= 64).
+// One query tile per CTA, two CTAs per SM, each row shared by two threads (D <= 64).
 //
 // The CTA takes query tile i of one head and walks its key tiles j = i, i - 1, ..., 0 (the diagonal first, as
 // above). It holds 256 TMEM columns: S [0, 128), P [128, 192) (fp16 pairs), O [192, 192 + D). Two CTAs share an
-// SM, so one CTA's prologue, pipeline fill and epilogue run while the other computes, and 768 single-tile CTAs
-// (configuration 2) balance over the SMs better than 384 two-tile ones. S has one slot: the softmax hands it back
-// (s_free) as soon as it has read S, and the MMA warp computes the next S meanwhile; P has columns of its own and is
-// rewritten only after the previous P V has completed (o_ready).
-// Warps (256 threads): 0-3 softmax (thread = row = TMEM lane), 4 TMA producer, 5 MMA issuer, 6-7 only complete
-// the second warpgroup (setmaxnreg acts per warpgroup).
+// SM, so one CTA's prologue, pipeline fill and epilogue run while the other computes, and single-tile CTAs balance
+// over the SMs better than two-tile ones (and fill more of them when a GPU holds few heads). S has one slot: the
+// softmax hands it back (s_free) as soon as it has read S, and the MMA warp computes the next S meanwhile; P has
+// columns of its own and is rewritten only after the previous P V has completed (o_ready).
+// Each S row is shared by two softmax threads, one per half of the key columns (threads of warps w and w + 4 see
+// the same TMEM lanes), which doubles the warps per SM sub-partition that take turns hiding each other's latency.
+// The halves agree on the row maximum through shared memory once per key tile (a 64-thread named barrier per
+// lane quadrant, whose 64 threads meet on an mbarrier of their own), keep their own partial row sums and rescale
+// their own half of O.
+// Warps (384 threads): 0-3 and 4-7 the two halves (thread = row = TMEM lane), 8 TMA producer, 9 MMA issuer, 10-11
+// only complete the third warpgroup (setmaxnreg acts per warpgroup).
 //
 // Synchronisation (all mbarriers, every wait bounded):
 //   q_full                     producer -> MMA
 //   k_full[s], v_full[s]       producer -> MMA, softmax (K, V tiles and the per-key vectors of stage s)
 //   kv_empty[s]                MMA commit -> producer (stage s free again)
 //   s_full                     MMA commit -> softmax (S of the next key tile ready)
-//   s_free                     softmax (128 arrivals) -> MMA (S read: the slot may take the next S)
-//   p_full                     softmax (128 arrivals) -> MMA (P in TMEM, O corrected)
+//   s_free                     softmax (256 arrivals) -> MMA (S read: the slot may take the next S)
+//   p_full                     softmax (256 arrivals) -> MMA (P in TMEM, O corrected)
 //   o_ready                    MMA commit -> softmax (the previous O += P V completed)
 //   o_done                     MMA commit -> softmax (final O complete)
-constexpr int kThreads1 = 256;
-constexpr int kWarpProducer1 = 4;
-constexpr int kWarpMma1 = 5;
+//   x_pair[q]                  the two softmax threads of each row of lane quadrant q (64 arrivals): row maxima
+//                              (once per key tile) and the partial row sums (once at the end) exchanged
+constexpr int kThreads1 = 384;
+constexpr int kSoftmaxThreads1 = 256;
+constexpr int kWarpProducer1 = 8;
+constexpr int kWarpMma1 = 9;
+constexpr int kHalf = kBT / 2;  // key columns per softmax thread
 
 template <int D>
 struct Fwd1Cfg {
@@ -491,8 +500,9 @@ struct Fwd1Cfg {
   static constexpr int OFF_K = OFF_Q + TILEB;
   static constexpr int OFF_V = OFF_K + NS * TILEB;
   static constexpr int OFF_COL = OFF_V + NS * TILEB;  // per stage: a, psi, phi
-  static constexpr int OFF_BAR = OFF_COL + NS * 3 * COLB;
-  static constexpr int NBAR = 1 + 3 * NS + 6;
+  static constexpr int OFF_X = OFF_COL + NS * 3 * COLB;  // row maxima of the halves [2 parities][2 halves][128]
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * kBT * 4;
+  static constexpr int NBAR = 1 + 3 * NS + 6 + 4;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static constexpr int COL_S = 0, COL_P = kBT, COL_O = kBT + kBT / 2;
   static constexpr int TMEM_COLS = 256;
@@ -520,7 +530,9 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   uint64_t* o_ready = p_full + 1;
   uint64_t* o_done = o_ready + 1;
   uint64_t* drain = o_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* x_pair = drain + 1;  // [4]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_pair + 4);
+  float* xmax = reinterpret_cast<float*>(smem + C::OFF_X);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // 1-d grid in longest-first order: every head's last query tile (the most key tiles) first.
@@ -537,11 +549,12 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       mbar_init(kv_empty + s, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
+    mbar_init(s_free, kSoftmaxThreads1);
+    mbar_init(p_full, kSoftmaxThreads1);
     mbar_init(o_ready, 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
+    for (int qq = 0; qq < 4; ++qq) mbar_init(x_pair + qq, 64);
     fence_mbar_init();
   }
   if (warp == kWarpMma1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -550,8 +563,8 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Register split: 128 per thread at launch (two CTAs per SM); the softmax warpgroup takes 200, the other 56.
-  if (warp >= 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  // Register split: 80 per thread at launch (two CTAs per SM); the softmax warpgroups take 104, the third 32.
+  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 32;" ::: "memory");
   if (warp == kWarpProducer1) {
     if (elect_one()) {
       prefetch_tmap(&tq);
@@ -641,17 +654,27 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     // Drain: every MMA issued by this warp has completed before TMEM can be released.
     mma_commit_w(drain);
     mbar_wait(drain, 0, p.status, 46);
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------------------------------------- softmax ----
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
-    const int r = warp * 32 + lane;
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;" ::: "memory");
+    const int q = warp & 3, half = warp >> 2;
+    const int r = q * 32 + lane;
     const int t = i * kBT + r;
-    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const int c0h = half * kHalf;  // first key column of this thread's half
+    const uint32_t tl = tmem + (uint32_t(q * 32) << 16);
     const float betal = p.beta[h] * kLog2e;
     const float pre_t = p.pre[size_t(z) * p.TP + t];
     const float* bmin = p.bmin + size_t(z) * p.NB;
-    float mrow = -kInf, lrow = 0.f, mid = kInf;
+    float mrow = -kInf, lrow = 0.f, mid = kInf;  // lrow: this half's part of the row sum
     bool ok = true;
+    // Exchange with the other half of the row through buffer `buf` ([2][128]) at exchange number `ph`: publish
+    // v, meet on x_pair[q] (bounded wait), return the partner's value.
+    auto exchange = [&](float* buf, float v, int ph) {
+      buf[half * kBT + r] = v;
+      mbar_arrive(x_pair + q);
+      ok = ok && mbar_wait(x_pair + q, ph & 1, p.status, 54);
+      return buf[(1 - half) * kBT + r];
+    };
     auto run = [&](auto neg_tag) {
       constexpr bool NEG = decltype(neg_tag)::value;
       auto ext = [](float a, float b2) { return NEG ? fmaxf(a, b2) : fminf(a, b2); };
@@ -662,32 +685,39 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         if (ok) ok = mbar_wait(s_full, k & 1, p.status, 51);
         if (!ok) break;
         tc_fence_after();
-        float s[kBT];
-#pragma unroll
-        for (int c = 0; c < kBT / 32; ++c) tmem_ld32(tl + C::COL_S + c * 32, s + c * 32);
+        float s[kHalf];
+        tmem_ld32(tl + C::COL_S + c0h, s);
+        tmem_ld32(tl + C::COL_S + c0h + 32, s + 32);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(s_free);  // the slot may take the next S now
-        const float* cA = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB);  // b'*min(SUF-psi,0)
-        const float* cE = cA + kBT;                                                               // -b'*psi
-        const float* cF = cA + 2 * kBT;                                                           // b'*phi
+        const float* cA = reinterpret_cast<const float*>(smem + C::OFF_COL + st * 3 * C::COLB) + c0h;
+        const float* cE = cA + kBT;       // -b'*psi
+        const float* cF = cA + 2 * kBT;   // b'*phi
         if (j == i) {
-          // Diagonal tile: keys from the row down; rr = extremum of b'*phi over (key, row] (+-inf when empty).
+          // Diagonal tile: keys from the row down; rr = extremum of b'*phi over (key, row] (+-inf when empty). The
+          // lower half starts from the extremum over the upper half's keys up to the row.
           float rr = NEG ? -kInf : kInf;
-          const int lim = min(r, p.T - 1 - j * kBT);  // last valid key of this row
+          if (half == 0) {
+#pragma unroll 8
+            for (int c = 0; c < kHalf; ++c)
+              if (kHalf + c <= r) rr = ext(rr, cF[kHalf + c]);
+          }
+          const int lim = min(r, p.T - 1 - j * kBT) - c0h;  // last valid key of this row, in this half
+          const int rh = r - c0h;
 #pragma unroll
-          for (int c = kBT - 1; c >= 0; --c) {
+          for (int c = kHalf - 1; c >= 0; --c) {
             const float bias = ext(0.f, rr + cE[c]);
             const float v = fmaf(s[c], p.scale2, bias);
             s[c] = c <= lim ? v : -kInf;
-            if (c <= r) rr = ext(rr, cF[c]);
+            if (c <= rh) rr = ext(rr, cF[c]);
           }
         } else {
           // Off the diagonal: bias = ext(a_s, b' * min(mid, PRE_t) - b' * psi_s), two keys per packed op.
           const float R = betal * fminf(mid, pre_t);
           const float2 R2 = make_float2(R, R);
 #pragma unroll
-          for (int c = 0; c < kBT; c += 2) {
+          for (int c = 0; c < kHalf; c += 2) {
             const float2 e2 = *reinterpret_cast<const float2*>(cE + c);
             const float2 a2 = *reinterpret_cast<const float2*>(cA + c);
             const float2 tt = __fadd2_rn(R2, e2);
@@ -700,14 +730,18 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         }
         float m4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-        for (int c = 4; c < kBT; c += 4) {
+        for (int c = 4; c < kHalf; c += 4) {
           m4[0] = fmaxf(m4[0], s[c]);
           m4[1] = fmaxf(m4[1], s[c + 1]);
           m4[2] = fmaxf(m4[2], s[c + 2]);
           m4[3] = fmaxf(m4[3], s[c + 3]);
         }
-        const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        // Lazy rescaling of the running maximum.
+        // The row maximum: each half publishes its own, then both read the other's (double-buffered by key step,
+        // so a half that runs one step ahead never overwrites a value its partner has yet to read).
+        const float mh = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        const float mt = fmaxf(mh, exchange(xmax + (k & 1) * 2 * kBT, mh, k));
+        if (!ok) break;
+        // Lazy rescaling of the running maximum (both halves of a row take the same decision).
         const float mnew = fmaxf(mrow, mt);
         bool need = false;
         float alpha = 1.f;
@@ -724,31 +758,31 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
           if (!ok) break;
           tc_fence_after();
         }
-        if (__any_sync(0xffffffffu, need)) {
+        if (__any_sync(0xffffffffu, need)) {  // this half's columns of O
           lrow *= alpha;
 #pragma unroll
-          for (int c = 0; c < D; c += 16) {
-            float o[16];
-            tmem_ld16(tl + C::COL_O + c, o);
+          for (int c = 0; c < D / 2; c += 8) {
+            float o[8];
+            tmem_ld8(tl + C::COL_O + half * (D / 2) + c, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] *= alpha;
-            tmem_st16(tl + C::COL_O + c, reinterpret_cast<const uint32_t*>(o));
+            for (int e = 0; e < 8; ++e) o[e] *= alpha;
+            tmem_st8(tl + C::COL_O + half * (D / 2) + c, reinterpret_cast<const uint32_t*>(o));
           }
         }
         const float2 nm2 = make_float2(-mrow, -mrow);
         float2 ls = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c0 = 0; c0 < kBT; c0 += 32) {
+        for (int cc = 0; cc < kHalf; cc += 32) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float2 xx = __fadd2_rn(make_float2(s[c0 + e], s[c0 + e + 1]), nm2);
+            const float2 xx = __fadd2_rn(make_float2(s[cc + e], s[cc + e + 1]), nm2);
             const float2 pp = make_float2(ex2(xx.x), ex2(xx.y));
             ls = __fadd2_rn(ls, pp);
             pk[e / 2] = pack_half2(pp.x, pp.y);
           }
-          tmem_st16(tl + C::COL_P + c0 / 2, pk);
+          tmem_st16(tl + C::COL_P + (c0h + cc) / 2, pk);
         }
         lrow += ls.x + ls.y;
         tmem_st_wait();
@@ -760,32 +794,30 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       run(std::true_type{});
     else
       run(std::false_type{});
+    // The row sum is the two halves' parts; the halves share it through the row-maximum buffer.
+    float l = lrow;
+    if (ok) l += exchange(xmax + (nsteps & 1) * 2 * kBT, lrow, nsteps);
     if (ok) ok = mbar_wait(o_done, 0, p.status, 52);
     if (ok) {
       tc_fence_after();
-      const float inv = 1.f / lrow;
+      const float inv = 1.f / l;
       const bool store = t < p.T;
-      __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(store ? t : 0) * p.o_st;
+      __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(store ? t : 0) * p.o_st + half * (D / 2);
 #pragma unroll
-      for (int c = 0; c < D; c += 16) {
-        float o[16];
-        tmem_ld16(tl + C::COL_O + c, o);
+      for (int c = 0; c < D / 2; c += 8) {
+        float o[8];
+        tmem_ld8(tl + C::COL_O + half * (D / 2) + c, o);
         tmem_ld_wait();
         if (store) {
-          uint4 w0, w1;
+          uint4 w0;
           w0.x = pack_half2(o[0] * inv, o[1] * inv);
           w0.y = pack_half2(o[2] * inv, o[3] * inv);
           w0.z = pack_half2(o[4] * inv, o[5] * inv);
           w0.w = pack_half2(o[6] * inv, o[7] * inv);
-          w1.x = pack_half2(o[8] * inv, o[9] * inv);
-          w1.y = pack_half2(o[10] * inv, o[11] * inv);
-          w1.z = pack_half2(o[12] * inv, o[13] * inv);
-          w1.w = pack_half2(o[14] * inv, o[15] * inv);
           reinterpret_cast<uint4*>(orow + c)[0] = w0;
-          reinterpret_cast<uint4*>(orow + c)[1] = w1;
         }
       }
-      if (store) p.lse[size_t(z) * p.T + t] = mrow + lg2(lrow);
+      if (store && half == 0) p.lse[size_t(z) * p.T + t] = mrow + lg2(l);
     }
   }
   tc_fence_before();
@@ -902,10 +934,13 @@ int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
     return FPA_ERR_UNSUPPORTED;
   }
   int rc;
+  const bool small = int64_t((d.NB + 1) / 2) * d.BH() < sm_count();
   switch (d.D) {
-    case 16: rc = launch1<16>(a, d, st, cols, status, s, err); break;
-    case 32: rc = launch1<32>(a, d, st, cols, status, s, err); break;
-    case 64: rc = launch1<64>(a, d, st, cols, status, s, err); break;
+    // D <= 64: two query tiles per CTA share every K and V tile they load (half the L2 traffic), which wins while
+    // their grid fills the SMs; below that, single-tile CTAs (twice as many, two per SM) finish sooner.
+    case 16: rc = small ? launch1<16>(a, d, st, cols, status, s, err) : launch<16>(a, d, st, cols, status, s, err); break;
+    case 32: rc = small ? launch1<32>(a, d, st, cols, status, s, err) : launch<32>(a, d, st, cols, status, s, err); break;
+    case 64: rc = small ? launch1<64>(a, d, st, cols, status, s, err) : launch<64>(a, d, st, cols, status, s, err); break;
     case 128: rc = launch<128>(a, d, st, cols, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }

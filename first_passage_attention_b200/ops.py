@@ -198,11 +198,48 @@ def first_passage_attention(q, k, v, phi, psi, beta, tau=1.0, impl=None, block=6
     return _FirstPassageAttention.apply(q, k, v, phi, psi, beta, float(tau), None)
 
 
+class _FieldFn(torch.autograd.Function):
+    """phi, psi [B, H, T] from the Field projection's output proj [B, T, 3H] (fp32, on a CUDA device) in one
+    kernel each way (fpa_field_fwd / fpa_field_bwd): the cumsum of delta and the two additions of kernel.py:507-509
+    and their backward, with no intermediate tensors."""
+
+    @staticmethod
+    def forward(ctx, proj, H):
+        lib = _lib.load()
+        B, T, _ = proj.shape
+        phi = torch.empty((B, H, T), dtype=torch.float32, device=proj.device)
+        psi = torch.empty_like(phi)
+        a = _lib.FpaFieldArgs(B=B, T=T, H=H, proj=_ptr(proj), proj_stride=(ctypes.c_int64 * 3)(*proj.stride()),
+                              phi=_ptr(phi), psi=_ptr(psi))
+        _lib.check(lib.fpa_field_fwd(ctypes.byref(a), _stream(proj.device)))
+        LaunchStats.kernels += 1
+        ctx.shape, ctx.H = proj.shape, H
+        return phi, psi
+
+    @staticmethod
+    def backward(ctx, dphi, dpsi):
+        lib = _lib.load()
+        B, T, H3 = ctx.shape
+        dev = (dphi if dphi is not None else dpsi).device
+        dphi = torch.zeros((B, ctx.H, T), device=dev) if dphi is None else dphi.float().contiguous()
+        dpsi = torch.zeros((B, ctx.H, T), device=dev) if dpsi is None else dpsi.float().contiguous()
+        dproj = torch.empty((B, T, H3), dtype=torch.float32, device=dev)
+        a = _lib.FpaFieldArgs(B=B, T=T, H=ctx.H, dphi=_ptr(dphi), dpsi=_ptr(dpsi), dproj=_ptr(dproj),
+                              dproj_stride=(ctypes.c_int64 * 3)(*dproj.stride()))
+        _lib.check(lib.fpa_field_bwd(ctypes.byref(a), _stream(dev)))
+        LaunchStats.kernels += 1
+        return dproj, None
+
+
 class Field(nn.Module):
     """The per-head field of the layer (kernel.py:492-509). One fp32 projection of x (B, T, d_model) gives three
     values per head and position: an increment delta, and offsets g and h. The walk W is the running sum of delta
     along T; the field is phi = W + g and the levels are psi = W + h, both (B, H, T). The strength is
-    beta = softplus(beta_raw) (H,), positive for any parameter value."""
+    beta = softplus(beta_raw) (H,), positive for any parameter value.
+
+    On a CUDA device in fp32 the walk and the two sums run as one kernel each way (fpa_field_fwd / fpa_field_bwd)
+    that writes phi and psi in the operator's layout; ``impl = "reference"`` (set by a layer built with it), CPU
+    inputs and float64 keep the PyTorch ops."""
 
     def __init__(self, d_model, n_heads, beta_init=1.0):
         super().__init__()
@@ -210,12 +247,16 @@ class Field(nn.Module):
         self.proj = nn.Linear(d_model, 3 * n_heads)
         # softplus(beta_raw) = beta_init at initialisation: beta_raw = log(expm1(beta_init)), written stably.
         self.beta_raw = nn.Parameter(torch.full((n_heads,), beta_init + math.log(-math.expm1(-beta_init))))
+        self.impl = None
 
     def forward(self, x):
         B, T, _ = x.shape
         dt = torch.float64 if x.dtype == torch.float64 else torch.float32
         with torch.autocast(device_type=x.device.type, enabled=False):
             out = F.linear(x.to(dt), self.proj.weight.to(dt), self.proj.bias.to(dt))
+        if x.is_cuda and dt == torch.float32 and self.impl != "reference":
+            phi, psi = _FieldFn.apply(out, self.n_heads)
+            return phi, psi, F.softplus(self.beta_raw)
         delta, g, h = out.view(B, T, 3, self.n_heads).permute(2, 0, 3, 1)
         w = torch.cumsum(delta, dim=-1)
         return w + g, w + h, F.softplus(self.beta_raw)
@@ -237,6 +278,7 @@ class FirstPassageAttention(nn.Module):
         self.qkv = nn.Linear(d_model, 3 * d_model, bias=False)
         self.out = nn.Linear(d_model, d_model, bias=False)
         self.field = Field(d_model, n_heads, beta_init)
+        self.field.impl = impl
 
     def forward(self, x):
         B, T, _ = x.shape

@@ -101,10 +101,26 @@ typedef struct FpaBwdArgs {
   int32_t path_taken;       /* out */
 } FpaBwdArgs;
 
+/* The layer's field (kernel.py:502-509). proj is the fp32 output of the Field's projection, [B, T, 3H] with element
+ * strides proj_stride = {b, t, column}: per head h, delta = column h, g = column H + h, hh = column 2H + h. Forward:
+ * w_t = sum_{u<=t} delta_u, phi = w + g, psi = w + hh, written to phi, psi [B, H, T] contiguous float32. Backward:
+ * from dphi, dpsi [B, H, T] contiguous float32 it writes dproj (same layout as proj, strides dproj_stride):
+ * d delta_t = sum_{u>=t} (dphi_u + dpsi_u), dg = dphi, dhh = dpsi. Deterministic (fixed summation order). */
+typedef struct FpaFieldArgs {
+  int32_t B, T, H;
+  const float* proj; int64_t proj_stride[3];
+  float* phi;               /* out (forward) */
+  float* psi;               /* out (forward) */
+  const float* dphi;        /* in (backward) */
+  const float* dpsi;        /* in (backward) */
+  float* dproj; int64_t dproj_stride[3]; /* out (backward) */
+} FpaFieldArgs;
+
 /* ABI version of the loaded library (FPA_ABI_VERSION). */
 FPA_API int fpa_abi_version(void);
 
-/* sizeof(FpaFwdArgs) for which == 0, sizeof(FpaBwdArgs) for which == 1; lets bindings check their struct mirror. */
+/* sizeof(FpaFwdArgs) for which == 0, sizeof(FpaBwdArgs) for 1, sizeof(FpaFieldArgs) for 2; lets bindings check their
+ * struct mirrors. */
 FPA_API size_t fpa_struct_size(int which);
 
 /* Workspace sizes in bytes for a call with these sizes (0 for invalid sizes). */
@@ -116,6 +132,11 @@ FPA_API int fpa_fwd(FpaFwdArgs* args, void* stream);
 
 /* Backward pass (replaces kernel.py:424-451). Returns an FpaStatus. */
 FPA_API int fpa_bwd(FpaBwdArgs* args, void* stream);
+
+/* Field forward and backward (replace the PyTorch ops of kernel.py:504-509: the fp32 projection's split into
+ * delta, g, h, the cumsum and the two additions, and their autograd backward). Return an FpaStatus. */
+FPA_API int fpa_field_fwd(const FpaFieldArgs* args, void* stream);
+FPA_API int fpa_field_bwd(const FpaFieldArgs* args, void* stream);
 
 /* Synchronises `stream`, then reads and clears the device status word at the head of a workspace that a previous
  * fpa_fwd / fpa_bwd call used: FPA_OK, or FPA_ERR_TIMEOUT if a bounded device-side wait expired in that call. */

@@ -411,3 +411,32 @@ def test_native_library_is_what_ran():
     assert LaunchStats.fwd_calls == 1 and LaunchStats.bwd_calls == 1 and LaunchStats.kernels >= 4
     maps = open("/proc/self/maps").read()
     assert _lib.LIB_PATH in maps
+
+
+@pytest.mark.parametrize("T", [1, 700, 1024, 3000])
+def test_field_kernel_matches_the_pytorch_field(T):
+    """The Field's walk and sums in one kernel each way (fpa_field_fwd / fpa_field_bwd) against the PyTorch ops of
+    kernel.py:504-509 on the same parameters: phi, psi and the gradients of x and of the projection's weight and bias,
+    with T below, at and above one 1024-position chunk."""
+    need_gpu()
+    from first_passage_attention_b200 import Field
+    torch.manual_seed(3)
+    fk = Field(48, 12).cuda()
+    fr = Field(48, 12).cuda()
+    fr.load_state_dict(fk.state_dict())
+    fr.impl = "reference"
+    x = torch.randn(2, T, 48, device="cuda")
+    outs = []
+    for f in (fk, fr):
+        xx = x.clone().requires_grad_()
+        phi, psi, beta = f(xx)
+        g = torch.Generator(device="cuda").manual_seed(9)
+        w_phi = torch.randn(phi.shape, device="cuda", generator=g)
+        w_psi = torch.randn(psi.shape, device="cuda", generator=g)
+        loss = (phi * w_phi).sum() + (psi * w_psi).sum() + beta.sum()
+        grads = torch.autograd.grad(loss, [xx, f.proj.weight, f.proj.bias])
+        outs.append([phi.detach(), psi.detach()] + list(grads))
+    assert outs[0][0].is_contiguous() and outs[0][0].shape == (2, 12, T)
+    for a, b in zip(*outs):
+        scale = b.abs().max().clamp_min(1e-6)
+        assert ((a - b).abs().max() / scale).item() <= 1e-5
