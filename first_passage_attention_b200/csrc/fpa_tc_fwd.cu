@@ -68,6 +68,8 @@ struct TcFwdCfg {
   static constexpr uint32_t IDESC_O = idesc_f16(kBT, D, 1);
   static constexpr int COL_O = NSLOT * kBT;
   static_assert(COL_O + 2 * D <= 512, "TMEM columns");
+  static constexpr int REG_LO = D >= 64 ? 40 : 24, REG_HI = D >= 64 ? 232 : 240;
+  static_assert(128 * REG_LO + 256 * REG_HI == kThreads * 168, "register split");
 };
 
 struct TcFwdParams {
@@ -178,9 +180,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA group keeps 56 and each
-  // softmax group takes 224 (128*56 + 256*224 = 384*168).
-  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA group keeps C::REG_LO and
+  // each softmax group takes C::REG_HI (128*40 + 256*232 = 128*24 + 256*240 = 384*168). With 224 the softmax
+  // rows spilled to local memory.
+  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REG_LO) : "memory");
   if (warp == kWarpProducer) {
     // The whole warp runs the loop (converged, uniform operands); one elected lane issues each copy.
     if (elect_one()) {
@@ -289,7 +292,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     }
   } else if (warp < 8) {
     // ----------------------------------------------------------------------------------- softmax groups ----
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REG_HI) : "memory");
     const int x = warp >> 2, wr = warp & 3;
     const int r = wr * 32 + lane;
     const int i = x == 0 ? i0 : i1;
@@ -300,7 +303,9 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     const float betal = p.beta[h] * kLog2e;
     const float pre_t = p.pre[size_t(z) * p.TP + t];
     const float* bmin = p.bmin + size_t(z) * p.NB;
-    float mrow = -kInf, lrow = 0.f, mid = kInf;
+    // The row sum is kept as two parts, keys [0, 64) and [64, 128) of every tile, added at the end: the same
+    // order of additions as the one-tile kernel below, so both kernels give bit-identical results.
+    float mrow = -kInf, lrow = 0.f, lrow2 = 0.f, mid = kInf;
     int cnt = 0;
     bool ok = active_wg;
     const int kfirst = x == 0 ? k0 : 0;
@@ -380,6 +385,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
         if (__any_sync(0xffffffffu, need)) {
           lrow *= alpha;
+          lrow2 *= alpha;
 #pragma unroll
           for (int c = 0; c < D; c += 16) {
             float o[16];
@@ -391,7 +397,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           }
         }
         const float2 nm2 = make_float2(-mrow, -mrow);
-        float2 ls = make_float2(0.f, 0.f);
+        float2 ls = make_float2(0.f, 0.f), ls2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c0 = 0; c0 < kBT; c0 += 32) {
           uint32_t pk[16];
@@ -400,12 +406,16 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             const float2 xx = __fadd2_rn(make_float2(s[c0 + e], s[c0 + e + 1]), nm2);
             const bool emu = kEmuEvery > 0 && ((c0 + e) / 2) % (kEmuEvery > 0 ? kEmuEvery : 1) == 0;
             const float2 pp = emu ? ex2_poly2(xx) : make_float2(ex2(xx.x), ex2(xx.y));
-            ls = __fadd2_rn(ls, pp);
+            if (c0 < kBT / 2)
+              ls = __fadd2_rn(ls, pp);
+            else
+              ls2 = __fadd2_rn(ls2, pp);
             pk[e / 2] = pack_half2(pp.x, pp.y);
           }
           tmem_st16(tl + col_s + c0 / 2, pk);
         }
         lrow += ls.x + ls.y;
+        lrow2 += ls2.x + ls2.y;
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_full + slot);
@@ -419,6 +429,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     if (ok && active_wg) ok = mbar_wait(o_done + x, 0, p.status, 22);
     if (ok && active_wg) {
       tc_fence_after();
+      lrow += lrow2;
       const float inv = 1.f / lrow;
       const bool store = t < p.T;
       __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(store ? t : 0) * p.o_st;
