@@ -105,6 +105,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return mbar_wait_limit(bar, parity, status, site, kWaitLimitNs);
 }
 
+// Three-input maximum (one instruction on sm_100a; PTX ISA 8.8).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ------------------------------------------------------------------------------------------------- TMA ------
 // 4-d tiled tensor copy global -> shared, completion counted in bytes on `bar`. No multicast.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -306,6 +313,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   d |= uint64_t(swizzle & 7u) << 61;
   return d;
 }
+
+// The same descriptor as two 32-bit words, for MMA loops that step through an operand: the low word holds the
+// start address (>> 4, bits 0-13) and the leading byte offset (>> 4, bits 16-29); the high word the stride byte
+// offset (>> 4, bits 0-13), the version (bit 14) and the swizzle mode (bits 29-31). Shared-memory addresses stay
+// below 2^18, so a byte offset added to the low word as (off >> 4) never carries out of the address field.
+__host__ __device__ constexpr uint32_t desc_hi(uint32_t sbo_bytes, uint32_t swizzle) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | ((swizzle & 7u) << 29);
+}
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__device__ __forceinline__ uint64_t desc_make(uint32_t lo, uint32_t hi) { return (uint64_t(hi) << 32) | lo; }
 
 // kind::f16 instruction descriptor: fp16 A and B, fp32 D; b_mn_major = 1 when B is stored N-contiguous.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {

@@ -230,29 +230,37 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 4);
     }
   } else if (warp == kWarpMma) {
-    {  // whole warp, converged: operands stay warp-uniform; one elected lane issues each MMA
-      const uint32_t q0 = smem_u32(smem + C::OFF_Q), q1 = q0 + C::TILEB;
+    {  // The whole warp runs the loop (its waits included); one elected lane issues the MMAs and commits. The
+       // descriptors are built once: each MMA then costs an add to the low word of its operands' descriptors.
+      const bool leader = elect_one();
+      constexpr uint32_t HI = desc_hi(8 * C::SWB, C::SW);
+      const uint32_t lq = desc_lo(smem_u32(smem + C::OFF_Q), 16);
+      const uint32_t lk = desc_lo(smem_u32(smem + C::OFF_K), 16);
+      const uint32_t lv = desc_lo(smem_u32(smem + C::OFF_V), C::BOXB);
       auto issue_s = [&](int n) {  // S of job n into its slot
         const int x = job_x(n), st = job_k(n) % C::NS;
-        const uint32_t qa = x == 0 ? q0 : q1;
-        const uint32_t ka = smem_u32(smem + C::OFF_K + st * C::TILEB);
+        const uint32_t la = lq + uint32_t(x * (C::TILEB >> 4)), lb = lk + uint32_t(st * (C::TILEB >> 4));
         const uint32_t dcol = tmem + (n % C::NSLOT) * kBT;
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
-          mma_ss_w(dcol, smem_desc(qa + off, 16, 8 * C::SWB, C::SW), smem_desc(ka + off, 16, 8 * C::SWB, C::SW),
-                   C::IDESC_S, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            constexpr int PER = C::SWB / 32;  // K-steps per swizzle row
+            const uint32_t off = uint32_t(((kk / PER) * C::BOXB + (kk % PER) * 32) >> 4);
+            mma_ss(dcol, desc_make(la + off, HI), desc_make(lb + off, HI), C::IDESC_S, kk > 0);
+          }
+          mma_commit(s_full + n % C::NSLOT);
         }
-        mma_commit_w(s_full + n % C::NSLOT);
+        __syncwarp();
       };
       auto issue_pv = [&](int n, bool acc) {  // O_x += P V of job n
         const int x = job_x(n), st = job_k(n) % C::NS;
-        const uint32_t va = smem_u32(smem + C::OFF_V + st * C::TILEB);
-        const uint32_t acol = tmem + (n % C::NSLOT) * kBT;
+        const uint32_t lb = lv + uint32_t(st * (C::TILEB >> 4));
+        const uint32_t acol = tmem + (n % C::NSLOT) * kBT, dcol = tmem + C::COL_O + x * D;
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < kBT / 16; ++kk) {
-          mma_ts_w(tmem + C::COL_O + x * D, acol + kk * 8, smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW),
-                   C::IDESC_O, (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBT / 16; ++kk)
+            mma_ts(dcol, acol + kk * 8, desc_make(lb + uint32_t((kk * 16 * C::SWB) >> 4), HI), C::IDESC_O,
+                   (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, p.status, 10);
@@ -279,8 +287,11 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         if (!ok) break;
         tc_fence_after();
         issue_pv(n, x == 0 ? k > k0 : k > 0);
-        mma_commit_w(o_ready + x);
-        if (x == 1 || !has1) mma_commit_w(kv_empty + st);  // last job of key step k
+        if (leader) {
+          mma_commit(o_ready + x);
+          if (x == 1 || !has1) mma_commit(kv_empty + st);  // last job of key step k
+        }
+        __syncwarp();
         const int m = n + C::NSLOT;
         if (m < njobs && need_k(job_k(m))) issue_s(m);
       }
@@ -357,15 +368,15 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           }
           mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
         }
-        float m4[4] = {s[0], s[1], s[2], s[3]};
+        float m4[4] = {fmaxf(s[0], s[4]), fmaxf(s[1], s[5]), fmaxf(s[2], s[6]), fmaxf(s[3], s[7])};
 #pragma unroll
-        for (int c = 4; c < kBT; c += 4) {
-          m4[0] = fmaxf(m4[0], s[c]);
-          m4[1] = fmaxf(m4[1], s[c + 1]);
-          m4[2] = fmaxf(m4[2], s[c + 2]);
-          m4[3] = fmaxf(m4[3], s[c + 3]);
+        for (int c = 8; c < kBT; c += 8) {
+          m4[0] = fmax3f(m4[0], s[c], s[c + 4]);
+          m4[1] = fmax3f(m4[1], s[c + 1], s[c + 5]);
+          m4[2] = fmax3f(m4[2], s[c + 2], s[c + 6]);
+          m4[3] = fmax3f(m4[3], s[c + 3], s[c + 7]);
         }
-        const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        const float mt = fmaxf(fmax3f(m4[0], m4[1], m4[2]), m4[3]);
         // Lazy rescaling of the running maximum.
         const float mnew = fmaxf(mrow, mt);
         bool need = false;
@@ -618,24 +629,36 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       mbar_wait(v_full + k % C::NS, (k / C::NS) & 1, p.status, 34);
     }
   } else if (warp == kWarpMma1) {
-    // Whole warp, converged (warp-uniform operands); one elected lane issues each MMA.
-    const uint32_t qa = smem_u32(smem + C::OFF_Q);
+    // The whole warp runs the loop; one elected lane issues the MMAs and commits, from descriptors built once.
+    const bool leader = elect_one();
+    constexpr uint32_t HI = desc_hi(8 * C::SWB, C::SW);
+    const uint32_t lq = desc_lo(smem_u32(smem + C::OFF_Q), 16);
+    const uint32_t lk = desc_lo(smem_u32(smem + C::OFF_K), 16);
+    const uint32_t lv = desc_lo(smem_u32(smem + C::OFF_V), C::BOXB);
     auto issue_s = [&](int k) {  // S = Q K^T of key step k into the S slot
-      const uint32_t ka = smem_u32(smem + C::OFF_K + (k % C::NS) * C::TILEB);
+      const uint32_t lb = lk + uint32_t((k % C::NS) * (C::TILEB >> 4));
+      if (leader) {
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk / (C::SWB / 32)) * C::BOXB + (kk % (C::SWB / 32)) * 32;
-        mma_ss_w(tmem + C::COL_S, smem_desc(qa + off, 16, 8 * C::SWB, C::SW),
-                 smem_desc(ka + off, 16, 8 * C::SWB, C::SW), C::IDESC_S, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          constexpr int PER = C::SWB / 32;
+          const uint32_t off = uint32_t(((kk / PER) * C::BOXB + (kk % PER) * 32) >> 4);
+          mma_ss(tmem + C::COL_S, desc_make(lq + off, HI), desc_make(lb + off, HI), C::IDESC_S, kk > 0);
+        }
+        mma_commit(s_full);
       }
-      mma_commit_w(s_full);
+      __syncwarp();
     };
-    auto issue_pv = [&](int k) {  // O += P V of key step k
-      const uint32_t va = smem_u32(smem + C::OFF_V + (k % C::NS) * C::TILEB);
+    auto issue_pv = [&](int k) {  // O += P V of key step k, then the commits that release O and the K/V stage
+      const uint32_t lb = lv + uint32_t((k % C::NS) * (C::TILEB >> 4));
+      if (leader) {
 #pragma unroll
-      for (int kk = 0; kk < kBT / 16; ++kk)
-        mma_ts_w(tmem + C::COL_O, tmem + C::COL_P + kk * 8,
-                 smem_desc(va + kk * 16 * C::SWB, C::BOXB, 8 * C::SWB, C::SW), C::IDESC_O, (k > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBT / 16; ++kk)
+          mma_ts(tmem + C::COL_O, tmem + C::COL_P + kk * 8, desc_make(lb + uint32_t((kk * 16 * C::SWB) >> 4), HI),
+                 C::IDESC_O, (k > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(o_ready);
+        mma_commit(kv_empty + k % C::NS);
+      }
+      __syncwarp();
     };
     bool ok = mbar_wait(q_full, 0, p.status, 40);
     if (ok) ok = mbar_wait(k_full, 0, p.status, 41);
@@ -658,8 +681,6 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       if (!ok) break;
       tc_fence_after();
       issue_pv(k);
-      mma_commit_w(o_ready);
-      mma_commit_w(kv_empty + k % C::NS);
     }
     mma_commit_w(o_done);
     // Drain: every MMA issued by this warp has completed before TMEM can be released.
@@ -739,17 +760,17 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
           }
           mid = fminf(mid, bmin[j]);  // tile j lies strictly between the next key tile and tile i
         }
-        float m4[4] = {s[0], s[1], s[2], s[3]};
+        float m4[4] = {fmaxf(s[0], s[4]), fmaxf(s[1], s[5]), fmaxf(s[2], s[6]), fmaxf(s[3], s[7])};
 #pragma unroll
-        for (int c = 4; c < kHalf; c += 4) {
-          m4[0] = fmaxf(m4[0], s[c]);
-          m4[1] = fmaxf(m4[1], s[c + 1]);
-          m4[2] = fmaxf(m4[2], s[c + 2]);
-          m4[3] = fmaxf(m4[3], s[c + 3]);
+        for (int c = 8; c < kHalf; c += 8) {
+          m4[0] = fmax3f(m4[0], s[c], s[c + 4]);
+          m4[1] = fmax3f(m4[1], s[c + 1], s[c + 5]);
+          m4[2] = fmax3f(m4[2], s[c + 2], s[c + 6]);
+          m4[3] = fmax3f(m4[3], s[c + 3], s[c + 7]);
         }
         // The row maximum: each half publishes its own, then both read the other's (double-buffered by key step,
         // so a half that runs one step ahead never overwrites a value its partner has yet to read).
-        const float mh = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        const float mh = fmaxf(fmax3f(m4[0], m4[1], m4[2]), m4[3]);
         const float mt = fmaxf(mh, exchange(xmax + (k & 1) * 2 * kBT, mh, k));
         if (!ok) break;
         // Lazy rescaling of the running maximum (both halves of a row take the same decision).
