@@ -59,9 +59,17 @@ int tb_parts_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcTbParts : 2
 // The backward follows the same choice as the forward: tensor cores for fp16 with a supported D, FFMA otherwise.
 int bwd_path(int requested, int dtype, int D) { return pick_path(requested, dtype, D); }
 
-size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
+// The forward's workspace without the key-range split's partial outputs: what fpa_fwd needs at least.
+size_t fwd_ws_min(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
   return fpa::kStatusBytes + fpa::stats_bytes(d) + (path == FPA_PATH_TENSOR ? fpa::keycols_bytes(d) : 0);
+}
+
+// What fpa_fwd_workspace_bytes reports: the minimum plus, on the tensor-core path, the partial outputs of the
+// key-range split that small grids take on the current device.
+size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
+  const size_t m = fwd_ws_min(dtype, B, H, T, D, path);
+  return path == FPA_PATH_TENSOR ? m + fpa::tc_fwd_split_bytes(fpa::make_dims(B, H, T, D, tile_of(path))) : m;
 }
 
 size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
@@ -73,6 +81,12 @@ size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
 }  // namespace
 
 void fpa::set_last_error(const std::string& msg) { g_last_error = msg; }
+
+size_t fpa::fwd_workspace_min_bytes(int dtype, int B, int H, int T, int D, int path) {
+  if (check_common(dtype, B, H, T, D, 1.f) != FPA_OK) return 0;
+  const int p = pick_path(path, dtype, D);
+  return p < 0 ? 0 : fwd_ws_min(dtype, B, H, T, D, p);
+}
 
 extern "C" {
 
@@ -105,7 +119,7 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
     return fail(FPA_ERR_INVALID_ARGUMENT, "null tensor pointer");
   int path = pick_path(a->path, a->dtype, a->D);
   if (path < 0) return fail(FPA_ERR_UNSUPPORTED, "the tensor-core path needs fp16 inputs and D in {16, 32, 64, 128}");
-  rc = check_workspace(a->workspace, a->workspace_bytes, fwd_ws(a->dtype, a->B, a->H, a->T, a->D, path));
+  rc = check_workspace(a->workspace, a->workspace_bytes, fwd_ws_min(a->dtype, a->B, a->H, a->T, a->D, path));
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   fpa::Dims d = fpa::make_dims(a->B, a->H, a->T, a->D, tile_of(path));
@@ -121,7 +135,8 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
   if (path == FPA_PATH_TENSOR) {
     int n = 0;
     fpa::prof_mark(s, "fwd_tc");
-    rc = fpa::tc_fwd(*a, d, st, cols, status, s, &n, &g_last_error);
+    const size_t used = fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::keycols_bytes(d);
+    rc = fpa::tc_fwd(*a, d, st, cols, ws + used, a->workspace_bytes - used, status, s, &n, &g_last_error);
     a->kernels_launched += n;
     if (rc) return rc;
   } else {

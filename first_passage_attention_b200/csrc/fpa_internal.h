@@ -54,6 +54,10 @@ cudaError_t allow_dynamic_smem(const void* fn, int bytes);
 // Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
 void set_last_error(const std::string& msg);
 
+// The least workspace fpa_fwd accepts for these sizes (fpa_fwd_workspace_bytes without the room for the
+// forward's key-range split, which fpa_fwd then leaves out); 0 for invalid sizes (fpa_capi.cu).
+size_t fwd_workspace_min_bytes(int dtype, int B, int H, int T, int D, int path);
+
 // Workspace carving (all arrays 256-byte aligned, after the 256-byte status word).
 size_t stats_bytes(const Dims& d);
 size_t bwd_scratch_bytes(const Dims& d, int tb_parts);

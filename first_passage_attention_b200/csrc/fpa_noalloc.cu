@@ -107,7 +107,7 @@ extern "C" FPA_API int fpa_fwd_noalloc(FpaFwdArgs* a, void* stream) {
     }
     return FPA_OK;
   }
-  const size_t need = fpa_fwd_workspace_bytes(a->dtype, a->B, a->H, a->T, a->D, a->path);
+  const size_t need = fpa::fwd_workspace_min_bytes(a->dtype, a->B, a->H, a->T, a->D, a->path);
   if (need == 0) return fpa_fwd(a, stream);  // invalid sizes: let fpa_fwd report them with its messages
   if (need > kNoAllocScratchBytes) {
     // Too large for the built-in scratch: nothing is launched.

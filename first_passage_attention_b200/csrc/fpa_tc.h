@@ -33,10 +33,23 @@ bool tma_layout_ok(const void* p, const int64_t st[4]);
 // is one box row (128 B for D >= 64, 64 B for D = 32, 32 B for D = 16); rows >= T read as zero.
 bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T, int D);
 
-// Forward pass on the tensor cores; `status` is the device status word of the workspace. Sets *launched to the
-// number of kernels launched. Returns an FpaStatus; on failure writes a message into *err.
-int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
-           int* launched, std::string* err);
+// Key-range split of the forward for grids too small to fill the SMs: each query tile's key tiles, from the
+// diagonal down, go in chunks of L tiles to separate CTAs (`items_per_head` CTAs per head), whose unnormalised
+// outputs a combine kernel joins in chunk order. L = 0: no split. Depends on the current device's SM count, and
+// FPA_B200_FWD_SPLIT=0 in the environment turns it off (the results then do not depend on how many heads a call
+// holds: a head computes bit for bit the same alone or inside a larger batch).
+struct FwdSplit {
+  int L = 0, items_per_head = 0;
+};
+FwdSplit tc_fwd_split_plan(const Dims& d);
+size_t tc_fwd_split_bytes(const Dims& d);  // workspace for the chunks' partial outputs (0 without a split)
+
+// Forward pass on the tensor cores; `status` is the device status word of the workspace and `split_ws` the
+// `split_avail` bytes after the key vectors. The key-range split runs only when split_avail covers
+// tc_fwd_split_bytes(d); otherwise the unsplit kernels run (same results up to the order of the additions).
+// Sets *launched to the number of kernels launched. Returns an FpaStatus; on failure writes a message into *err.
+int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, char* split_ws,
+           size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err);
 
 // Backward pass on the tensor cores (fp16). `extra` is tc_bwd_extra_bytes(d) bytes of workspace (raw key vectors,
 // the stored g of the diagonal tiles, a padded copy of lse). Launches the field statistics, delta, the kv-pass,

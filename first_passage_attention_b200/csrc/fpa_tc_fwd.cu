@@ -29,6 +29,7 @@
 //   o_done[x]           MMA commit -> softmax x (final O_x complete)
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -85,6 +86,19 @@ struct TcFwdParams {
   int* status;
   int B, H, T, NB, TP, NPAIR;
   float scale2;        // D^-1/2 * log2(e)
+};
+
+// Key-range split of the one-tile kernel (L = 0: none): chunk c of query tile i covers key tiles i - c L down to
+// max(0, i - c L - L + 1); a head's IPH chunks are numbered with i descending, c ascending. Query tiles with more
+// than one chunk leave their unnormalised output in po [z * IPH + chunk][D / 4][128] (float4 groups of columns,
+// rows innermost, so that a warp's stores and the combine kernel's loads are coalesced) with the row maximum pm
+// and row sum pl [z * IPH + chunk][128] for fwd_combine_kernel. A separate kernel argument, so that the two-tile
+// kernel's parameters stay as they are.
+struct FwdSplitParams {
+  int L, IPH;
+  float4* po;
+  float* pm;
+  float* pl;
 };
 
 // With kEmuEvery > 0, every kEmuEvery-th pair of columns takes its exponentials on the FMA pipe instead of the
@@ -537,7 +551,7 @@ struct Fwd1Cfg {
 template <int D>
 __global__ void __launch_bounds__(kThreads1, 2)
 tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-               const __grid_constant__ CUtensorMap tv, const TcFwdParams p) {
+               const __grid_constant__ CUtensorMap tv, const TcFwdParams p, const FwdSplitParams sp) {
   using C = Fwd1Cfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -557,11 +571,24 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   float* xmax = reinterpret_cast<float*>(smem + C::OFF_X);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-d grid in longest-first order: every head's last query tile (the most key tiles) first.
+  // 1-d grid in longest-first order: every head's last query tile (the most key tiles) first. With a key-range
+  // split the CTA takes one chunk: key tiles jhi, jhi - 1, ..., jlo of query tile i.
   const int nbh = p.B * p.H;
-  const int i = p.NB - 1 - int(blockIdx.x) / nbh;
   const int z = int(blockIdx.x) % nbh, b = z / p.H, h = z % p.H;
-  const int nsteps = i + 1;
+  int i = p.NB - 1 - int(blockIdx.x) / nbh, jhi = i, jlo = 0, slot = -1;
+  if (sp.L > 0) {
+    const int u0 = int(blockIdx.x) / nbh;
+    int u = u0;
+    for (i = p.NB - 1; i > 0; --i) {
+      const int nc = (i + sp.L) / sp.L;
+      if (u < nc) break;
+      u -= nc;
+    }
+    jhi = i - u * sp.L;
+    jlo = max(0, jhi - sp.L + 1);
+    if (i >= sp.L) slot = z * sp.IPH + u0;  // more than one chunk: partial output
+  }
+  const int nsteps = jhi - jlo + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -603,7 +630,7 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     bool ok = true;
     const size_t colbase = size_t(z) * p.TP;
     for (int k = 0; k < nsteps && ok; ++k) {
-      const int st = k % C::NS, j = i - k;
+      const int st = k % C::NS, j = jhi - k;
       if (k >= C::NS) ok = mbar_wait(kv_empty + st, ((k / C::NS) - 1) & 1, p.status, 31);
       if (!ok) break;
       uint8_t* sk = smem + C::OFF_K + st * C::TILEB;
@@ -698,6 +725,7 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     const float pre_t = p.pre[size_t(z) * p.TP + t];
     const float* bmin = p.bmin + size_t(z) * p.NB;
     float mrow = -kInf, lrow = 0.f, mid = kInf;  // lrow: this half's part of the row sum
+    for (int jj = jhi + 1; jj < i; ++jj) mid = fminf(mid, bmin[jj]);  // a chunk below the diagonal
     bool ok = true;
     // Exchange with the other half of the row through buffer `buf` ([2][128]) at exchange number `ph`: publish
     // v, meet on x_pair[q] (bounded wait), return the partner's value.
@@ -712,7 +740,7 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       auto ext = [](float a, float b2) { return NEG ? fmaxf(a, b2) : fminf(a, b2); };
       const float2 sc2 = make_float2(p.scale2, p.scale2);
       for (int k = 0; k < nsteps && ok; ++k) {
-        const int j = i - k, st = k % C::NS;
+        const int j = jhi - k, st = k % C::NS;
         ok = mbar_wait(k_full + st, (k / C::NS) & 1, p.status, 50);
         if (ok) ok = mbar_wait(s_full, k & 1, p.status, 51);
         if (!ok) break;
@@ -830,7 +858,23 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     float l = lrow;
     if (ok) l += exchange(xmax + (nsteps & 1) * 2 * kBT, lrow, nsteps);
     if (ok) ok = mbar_wait(o_done, 0, p.status, 52);
-    if (ok) {
+    if (ok && slot >= 0) {
+      // One chunk of several: the unnormalised output, row maximum and row sum for the combine kernel.
+      tc_fence_after();
+      float4* pcol = sp.po + size_t(slot) * (D / 4) * kBT + (half * (D / 8)) * kBT + r;
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 8) {
+        float o[8];
+        tmem_ld8(tl + C::COL_O + half * (D / 2) + c, o);
+        tmem_ld_wait();
+        pcol[(c / 4) * kBT] = make_float4(o[0], o[1], o[2], o[3]);
+        pcol[(c / 4 + 1) * kBT] = make_float4(o[4], o[5], o[6], o[7]);
+      }
+      if (half == 0) {
+        sp.pm[size_t(slot) * kBT + r] = mrow;
+        sp.pl[size_t(slot) * kBT + r] = l;
+      }
+    } else if (ok) {
       tc_fence_after();
       const float inv = 1.f / l;
       const bool store = t < p.T;
@@ -860,22 +904,59 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   }
 }
 
+// Joins the chunks of the query tiles that the one-tile kernel split (block = query tile L + blockIdx.x of head z,
+// thread = row), in chunk order: M = max of the chunks' row maxima, l = sum of l_c 2^(m_c - M), O = sum of
+// O_c 2^(m_c - M); then o = O / l and lse = M + log2 l, as the unsplit kernel writes them.
 template <int D>
-int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
-            std::string* err) {
-  using C = Fwd1Cfg<D>;
-  CUtensorMap mq, mk, mv;
-  if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
-      !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D)) {
-    *err = "cuTensorMapEncodeTiled failed for q, k or v";
-    return FPA_ERR_CUDA;
+__global__ void __launch_bounds__(kBT) fwd_combine_kernel(const TcFwdParams p, const FwdSplitParams sp) {
+  const int i = sp.L + int(blockIdx.x), z = blockIdx.y, r = threadIdx.x;
+  const int nc = (i + sp.L) / sp.L;
+  const int t = i * kBT + r;
+  if (t >= p.T) return;
+  int base = 0;  // chunks of the query tiles after i (numbered first)
+  for (int ii = p.NB - 1; ii > i; --ii) base += (ii + sp.L) / sp.L;
+  const size_t s0 = size_t(z) * sp.IPH + base;
+  float M = -kInf;
+  for (int c = 0; c < nc; ++c) M = fmaxf(M, sp.pm[(s0 + c) * kBT + r]);
+  float l = 0.f, acc[D];
+#pragma unroll
+  for (int e = 0; e < D; ++e) acc[e] = 0.f;
+  for (int c = 0; c < nc; ++c) {
+    const float w = ex2(sp.pm[(s0 + c) * kBT + r] - M);
+    l = fmaf(sp.pl[(s0 + c) * kBT + r], w, l);
+    const float4* src = sp.po + (s0 + c) * (D / 4) * kBT + r;
+#pragma unroll
+    for (int e = 0; e < D / 4; ++e) {
+      const float4 v = src[e * kBT];
+      acc[4 * e] = fmaf(v.x, w, acc[4 * e]);
+      acc[4 * e + 1] = fmaf(v.y, w, acc[4 * e + 1]);
+      acc[4 * e + 2] = fmaf(v.z, w, acc[4 * e + 2]);
+      acc[4 * e + 3] = fmaf(v.w, w, acc[4 * e + 3]);
+    }
   }
-  auto fn = tc_fwd1_kernel<D>;
-  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(fn), C::SMEM);
-  if (e != cudaSuccess) {
-    *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
-    return FPA_ERR_CUDA;
+  const float inv = 1.f / l;
+  const int b = z / p.H, h = z % p.H;
+  __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(t) * p.o_st;
+#pragma unroll
+  for (int e = 0; e < D; e += 8) {
+    uint4 w0;
+    w0.x = pack_half2(acc[e] * inv, acc[e + 1] * inv);
+    w0.y = pack_half2(acc[e + 2] * inv, acc[e + 3] * inv);
+    w0.z = pack_half2(acc[e + 4] * inv, acc[e + 5] * inv);
+    w0.w = pack_half2(acc[e + 6] * inv, acc[e + 7] * inv);
+    reinterpret_cast<uint4*>(orow + e)[0] = w0;
   }
+  p.lse[size_t(z) * p.T + t] = M + lg2(l);
+}
+
+// Chunks per head with chunks of L key tiles: query tile i has ceil((i + 1) / L) of them.
+int chunks_per_head(int NB, int L) {
+  int n = 0;
+  for (int i = 0; i < NB; ++i) n += (i + L) / L;
+  return n;
+}
+
+TcFwdParams fwd_params(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status) {
   TcFwdParams p;
   p.cola = cols.a;
   p.colpsi = cols.psi;
@@ -895,19 +976,61 @@ int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& 
   p.NB = d.NB;
   p.TP = d.TP;
   p.NPAIR = 0;
-  p.scale2 = float(1.0 / sqrt(double(D))) * kLog2e;
-  fn<<<d.NB * d.BH(), kThreads1, C::SMEM, s>>>(mq, mk, mv, p);
+  p.scale2 = float(1.0 / sqrt(double(d.D))) * kLog2e;
+  return p;
+}
+
+// One-tile forward; with sp.L > 0 its chunks and then the combine kernel. Sets *launched.
+template <int D>
+int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, const FwdSplit& sp,
+            char* split_ws, int* status, cudaStream_t s, int* launched, std::string* err) {
+  using C = Fwd1Cfg<D>;
+  CUtensorMap mq, mk, mv;
+  if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
+      !make_tile_map(&mv, a.v, a.v_stride, d.B, d.H, d.T, D)) {
+    *err = "cuTensorMapEncodeTiled failed for q, k or v";
+    return FPA_ERR_CUDA;
+  }
+  auto fn = tc_fwd1_kernel<D>;
+  cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(fn), C::SMEM);
+  if (e != cudaSuccess) {
+    *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
+    return FPA_ERR_CUDA;
+  }
+  const TcFwdParams p = fwd_params(a, d, st, cols, status);
+  FwdSplitParams q{0, 0, nullptr, nullptr, nullptr};
+  int grid = d.NB * d.BH();
+  if (sp.L > 0) {
+    const size_t n = size_t(d.BH()) * sp.items_per_head * kBT;
+    q.L = sp.L;
+    q.IPH = sp.items_per_head;
+    q.po = reinterpret_cast<float4*>(split_ws);
+    q.pm = reinterpret_cast<float*>(split_ws + align256(n * D * sizeof(float)));
+    q.pl = q.pm + align256(n * sizeof(float)) / sizeof(float);
+    grid = sp.items_per_head * d.BH();
+  }
+  fn<<<grid, kThreads1, C::SMEM, s>>>(mq, mk, mv, p, q);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
+  }
+  *launched = 1;
+  if (sp.L > 0) {
+    fwd_combine_kernel<D><<<dim3(d.NB - sp.L, d.BH()), kBT, 0, s>>>(p, q);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      *err = std::string("forward combine launch: ") + cudaGetErrorString(e);
+      return FPA_ERR_CUDA;
+    }
+    *launched = 2;
   }
   return FPA_OK;
 }
 
 template <int D>
 int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
-           std::string* err) {
+           int* launched, std::string* err) {
   using C = TcFwdCfg<D>;
   CUtensorMap mq, mk, mv;
   if (!make_tile_map(&mq, a.q, a.q_stride, d.B, d.H, d.T, D) || !make_tile_map(&mk, a.k, a.k_stride, d.B, d.H, d.T, D) ||
@@ -921,41 +1044,58 @@ int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
     *err = std::string("tensor-core forward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
-  TcFwdParams p;
-  p.cola = cols.a;
-  p.colpsi = cols.psi;
-  p.colphi = cols.phi;
-  p.pre = st.pre;
-  p.bmin = st.bmin;
-  p.beta = a.beta;
-  p.o = static_cast<__half*>(a.o);
-  p.o_sb = a.o_stride[0];
-  p.o_sh = a.o_stride[1];
-  p.o_st = a.o_stride[2];
-  p.lse = a.lse;
-  p.status = status;
-  p.B = d.B;
-  p.H = d.H;
-  p.T = d.T;
-  p.NB = d.NB;
-  p.TP = d.TP;
+  TcFwdParams p = fwd_params(a, d, st, cols, status);
   p.NPAIR = (d.NB + 1) / 2;
-  p.scale2 = float(1.0 / sqrt(double(D))) * kLog2e;
   fn<<<p.NPAIR * d.BH(), kThreads, C::SMEM, s>>>(mq, mk, mv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
+  *launched = 1;
   return FPA_OK;
+}
+
+// D <= 64: the two-tile kernel while its grid fills the SMs (two query tiles per CTA share every K and V tile
+// they load, half the L2 traffic); below that the one-tile kernel (twice as many CTAs, two per SM).
+bool use_one_tile(const Dims& d) { return d.D <= 64 && int64_t((d.NB + 1) / 2) * d.BH() < sm_count(); }
+
+bool split_enabled() {
+  const char* e = getenv("FPA_B200_FWD_SPLIT");
+  return !(e && e[0] == '0' && e[1] == 0);
 }
 
 }  // namespace
 
 bool tc_supports(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
-int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, int* status, cudaStream_t s,
-           int* launched, std::string* err) {
+FwdSplit tc_fwd_split_plan(const Dims& d) {
+  FwdSplit sp;
+  if (!tc_supports(d.D) || !use_one_tile(d) || d.NB < 4 || !split_enabled()) return sp;
+  // The one-tile grid (NB CTAs per head, the longest NB key tiles) leaves some of the 2 x SMs CTA slots idle;
+  // cut each query tile's key range into chunks of L tiles, L as small as keeps every chunk in one wave of the
+  // slots, and only when that at least halves the longest chain of key tiles.
+  const int64_t slots = 2 * int64_t(sm_count());
+  for (int L = 2; 2 * L <= d.NB; ++L) {
+    const int iph = chunks_per_head(d.NB, L);
+    if (int64_t(iph) * d.BH() <= slots) {
+      sp.L = L;
+      sp.items_per_head = iph;
+      return sp;
+    }
+  }
+  return sp;
+}
+
+size_t tc_fwd_split_bytes(const Dims& d) {
+  const FwdSplit sp = tc_fwd_split_plan(d);
+  if (sp.L == 0) return 0;
+  const size_t n = size_t(d.BH()) * sp.items_per_head * kBT;
+  return align256(n * d.D * sizeof(float)) + 2 * align256(n * sizeof(float));
+}
+
+int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, char* split_ws,
+           size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err) {
   *launched = 0;
   if (!tma_layout_ok(a.q, a.q_stride) || !tma_layout_ok(a.k, a.k_stride) || !tma_layout_ok(a.v, a.v_stride)) {
     *err = "the tensor-core path needs q, k, v with unit innermost stride and 16-byte aligned rows";
@@ -965,19 +1105,25 @@ int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
     *err = "the tensor-core path needs o with unit innermost stride and 16-byte aligned rows";
     return FPA_ERR_UNSUPPORTED;
   }
-  int rc;
-  const bool small = int64_t((d.NB + 1) / 2) * d.BH() < sm_count();
+  const bool one = use_one_tile(d);
+  FwdSplit sp;
+  if (one) {
+    sp = tc_fwd_split_plan(d);
+    if (sp.L > 0 && split_avail < tc_fwd_split_bytes(d)) sp = FwdSplit{};  // a workspace sized without the split
+  }
   switch (d.D) {
-    // D <= 64: two query tiles per CTA share every K and V tile they load (half the L2 traffic), which wins while
-    // their grid fills the SMs; below that, single-tile CTAs (twice as many, two per SM) finish sooner.
-    case 16: rc = small ? launch1<16>(a, d, st, cols, status, s, err) : launch<16>(a, d, st, cols, status, s, err); break;
-    case 32: rc = small ? launch1<32>(a, d, st, cols, status, s, err) : launch<32>(a, d, st, cols, status, s, err); break;
-    case 64: rc = small ? launch1<64>(a, d, st, cols, status, s, err) : launch<64>(a, d, st, cols, status, s, err); break;
-    case 128: rc = launch<128>(a, d, st, cols, status, s, err); break;
+    case 16:
+      return one ? launch1<16>(a, d, st, cols, sp, split_ws, status, s, launched, err)
+                 : launch<16>(a, d, st, cols, status, s, launched, err);
+    case 32:
+      return one ? launch1<32>(a, d, st, cols, sp, split_ws, status, s, launched, err)
+                 : launch<32>(a, d, st, cols, status, s, launched, err);
+    case 64:
+      return one ? launch1<64>(a, d, st, cols, sp, split_ws, status, s, launched, err)
+                 : launch<64>(a, d, st, cols, status, s, launched, err);
+    case 128: return launch<128>(a, d, st, cols, status, s, launched, err);
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  if (rc == FPA_OK) *launched = 1;
-  return rc;
 }
 
 }  // namespace fpa

