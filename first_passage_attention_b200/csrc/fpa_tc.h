@@ -51,11 +51,23 @@ size_t tc_fwd_split_bytes(const Dims& d);  // workspace for the chunks' partial 
 int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, char* split_ws,
            size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err);
 
+// Work-unit split of the persistent backward passes for grids too small to fill the SMs: kv-pass units (a key
+// tile's query tiles) and q-pass units (a query tile's key tiles) longer than L tiles are cut into chunks of L
+// (`units_per_head` units per head and pass), whose partial results two combine kernels join in chunk order.
+// L = 0: no split. Depends on the current device's SM count; FPA_B200_BWD_SPLIT=0 in the environment turns it off.
+struct BwdSplit {
+  int L = 0, units_per_head = 0;
+};
+BwdSplit tc_bwd_split_plan(const Dims& d);
+size_t tc_bwd_split_bytes(const Dims& d);  // workspace for the chunks' partial results (0 without a split)
+
 // Backward pass on the tensor cores (fp16). `extra` is tc_bwd_extra_bytes(d) bytes of workspace (raw key vectors,
-// the stored g of the diagonal tiles, a padded copy of lse). Launches the field statistics, delta, the kv-pass,
-// the diagonal soft-min and the q-pass; the caller then runs the dphi combination and the dbeta reduction.
+// the stored g of the diagonal tiles, a padded copy of lse), `split_ws` the `split_avail` bytes after it; the
+// work-unit split runs only when split_avail covers tc_bwd_split_bytes(d). Launches the field statistics, delta,
+// the kv-pass, the diagonal soft-min and the q-pass (and the split's combine kernels); the caller then runs the
+// dphi combination and the dbeta reduction.
 size_t tc_bwd_extra_bytes(const Dims& d);
-int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
-           cudaStream_t s, int* launched, std::string* err);
+int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, char* split_ws,
+           size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err);
 
 }  // namespace fpa
