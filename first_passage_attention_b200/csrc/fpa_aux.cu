@@ -67,11 +67,13 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
-                             const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv) {
+                             const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv, int* tile_cnt,
+                             int ncnt) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (NB, H, B): z = b * H + h
   if (j == 0 && z == 0 && tid < 4 && status) status[tid] = 0;  // status word and the work-unit counters
+  if (tid < ncnt) tile_cnt[(size_t(z) * NB + j) * ncnt + tid] = 0;  // the split kernels' per-tile join counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
   // Tensor-core backward: delta_t = sum_d dO[t, d] O[t, d] (kernel.py:166-174) in float32, read coalesced: each warp
@@ -210,11 +212,12 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
 
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
-                         const Fact* fact, const QvIn* qv) {
+                         const Fact* fact, const QvIn* qv, int* tile_cnt, int ncnt) {
   const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   const QvIn q = qv ? *qv : QvIn{nullptr, Str4{0, 0, 0, 0}, nullptr, Str4{0, 0, 0, 0}, nullptr, nullptr, 0};
   stats_kernel<<<dim3(d.NB, d.H, d.B), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
-                                                   cols_scaled, beta, d.H, f, status, q);
+                                                   cols_scaled, beta, d.H, f, status, q, tile_cnt,
+                                                   tile_cnt ? ncnt : 0);
   return cudaGetLastError();
 }
 

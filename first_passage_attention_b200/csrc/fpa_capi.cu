@@ -72,18 +72,10 @@ size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
   return path == FPA_PATH_TENSOR ? m + fpa::tc_fwd_split_bytes(fpa::make_dims(B, H, T, D, tile_of(path))) : m;
 }
 
-// The backward's workspace without the work-unit split's partial results: what fpa_bwd needs at least.
-size_t bwd_ws_min(int dtype, int B, int H, int T, int D, int path) {
+size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
   return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, tb_parts_of(path)) +
          (path == FPA_PATH_TENSOR ? fpa::tc_bwd_extra_bytes(d) : 0);
-}
-
-// What fpa_bwd_workspace_bytes reports: the minimum plus, on the tensor-core path, the partial results of the
-// work-unit split that small grids take on the current device.
-size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
-  const size_t m = bwd_ws_min(dtype, B, H, T, D, path);
-  return path == FPA_PATH_TENSOR ? m + fpa::tc_bwd_split_bytes(fpa::make_dims(B, H, T, D, tile_of(path))) : m;
 }
 
 }  // namespace
@@ -135,15 +127,20 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
   int* status = reinterpret_cast<int*>(ws);
   fpa::Stats st = fpa::carve_stats(ws + fpa::kStatusBytes, d);
   fpa::KeyCols cols{nullptr, nullptr, nullptr};
-  if (path == FPA_PATH_TENSOR) cols = fpa::carve_keycols(ws + fpa::kStatusBytes + fpa::stats_bytes(d), d);
+  int* join_cnt = nullptr;  // the key-range split's per-tile counters, zeroed by the stats kernel
+  const size_t used = fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::keycols_bytes(d);
+  if (path == FPA_PATH_TENSOR) {
+    cols = fpa::carve_keycols(ws + fpa::kStatusBytes + fpa::stats_bytes(d), d);
+    join_cnt = fpa::tc_fwd_split_counters(d, ws + used, a->workspace_bytes - used);
+  }
   fpa::prof_mark(s, "stats");
-  cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, cols, 1, status, s);
+  cudaError_t e = fpa::launch_stats(a->phi, a->psi, a->beta, d, a->tau, st, cols, 1, status, s, nullptr, nullptr,
+                                    join_cnt, 1);
   if (e != cudaSuccess) return cuda_fail(e, "stats kernel");
   a->kernels_launched = 1;
   if (path == FPA_PATH_TENSOR) {
     int n = 0;
     fpa::prof_mark(s, "fwd_tc");
-    const size_t used = fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::keycols_bytes(d);
     rc = fpa::tc_fwd(*a, d, st, cols, ws + used, a->workspace_bytes - used, status, s, &n, &g_last_error);
     a->kernels_launched += n;
     if (rc) return rc;
@@ -168,7 +165,7 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
     return fail(FPA_ERR_INVALID_ARGUMENT, "null tensor pointer");
   int path = bwd_path(a->path, a->dtype, a->D);
   if (path < 0) return fail(FPA_ERR_UNSUPPORTED, "the tensor-core path needs fp16 inputs and D in {16, 32, 64, 128}");
-  rc = check_workspace(a->workspace, a->workspace_bytes, bwd_ws_min(a->dtype, a->B, a->H, a->T, a->D, path));
+  rc = check_workspace(a->workspace, a->workspace_bytes, bwd_ws(a->dtype, a->B, a->H, a->T, a->D, path));
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   fpa::Dims d = fpa::make_dims(a->B, a->H, a->T, a->D, tile_of(path));
@@ -180,11 +177,8 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   cudaError_t e;
   if (path == FPA_PATH_TENSOR) {
     char* extra = ws + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, sc.tb_parts);
-    const size_t used = fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, sc.tb_parts) +
-                        fpa::tc_bwd_extra_bytes(d);
     int m = 0;
-    rc = fpa::tc_bwd(*a, d, st, sc, extra, extra + fpa::tc_bwd_extra_bytes(d), a->workspace_bytes - used, status, s,
-                     &m, &g_last_error);
+    rc = fpa::tc_bwd(*a, d, st, sc, extra, status, s, &m, &g_last_error);
     n += m;
     if (rc) {
       a->kernels_launched = n;

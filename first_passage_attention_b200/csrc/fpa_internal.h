@@ -68,9 +68,12 @@ BwdScratch carve_bwd(char* base, const Dims& d, int tb_parts);
 size_t keycols_bytes(const Dims& d);
 KeyCols carve_keycols(char* base, const Dims& d);
 // cols_scaled = 1: the forward's b'-scaled key vectors; 0: raw (a = SUF - psi, psi, phi) for the backward.
+// tile_cnt (optional): ncnt ints per (head, tile), [BH][NB][ncnt], set to zero (the join counters of the split
+// kernels that follow).
 cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, const Dims& d, float tau,
                          const Stats& st, const KeyCols& cols, int cols_scaled, int* status, cudaStream_t s,
-                         const Fact* fact = nullptr, const QvIn* qv = nullptr);
+                         const Fact* fact = nullptr, const QvIn* qv = nullptr, int* tile_cnt = nullptr,
+                         int ncnt = 0);
 cudaError_t launch_delta(int dtype, const void* o, Str4 so, const void* dout, Str4 sdo, const Dims& d, float* delta,
                          const float* lse, float* lsep, cudaStream_t s);
 cudaError_t launch_qv_pack(const float* lse, const float* delta, const float* pre, const float* prey, const Dims& d,

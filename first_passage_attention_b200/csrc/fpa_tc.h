@@ -35,14 +35,17 @@ bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int 
 
 // Key-range split of the forward for grids too small to fill the SMs: each query tile's key tiles, from the
 // diagonal down, go in chunks of L tiles to separate CTAs (`items_per_head` CTAs per head), whose unnormalised
-// outputs a combine kernel joins in chunk order. L = 0: no split. Depends on the current device's SM count, and
-// FPA_B200_FWD_SPLIT=0 in the environment turns it off (the results then do not depend on how many heads a call
-// holds: a head computes bit for bit the same alone or inside a larger batch).
+// outputs the chunk that finishes last joins in chunk order. L = 0: no split. Depends on the current device's SM
+// count, and FPA_B200_FWD_SPLIT=0 in the environment turns it off (the results then do not depend on how many
+// heads a call holds: a head computes bit for bit the same alone or inside a larger batch).
 struct FwdSplit {
   int L = 0, items_per_head = 0;
 };
 FwdSplit tc_fwd_split_plan(const Dims& d);
 size_t tc_fwd_split_bytes(const Dims& d);  // workspace for the chunks' partial outputs (0 without a split)
+// The split's per-tile join counters ([BH][NB] ints at the head of split_ws, which the stats kernel zeroes), or
+// nullptr when this call runs unsplit (no split planned, or split_avail short of tc_fwd_split_bytes).
+int* tc_fwd_split_counters(const Dims& d, char* split_ws, size_t split_avail);
 
 // Forward pass on the tensor cores; `status` is the device status word of the workspace and `split_ws` the
 // `split_avail` bytes after the key vectors. The key-range split runs only when split_avail covers
@@ -51,23 +54,11 @@ size_t tc_fwd_split_bytes(const Dims& d);  // workspace for the chunks' partial 
 int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, char* split_ws,
            size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err);
 
-// Work-unit split of the persistent backward passes for grids too small to fill the SMs: kv-pass units (a key
-// tile's query tiles) and q-pass units (a query tile's key tiles) longer than L tiles are cut into chunks of L
-// (`units_per_head` units per head and pass), whose partial results two combine kernels join in chunk order.
-// L = 0: no split. Depends on the current device's SM count; FPA_B200_BWD_SPLIT=0 in the environment turns it off.
-struct BwdSplit {
-  int L = 0, units_per_head = 0;
-};
-BwdSplit tc_bwd_split_plan(const Dims& d);
-size_t tc_bwd_split_bytes(const Dims& d);  // workspace for the chunks' partial results (0 without a split)
-
 // Backward pass on the tensor cores (fp16). `extra` is tc_bwd_extra_bytes(d) bytes of workspace (raw key vectors,
-// the stored g of the diagonal tiles, a padded copy of lse), `split_ws` the `split_avail` bytes after it; the
-// work-unit split runs only when split_avail covers tc_bwd_split_bytes(d). Launches the field statistics, delta,
-// the kv-pass, the diagonal soft-min and the q-pass (and the split's combine kernels); the caller then runs the
-// dphi combination and the dbeta reduction.
+// the stored g of the diagonal tiles, a padded copy of lse). Launches the field statistics, delta, the kv-pass,
+// the diagonal soft-min and the q-pass; the caller then runs the dphi combination and the dbeta reduction.
 size_t tc_bwd_extra_bytes(const Dims& d);
-int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, char* split_ws,
-           size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err);
+int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
+           cudaStream_t s, int* launched, std::string* err);
 
 }  // namespace fpa

@@ -23,8 +23,6 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <cmath>
-#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -144,78 +142,6 @@ struct TcBwdParams {
   int B, H, T, NB, TP;
   float scale, scale2, il2;
 };
-
-// Split of the persistent passes' work units for grids too small to fill the SMs (L = 0: none). A kv-pass unit is
-// then a chunk of at most L query tiles of one key tile j: chunk c covers i = j + c L .. min(NB, j + c L + L) - 1;
-// a q-pass unit a chunk of at most L key tiles of one query tile i, from the diagonal down: chunk c covers
-// j = i - c L down to max(0, i - c L - L + 1). A head has UPH units per pass (numbered key tile ascending / query
-// tile descending, then chunk ascending). Tiles with more than one chunk leave partial results in the slot of
-// their unit (z * UPH + unit), joined in chunk order by kv_combine_kernel / q_combine_kernel:
-//   kv: dV, dK [slot][D/4][128] float4 (rows innermost: coalesced stores and loads), per key the dpsi sum g and
-//       the W sum [slot][128], the dbeta partial [slot];
-//   q:  dQ [slot][D/4][128] float4, per query r_t [slot][128].
-struct BwdSplitParams {
-  int L, UPH;
-  float4* pdv;
-  float4* pdk;
-  float* pg;
-  float* pw;
-  float* pdb;
-  float4* pdq;
-  float* pr;
-};
-
-// Chunks of key tile j (kv) / query tile i (q).
-__host__ __device__ __forceinline__ int kv_chunks(int NB, int j, int L) { return (NB - j + L - 1) / L; }
-__host__ __device__ __forceinline__ int q_chunks(int i, int L) { return (i + L) / L; }
-
-struct KvUnit {
-  int j, i0, nsteps, slot;  // key tile, first query tile, query tiles, partial slot (-1: final results)
-};
-__device__ __forceinline__ KvUnit kv_unit(int u0, int z, int NB, const BwdSplitParams& sp) {
-  KvUnit r;
-  if (sp.L == 0) {
-    r.j = r.i0 = u0;
-    r.nsteps = NB - u0;
-    r.slot = -1;
-    return r;
-  }
-  int u = u0, j = 0;
-  for (; j < NB - 1; ++j) {
-    const int nc = kv_chunks(NB, j, sp.L);
-    if (u < nc) break;
-    u -= nc;
-  }
-  r.j = j;
-  r.i0 = j + u * sp.L;
-  r.nsteps = min(sp.L, NB - r.i0);
-  r.slot = NB - j > sp.L ? z * sp.UPH + u0 : -1;
-  return r;
-}
-
-struct QUnit {
-  int i, jhi, nsteps, slot;  // query tile, first (highest) key tile, key tiles, partial slot (-1: final results)
-};
-__device__ __forceinline__ QUnit q_unit(int u0, int z, int NB, const BwdSplitParams& sp) {
-  QUnit r;
-  if (sp.L == 0) {
-    r.i = r.jhi = NB - 1 - u0;
-    r.nsteps = r.i + 1;
-    r.slot = -1;
-    return r;
-  }
-  int u = u0, i = NB - 1;
-  for (; i > 0; --i) {
-    const int nc = q_chunks(i, sp.L);
-    if (u < nc) break;
-    u -= nc;
-  }
-  r.i = i;
-  r.jhi = i - u * sp.L;
-  r.nsteps = min(sp.L, r.jhi + 1);
-  r.slot = i + 1 > sp.L ? z * sp.UPH + u0 : -1;
-  return r;
-}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
@@ -348,42 +274,6 @@ __device__ __forceinline__ bool bar_all(bool v, int id, int n) {
 __device__ __forceinline__ bool rows_all(bool v) { return bar_all(v, kNamedBarRows, kRowThreads); }  // 256 row threads
 __device__ __forceinline__ bool diag_all(bool v) { return bar_all(v, kNamedBarDiag, 64); }  // warps 2-3
 
-// DPHI2_u = sum_{t >= u in the tile} 2^{a2_u - c2_t} r_t (u in the query's own tile). PRE is non-increasing within
-// the tile, so DPHI2_u = 2^{a2_u - c2_u} Q_u with Q_u = r_u + f_u Q_{u+1}, f_u = 2^{c2_u - c2_{u+1}} <= 1, a linear
-// recurrence that contracts. One warp solves it: four positions per lane, then a suffix scan of the lanes' affine
-// maps Q_{4l} = A + B Q_{4l+4}. On entry rsh holds r (both row groups joined) and csh c2; on exit rsh holds Q.
-// Positions >= tend count as zero.
-__device__ __forceinline__ void dphi2_scan(float* rsh, const float* csh, int tend, int lane) {
-  float rv[4], fv[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int u = 4 * lane + e;
-    rv[e] = u < tend ? rsh[u] : 0.f;
-    fv[e] = u + 1 < tend ? ex2(csh[u] - csh[u + 1]) : 0.f;
-  }
-  float A = rv[3], Bm = fv[3];
-#pragma unroll
-  for (int e = 2; e >= 0; --e) {
-    A = fmaf(fv[e], A, rv[e]);
-    Bm *= fv[e];
-  }
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float A2 = __shfl_down_sync(0xffffffffu, A, o), B2 = __shfl_down_sync(0xffffffffu, Bm, o);
-    if (lane + o < 32) {
-      A = fmaf(Bm, A2, A);
-      Bm *= B2;
-    }
-  }
-  float qn = __shfl_down_sync(0xffffffffu, A, 1);  // Q_{4l+4}
-  if (lane == 31) qn = 0.f;
-#pragma unroll
-  for (int e = 3; e >= 0; --e) {
-    qn = fmaf(fv[e], qn, rv[e]);
-    rsh[4 * lane + e] = qn;
-  }
-}
-
 // ------------------------------------------------------------------------------------------------ kv-pass ----
 // Persistent, like the q-pass: work units are key tiles j of one head (longest first) taken from a counter. The
 // producer stages each unit's K and V tiles by TMA (or, when K and V stay in shared memory, loads them there once
@@ -395,7 +285,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                 const TcBwdParams p, const BwdSplitParams sp) {
+                 const TcBwdParams p) {
   using C = TcBwdCfg<D, true>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -422,7 +312,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbh = p.B * p.H;
-  const int nunits = (sp.L > 0 ? sp.UPH : p.NB) * nbh;
+  const int nunits = p.NB * nbh;
   // K and V as TMEM operands of S^T and dP^T (both stationary) when the columns fit.
   constexpr bool AT = C::AT;
   constexpr int COL_K = C::COL_X, COL_V = COL_K + D / 2;
@@ -481,11 +371,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       }
       x = __shfl_sync(0xffffffffu, x, 0);
       if (x >= nunits) break;
-      const int z = x % nbh, b = z / p.H, h = z % p.H;
-      const KvUnit ku = kv_unit(x / nbh, z, p.NB, sp);
-      const int j = ku.j;
+      const int j = x / nbh, z = x % nbh, b = z / p.H, h = z % p.H;
       const size_t zb = size_t(z) * p.TP;
-      const int nsteps = ku.nsteps;
+      const int nsteps = p.NB - j;
       if constexpr (AT) {
         if (nx > 0) ok = mbar_wait(x_empty, (nx - 1) & 1, p.status, 131);
         if (!ok) break;
@@ -519,7 +407,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         ++nx;
       }
       for (int k = 0; k < nsteps && ok; ++k) {
-        const int st = gk % C::NS, i = ku.i0 + k;
+        const int st = gk % C::NS, i = j + k;
         if (gk >= C::NS) ok = mbar_wait(st_empty + st, ((gk / C::NS) - 1) & 1, p.status, 101);
         if (!ok) break;
         if (elect_one()) {
@@ -561,7 +449,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(u_empty + us);
       if (x >= nunits) break;
-      const int njobs = 2 * kv_unit(x / nbh, x % nbh, p.NB, sp).nsteps;
+      const int njobs = 2 * (p.NB - x / nbh);
       auto need_tile = [&](int kt) {
         const int gt = gk + kt;
         if (ok && gt > loaded) {
@@ -633,7 +521,6 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     float* mm = es + kBT;  // per-warp maximum and minimum of a2 over the tile's positions
     const int wt = threadIdx.x - 64;
     bool ok = true;
-    int nd = 0;  // units with a diagonal tile taken so far (their g_full / g_free phases)
     for (int u = 0;; ++u) {
       const int us = u % kUQ;
       int x = nunits;
@@ -642,10 +529,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(u_empty + us);
       if (!diag_all(ok && x < nunits)) break;
-      const int z = x % nbh;
-      const KvUnit ku = kv_unit(x / nbh, z, p.NB, sp);
-      if (ku.i0 != ku.j) continue;  // a chunk past the diagonal tile: nothing to do here
-      const int j = ku.j;
+      const int j = x / nbh, z = x % nbh;
       const size_t zb = size_t(z) * p.TP;
       const int tend = min(kBT, p.T - j * kBT);
       float vmax = -kInf, vmin = kInf;
@@ -673,7 +557,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         for (int t = wt; t < kBT; t += 64) es[t] = t < tend ? ex2(a2s[t] - M) : 0.f;
         asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");
       }
-      ok = mbar_wait(g_full, nd & 1, p.status, 130);
+      ok = mbar_wait(g_full, u & 1, p.status, 130);
       if (ok && fast) {
 #pragma unroll 1
         for (int q = 0; q < 2; ++q) {
@@ -781,7 +665,6 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       }
       asm volatile("bar.sync %0, 64;" ::"r"(kNamedBarDiag) : "memory");  // G, a2s, es, mm are reused
       mbar_arrive(g_free);
-      ++nd;
     }
   } else if (warp >= kRowWarp0) {
     regs_rows<D>();
@@ -797,9 +680,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     int gn = 0, gk = 0;
     // The finished unit, written out after the next unit's K and V rows are in TMEM.
     bool have_prev = false, pv_done = false, pv_ok = false;
-    int pv_s = 0, pv_j = 0, pv_b = 0, pv_h = 0, pv_z = 0, pv_slot = -1;
+    int pv_s = 0, pv_j = 0, pv_b = 0, pv_h = 0, pv_z = 0;
     float pv_g = 0.f, pv_db = 0.f, pv_w = 0.f, pv_bh = 0.f;
-    int nd = 0;  // units with a diagonal tile taken so far (their g_full / g_free phases)
     for (int u = 0;; ++u) {
       const int us = u % kUQ;
       int x = nunits;
@@ -808,9 +690,8 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(u_empty + us);
       const bool more = rows_all(ok && x < nunits);
+      const int j = more ? x / nbh : 0;
       const int z = more ? x % nbh : 0, b = z / p.H, h = z % p.H;
-      const KvUnit ku = more ? kv_unit(x / nbh, z, p.NB, sp) : KvUnit{0, 0, 0, -1};
-      const int j = ku.j;
       const size_t zb = size_t(z) * p.TP;
       const int s = j * kBT + r;
       const bool s_ok = more && s < p.T;
@@ -823,9 +704,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         xs_s = p.xs[zb + s];  // SUF_s - psi_s (+inf for the last key of the tile)
         suf_s = p.suf[zb + s];
         sufl_s = p.sufl[zb + s];
-        bl_n = p.bl[size_t(z) * p.NB + ku.i0];
-        bmin_n = p.bmin[size_t(z) * p.NB + ku.i0];
-        prer_n = p.prer[size_t(z) * p.NB + ku.i0];
+        bl_n = p.bl[size_t(z) * p.NB + j];
+        bmin_n = p.bmin[size_t(z) * p.NB + j];
+        prer_n = p.prer[size_t(z) * p.NB + j];
       }
       if constexpr (AT) {
         // The previous unit's last S^T / dP^T products (the last readers of the K and V columns) are complete:
@@ -847,6 +728,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         // dV and dK of the finished unit out of TMEM (its MMAs have completed); the MMA warp may then start this
         // unit's.
         if (pv_done && !mbar_wait(acc_done, (u - 1) & 1, p.status, 122)) pv_done = pv_ok = ok = false;
+        pv_done = __all_sync(0xffffffffu, pv_done);  // warp-uniform: the TMEM loads below are warp-collective
         if (pv_done) {
           tc_fence_after();
           __half* dvrow = p.dv + pv_b * p.dv_s[0] + pv_h * p.dv_s[1] + int64_t(pv_s) * p.dv_s[2];
@@ -858,16 +740,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
               tmem_ld16(tl + C::COL_A1 + c, a1);
               tmem_ld16(tl + C::COL_A2 + c, a2);
               tmem_ld_wait();
-              if (pv_ok && pv_slot >= 0) {
-                // One chunk of several: fp32 partials (dK unscaled) for kv_combine_kernel.
-                float4* pv4 = sp.pdv + (size_t(pv_slot) * (D / 4) + c / 4) * kBT + r;
-                float4* pk4 = sp.pdk + (size_t(pv_slot) * (D / 4) + c / 4) * kBT + r;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  pv4[e * kBT] = make_float4(a1[4 * e], a1[4 * e + 1], a1[4 * e + 2], a1[4 * e + 3]);
-                  pk4[e * kBT] = make_float4(a2[4 * e], a2[4 * e + 1], a2[4 * e + 2], a2[4 * e + 3]);
-                }
-              } else if (pv_ok) {
+              if (pv_ok) {
                 uint32_t u1[8], u2[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -891,25 +764,15 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         }
         rows_sync();
         if (pv_ok && grp == 0) {
-          if (pv_slot >= 0) {
-            sp.pg[size_t(pv_slot) * kBT + r] = pv_g + xg[r];
-            sp.pw[size_t(pv_slot) * kBT + r] = pv_w + xw[r];
-          } else {
-            p.dpsi[size_t(pv_z) * p.T + pv_s] = -pv_bh * (pv_g + xg[r]);
-            p.w[size_t(pv_z) * p.TP + pv_s] = pv_w + xw[r];
-          }
+          p.dpsi[size_t(pv_z) * p.T + pv_s] = -pv_bh * (pv_g + xg[r]);
+          p.w[size_t(pv_z) * p.TP + pv_s] = pv_w + xw[r];
         }
         const float db = rows_sum(pv_db, red);  // xg, xw are next written after rows_all
-        if (threadIdx.x == kRowWarp0 * 32) {
-          if (pv_slot >= 0)
-            sp.pdb[pv_slot] = db;
-          else
-            p.dbeta[size_t(pv_z) * p.NB + pv_j] = db;
-        }
+        if (threadIdx.x == kRowWarp0 * 32) p.dbeta[size_t(pv_z) * p.NB + pv_j] = db;
       }
       if (!more) break;
 
-      const int nsteps = ku.nsteps;
+      const int nsteps = p.NB - j;
       const float betal = bh * kLog2e;
       const float c2_s = suf_s < kInf ? -suf_s * p.il2 : -kInf;
       const float* bmin = p.bmin + size_t(z) * p.NB;
@@ -919,20 +782,11 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       float gsum = 0.f, dbsum = 0.f, wsum = 0.f;
       float2 gsum2 = make_float2(0.f, 0.f), dbsum2 = make_float2(0.f, 0.f);
       float mid = kInf, midl = -kInf;
-      // A chunk past the diagonal starts with the tiles strictly between j and its first query tile already
-      // passed, folded in the order the unsplit walk folds them. (The split is planned for D <= 64 only: for
-      // D = 128 a start value that is not a constant costs this kernel register spills.)
-      if constexpr (D <= 64) {
-        for (int ii = j + 1; ii < ku.i0; ++ii) {
-          mid = fminf(mid, bmin[ii]);
-          midl = lse2(midl, bl[ii]);
-        }
-      }
       // Per-tile scalars of query tile i (those of the first tile were loaded above), loaded one tile ahead so
       // their latency hides behind the element work.
       const float* prer = p.prer + size_t(z) * p.NB;
       for (int k = 0; k < nsteps && ok; ++k) {
-        const int gt = gk + k, st = gt % C::NS, i = ku.i0 + k;
+        const int gt = gk + k, st = gt % C::NS, i = j + k;
         const float bli = bl_n, bmini = bmin_n, preri = prer_n;
         if (i + 1 < p.NB) {
           bl_n = bl[i + 1];
@@ -951,7 +805,7 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         const float4* QV = reinterpret_cast<const float4*>(vbase);  // query pairs: (-lse, -delta), (PRE, prey)
         const float* vprel = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
         const float* vphi = reinterpret_cast<const float*>(vbase + 5 * C::VECB);
-        const bool diag = i == j;
+        const bool diag = k == 0;
         const float cmid2 = mid < kInf ? -mid * p.il2 : -kInf;
         float rs = fmaxf(c2_s, cmid2);
         const bool vrs = !diag && rs > -kInf;
@@ -1070,10 +924,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         };
         if (diag) {
           // The diagonal tile writes its g into G: the soft-min warps must be done with the previous unit's.
-          if (C::FUSEDIAG && nd > 0) ok = mbar_wait(g_free, (nd - 1) & 1, p.status, 123);
+          if (C::FUSEDIAG && u > 0) ok = mbar_wait(g_free, (u - 1) & 1, p.status, 123);
           if (!ok) break;
           tile(std::true_type{}, std::false_type{});
-          ++nd;
         }
         else if (fact)
           tile(std::false_type{}, std::true_type{});
@@ -1109,7 +962,6 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
       pv_db = dbsum;
       pv_w = wsum;
       pv_bh = bh;
-      pv_slot = ku.slot;
       gn += 2 * nsteps;
       gk += nsteps;
     }
@@ -1132,7 +984,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                const TcBwdParams p, const BwdSplitParams sp) {
+                const TcBwdParams p) {
   using C = TcBwdCfg<D, false>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1156,7 +1008,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbh = p.B * p.H;
-  const int nunits = (sp.L > 0 ? sp.UPH : p.NB) * nbh;
+  const int nunits = p.NB * nbh;
   // Q and dO (stationary) as TMEM operands of S and dP.
   constexpr int COL_Q = C::COL_X, COL_DO = COL_Q + D / 2;
 
@@ -1211,9 +1063,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
       x = __shfl_sync(0xffffffffu, x, 0);
       if (x >= nunits) break;
-      const int z = x % nbh, b = z / p.H, h = z % p.H;
-      const QUnit qu = q_unit(x / nbh, z, p.NB, sp);
-      const int i = qu.i;
+      const int i = p.NB - 1 - x / nbh, z = x % nbh, b = z / p.H, h = z % p.H;
       const size_t zb = size_t(z) * p.TP;
       if (nx > 0) ok = mbar_wait(x_empty, (nx - 1) & 1, p.status, 231);
       if (!ok) break;
@@ -1226,8 +1076,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       }
       __syncwarp();
       ++nx;
-      for (int k = 0; k < qu.nsteps && ok; ++k, ++gk) {
-        const int st = gk % C::NS, j = qu.jhi - k;
+      for (int k = 0; k <= i && ok; ++k, ++gk) {
+        const int st = gk % C::NS, j = i - k;
         if (gk >= C::NS) ok = mbar_wait(st_empty + st, ((gk / C::NS) - 1) & 1, p.status, 201);
         if (!ok) break;
         if (elect_one()) {
@@ -1266,7 +1116,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) mbar_arrive(u_empty + us);
       if (x >= nunits) break;
-      const int njobs = 2 * q_unit(x / nbh, x % nbh, p.NB, sp).nsteps;
+      const int i = p.NB - 1 - x / nbh;
+      const int njobs = 2 * (i + 1);
       auto need_tile = [&](int kt) {
         const int gt = gk + kt;
         if (ok && gt > loaded) {
@@ -1320,7 +1171,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     int gn = 0, gk = 0;
     // The finished unit, read out and written after the next unit's Q and dO rows are in TMEM.
     bool have_prev = false, pv_done = false;
-    int pv_t = 0, pv_i = 0, pv_b = 0, pv_h = 0, pv_slot = -1;
+    int pv_t = 0, pv_i = 0, pv_b = 0, pv_h = 0;
     size_t pv_zb = 0;
     bool pv_ok = false;
     float pv_racc = 0.f, pv_c2 = 0.f, pv_a2 = 0.f;
@@ -1332,9 +1183,8 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(u_empty + us);
       const bool more = rows_all(ok && x < nunits);
+      const int i = more ? p.NB - 1 - x / nbh : 0;
       const int z = more ? x % nbh : 0, b = z / p.H, h = z % p.H;
-      const QUnit qu = more ? q_unit(x / nbh, z, p.NB, sp) : QUnit{0, 0, 0, -1};
-      const int i = qu.i;
       const size_t zb = size_t(z) * p.TP;
       const int t = i * kBT + r;
       const bool t_ok = more && t < p.T;
@@ -1350,10 +1200,10 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         prel_t = p.prel[zb + t];
         phi_t = p.phi[zb + t];
         beta_h = p.beta[h];
-        bl_n = p.bl[size_t(z) * p.NB + qu.jhi];
-        bmin_n = p.bmin[size_t(z) * p.NB + qu.jhi];
-        sufr_n = p.sufr[size_t(z) * p.NB + qu.jhi];
-        sufl0_n = p.sufl[zb + size_t(qu.jhi) * kBT];
+        bl_n = p.bl[size_t(z) * p.NB + i];
+        bmin_n = p.bmin[size_t(z) * p.NB + i];
+        sufr_n = p.sufr[size_t(z) * p.NB + i];
+        sufl0_n = p.sufl[zb + size_t(i) * kBT];
       }
       // The previous unit's last S / dP products (the last readers of the Q and dO columns) are complete: s_last
       // is waited in unit order, and its next phase needs this unit's Q and dO.
@@ -1373,6 +1223,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         // dQ of the finished unit out of TMEM (its MMAs have completed); the MMA warp may then start this unit's.
         float dqv[DH];
         bool done = pv_done && mbar_wait(acc_done, (u - 1) & 1, p.status, 222);
+        done = __all_sync(0xffffffffu, done);  // warp-uniform: the TMEM loads below are warp-collective
         if (done) {
           tc_fence_after();
           if (D >= 32 || grp == 0) {
@@ -1385,43 +1236,65 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         mbar_arrive(acc_free);
         if (!done) ok = false;
         if (done && pv_ok && (D >= 32 || grp == 0)) {
-          if (pv_slot >= 0) {
-            // One chunk of several: the fp32 partial (unscaled) for q_combine_kernel.
-            float4* pq4 = sp.pdq + (size_t(pv_slot) * (D / 4) + grp * (DH / 4)) * kBT + r;
+          __half* dqrow = p.dq + pv_b * p.dq_s[0] + pv_h * p.dq_s[1] + int64_t(pv_t) * p.dq_s[2] + grp * DH;
 #pragma unroll
-            for (int c = 0; c < DH; c += 4) pq4[(c / 4) * kBT] = make_float4(dqv[c], dqv[c + 1], dqv[c + 2], dqv[c + 3]);
-          } else {
-            __half* dqrow = p.dq + pv_b * p.dq_s[0] + pv_h * p.dq_s[1] + int64_t(pv_t) * p.dq_s[2] + grp * DH;
+          for (int c = 0; c < DH; c += 8) {
+            uint32_t w4[4];
 #pragma unroll
-            for (int c = 0; c < DH; c += 8) {
-              uint32_t w4[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) w4[e] = pack_half2(dqv[c + 2 * e] * p.scale, dqv[c + 2 * e + 1] * p.scale);
-              reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
+            for (int e = 0; e < 4; ++e) w4[e] = pack_half2(dqv[c + 2 * e] * p.scale, dqv[c + 2 * e + 1] * p.scale);
+            reinterpret_cast<uint4*>(dqrow + c)[0] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
         }
-        // r_t joins the two groups' partial sums in a fixed order (group 0 + group 1); a chunk of several leaves it
-        // for q_combine_kernel, which then runs the DPHI2 recurrence. rsh, csh and rx are next written after the
-        // rows_all of the next unit.
+        // DPHI2_u = sum_{t >= u in this tile} 2^{a2_u - c2_t} r_t  (u in the query's own tile), with r_t joining
+        // the two groups' partial sums in a fixed order. PRE is non-increasing within the tile, so
+        //   DPHI2_u = 2^{a2_u - c2_u} Q_u,  Q_u = r_u + f_u Q_{u+1},  f_u = 2^{c2_u - c2_{u+1}} <= 1,
+        // a linear recurrence that contracts; the first row warp solves it: four positions per lane, then a suffix
+        // scan of the lanes' affine maps Q_{4l} = A + B Q_{4l+4}.
         if (grp == 1) rx[r] = pv_racc;
         rows_sync();
-        if (pv_slot >= 0) {
-          if (grp == 0 && pv_ok) sp.pr[size_t(pv_slot) * kBT + r] = pv_racc + rx[r];
-        } else {
-          if (grp == 0) {
-            rsh[r] = pv_racc + rx[r];
-            csh[r] = pv_c2;
-          }
-          rows_sync();
-          if (warp == kRowWarp0) dphi2_scan(rsh, csh, min(kBT, p.T - pv_i * kBT), lane);
-          rows_sync();
-          if (grp == 0 && pv_ok) p.dphi2[pv_zb + pv_t] = ex2(pv_a2 - pv_c2) * rsh[r];
+        if (grp == 0) {
+          rsh[r] = pv_racc + rx[r];
+          csh[r] = pv_c2;
         }
+        rows_sync();
+        if (warp == kRowWarp0) {
+          const int tend = min(kBT, p.T - pv_i * kBT);
+          float rv[4], fv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int u = 4 * lane + e;
+            rv[e] = u < tend ? rsh[u] : 0.f;
+            fv[e] = u + 1 < tend ? ex2(csh[u] - csh[u + 1]) : 0.f;
+          }
+          float A = rv[3], Bm = fv[3];
+#pragma unroll
+          for (int e = 2; e >= 0; --e) {
+            A = fmaf(fv[e], A, rv[e]);
+            Bm *= fv[e];
+          }
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float A2 = __shfl_down_sync(0xffffffffu, A, o), B2 = __shfl_down_sync(0xffffffffu, Bm, o);
+            if (lane + o < 32) {
+              A = fmaf(Bm, A2, A);
+              Bm *= B2;
+            }
+          }
+          float qn = __shfl_down_sync(0xffffffffu, A, 1);  // Q_{4l+4}
+          if (lane == 31) qn = 0.f;
+#pragma unroll
+          for (int e = 3; e >= 0; --e) {
+            qn = fmaf(fv[e], qn, rv[e]);
+            rsh[4 * lane + e] = qn;
+          }
+        }
+        rows_sync();
+        // rsh, csh and rx are next written after the rows_all of the next unit.
+        if (grp == 0 && pv_ok) p.dphi2[pv_zb + pv_t] = ex2(pv_a2 - pv_c2) * rsh[r];
       }
       if (!more) break;
 
-      const int nsteps = qu.nsteps;
+      const int nsteps = i + 1;
       const float betal = beta_h * kLog2e;
       const float nlse = nl_nd.x, ndel = nl_nd.y;
       const float c2_t = t_ok ? -pre_t * p.il2 : 0.f;
@@ -1433,17 +1306,11 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       const float2 nlse2 = make_float2(nlse, nlse), ndel2 = make_float2(ndel, ndel);
       float2 racc2 = make_float2(0.f, 0.f);
       float mid = kInf, midl = -kInf;
-      // A chunk below the diagonal starts with the key tiles strictly between its first one and i already passed,
-      // folded in the order the unsplit walk folds them.
-      for (int jj = i - 1; jj > qu.jhi; --jj) {
-        mid = fminf(mid, bmin[jj]);
-        midl = lse2(midl, bl[jj]);
-      }
       // Per-tile scalars of key tile j (those of the first tile were loaded above), loaded one tile ahead so their
       // latency hides behind the element work.
       const float* sufr = p.sufr + size_t(z) * p.NB;
       for (int k = 0; k < nsteps && ok; ++k) {
-        const int gt = gk + k, st = gt % C::NS, j = qu.jhi - k;
+        const int gt = gk + k, st = gt % C::NS, j = i - k;
         const float blj = bl_n, bminj = bmin_n, sufrj = sufr_n, sufl0 = sufl0_n;
         if (j > 0) {
           bl_n = bl[j - 1];
@@ -1462,7 +1329,7 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         const uint8_t* vbase = smem + C::OFF_VEC + st * C::VECSTAGE;
         const float4* KV = reinterpret_cast<const float4*>(vbase);  // key pairs: (SUF - psi, -psi), (sufy, SUFL)
         const float* vphi = reinterpret_cast<const float*>(vbase + 4 * C::VECB);
-        const bool diag = j == i;
+        const bool diag = k == 0;
         const float cap = fminf(mid, pre_t);
         const float mterm = ex2(midl - c2_t) + bpre;
         // 2^{SUFL_s - c2_t} = sufy_s * 2^{SUFL_first - c2_t} when both factors stay in range.
@@ -1570,7 +1437,6 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       pv_racc = racc2.x + racc2.y;
       pv_c2 = c2_t;
       pv_a2 = a2_t;
-      pv_slot = qu.slot;
       gn += 2 * nsteps;
       gk += nsteps;
     }
@@ -1581,113 +1447,6 @@ tc_bwd_q_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-}
-
-// Joins the kv-pass chunks of the key tiles that have several (block = key tile blockIdx.x < NB - L of head
-// blockIdx.y, thread = key), in chunk order: dV and dK (fp16; dK times D^-1/2, as the unsplit write-out), dpsi =
-// -beta_h * sum g, W = sum w, and the key tile's dbeta partial (thread 0).
-template <int D>
-__global__ void __launch_bounds__(kBT) kv_combine_kernel(const TcBwdParams p, const BwdSplitParams sp) {
-  const int j = blockIdx.x, z = blockIdx.y, r = threadIdx.x;
-  const int nc = kv_chunks(p.NB, j, sp.L);
-  int base = 0;  // units of the key tiles before j
-  for (int jj = 0; jj < j; ++jj) base += kv_chunks(p.NB, jj, sp.L);
-  const size_t s0 = size_t(z) * sp.UPH + base;
-  const int s = j * kBT + r, b = z / p.H, h = z % p.H;
-  if (r == 0) {
-    float db = 0.f;
-    for (int c = 0; c < nc; ++c) db += sp.pdb[s0 + c];
-    p.dbeta[size_t(z) * p.NB + j] = db;
-  }
-  if (s >= p.T) return;
-  float g = 0.f, w = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    g += sp.pg[(s0 + c) * kBT + r];
-    w += sp.pw[(s0 + c) * kBT + r];
-  }
-  p.dpsi[size_t(z) * p.T + s] = -p.beta[h] * g;
-  p.w[size_t(z) * p.TP + s] = w;
-  __half* dvrow = p.dv + b * p.dv_s[0] + h * p.dv_s[1] + int64_t(s) * p.dv_s[2];
-  __half* dkrow = p.dk + b * p.dk_s[0] + h * p.dk_s[1] + int64_t(s) * p.dk_s[2];
-#pragma unroll
-  for (int e4 = 0; e4 < D / 4; e4 += 2) {
-    float av[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, ak[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < nc; ++c) {
-      const size_t o = ((s0 + c) * (D / 4) + e4) * kBT + r;
-      const float4 v0 = sp.pdv[o], v1 = sp.pdv[o + kBT], k0 = sp.pdk[o], k1 = sp.pdk[o + kBT];
-      av[0] += v0.x, av[1] += v0.y, av[2] += v0.z, av[3] += v0.w, av[4] += v1.x, av[5] += v1.y, av[6] += v1.z;
-      av[7] += v1.w;
-      ak[0] += k0.x, ak[1] += k0.y, ak[2] += k0.z, ak[3] += k0.w, ak[4] += k1.x, ak[5] += k1.y, ak[6] += k1.z;
-      ak[7] += k1.w;
-    }
-    uint4 wv, wk;
-    wv.x = pack_half2(av[0], av[1]);
-    wv.y = pack_half2(av[2], av[3]);
-    wv.z = pack_half2(av[4], av[5]);
-    wv.w = pack_half2(av[6], av[7]);
-    wk.x = pack_half2(ak[0] * p.scale, ak[1] * p.scale);
-    wk.y = pack_half2(ak[2] * p.scale, ak[3] * p.scale);
-    wk.z = pack_half2(ak[4] * p.scale, ak[5] * p.scale);
-    wk.w = pack_half2(ak[6] * p.scale, ak[7] * p.scale);
-    reinterpret_cast<uint4*>(dvrow + 4 * e4)[0] = wv;
-    reinterpret_cast<uint4*>(dkrow + 4 * e4)[0] = wk;
-  }
-}
-
-// Joins the q-pass chunks of the query tiles that have several (block = query tile L + blockIdx.x of head
-// blockIdx.y, thread = query), in chunk order: dQ (fp16, times D^-1/2) and r_t, from which it runs the DPHI2
-// recurrence of the tile (dphi2_scan) as the unsplit q-pass does at the end of a unit.
-template <int D>
-__global__ void __launch_bounds__(kBT) q_combine_kernel(const TcBwdParams p, const BwdSplitParams sp) {
-  __shared__ float rsh[kBT], csh[kBT];
-  const int i = sp.L + int(blockIdx.x), z = blockIdx.y, r = threadIdx.x;
-  const int nc = q_chunks(i, sp.L);
-  int base = 0;  // units of the query tiles after i
-  for (int ii = p.NB - 1; ii > i; --ii) base += q_chunks(ii, sp.L);
-  const size_t s0 = size_t(z) * sp.UPH + base;
-  const int t = i * kBT + r, b = z / p.H, h = z % p.H;
-  const bool t_ok = t < p.T;
-  const size_t zb = size_t(z) * p.TP;
-  float rt = 0.f;
-  if (t_ok)
-    for (int c = 0; c < nc; ++c) rt += sp.pr[(s0 + c) * kBT + r];
-  const float c2 = t_ok ? -p.pre[zb + t] * p.il2 : 0.f;
-  rsh[r] = rt;
-  csh[r] = c2;
-  __syncthreads();
-  if (r < 32) dphi2_scan(rsh, csh, min(kBT, p.T - i * kBT), r);
-  __syncthreads();
-  if (!t_ok) return;
-  p.dphi2[zb + t] = ex2(-p.phi[zb + t] * p.il2 - c2) * rsh[r];
-  __half* dqrow = p.dq + b * p.dq_s[0] + h * p.dq_s[1] + int64_t(t) * p.dq_s[2];
-#pragma unroll
-  for (int e4 = 0; e4 < D / 4; e4 += 2) {
-    float aq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < nc; ++c) {
-      const size_t o = ((s0 + c) * (D / 4) + e4) * kBT + r;
-      const float4 q0 = sp.pdq[o], q1 = sp.pdq[o + kBT];
-      aq[0] += q0.x, aq[1] += q0.y, aq[2] += q0.z, aq[3] += q0.w, aq[4] += q1.x, aq[5] += q1.y, aq[6] += q1.z;
-      aq[7] += q1.w;
-    }
-    uint4 wq;
-    wq.x = pack_half2(aq[0] * p.scale, aq[1] * p.scale);
-    wq.y = pack_half2(aq[2] * p.scale, aq[3] * p.scale);
-    wq.z = pack_half2(aq[4] * p.scale, aq[5] * p.scale);
-    wq.w = pack_half2(aq[6] * p.scale, aq[7] * p.scale);
-    reinterpret_cast<uint4*>(dqrow + 4 * e4)[0] = wq;
-  }
-}
-
-// Units per head of the split passes with chunks of L tiles (the same for both passes).
-int split_units_per_head(int NB, int L) {
-  int n = 0;
-  for (int m = 1; m <= NB; ++m) n += (m + L - 1) / L;
-  return n;
-}
-
-bool bwd_split_enabled() {
-  const char* e = getenv("FPA_B200_BWD_SPLIT");
-  return !(e && e[0] == '0' && e[1] == 0);
 }
 
 // The q-pass depends on nothing the kv-pass writes, so it runs on an auxiliary stream forked from the caller's
@@ -1733,8 +1492,8 @@ bool fork_of(cudaStream_t s, Fork* out) {
 
 template <int D>
 int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, const KeyCols& cols,
-               const Fact& fact, float* gd, const float4* qv4, int* sched, const BwdSplitParams& sp, int* status,
-               cudaStream_t s, std::string* err) {
+               const Fact& fact, float* gd, const float4* qv4, int* sched, int* status, cudaStream_t s,
+               std::string* err) {
   using CK = TcBwdCfg<D, true>;
   using CQ = TcBwdCfg<D, false>;
   CUtensorMap mq, mk, mv, mdo;
@@ -1804,7 +1563,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     *err = std::string("tensor-core backward: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
-  const int grid = (sp.L > 0 ? sp.UPH : d.NB) * d.BH();  // work units per pass
+  const int grid = d.NB * d.BH();
   const int pgrid = std::min(grid, sm_count());  // persistent; the stats kernel zeroed the unit counters
   Fork f;
   const bool forked = !prof_on() && fork_of(s, &f);  // per-kernel timing needs one stream
@@ -1819,25 +1578,15 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     sq = f.aux;
   }
   prof_mark(s, "bwd_kv_tc");
-  kv<<<pgrid, kThreads, smem_kv, s>>>(mq, mk, mv, mdo, p, sp);
+  kv<<<pgrid, kThreads, smem_kv, s>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
-  if (e == cudaSuccess && sp.L > 0) {
-    prof_mark(s, "bwd_kv_combine");
-    kv_combine_kernel<D><<<dim3(d.NB - sp.L, d.BH()), kBT, 0, s>>>(p, sp);
-    e = cudaGetLastError();
-  }
   if (e == cudaSuccess && !CK::FUSEDIAG) {
     prof_mark(s, "diag_dphi");
     e = launch_diag_dphi(a.phi, gd, d, a.tau, sc.dphi4, s);
   }
   if (e == cudaSuccess) {
     prof_mark(s, "bwd_q_tc");
-    qk<<<pgrid, kThreads, smem_q, sq>>>(mq, mk, mv, mdo, p, sp);
-    e = cudaGetLastError();
-  }
-  if (e == cudaSuccess && sp.L > 0) {
-    prof_mark(sq, "bwd_q_combine");
-    q_combine_kernel<D><<<dim3(d.NB - sp.L, d.BH()), kBT, 0, sq>>>(p, sp);
+    qk<<<pgrid, kThreads, smem_q, sq>>>(mq, mk, mv, mdo, p);
     e = cudaGetLastError();
   }
   if (forked) {  // join even after a failed launch, so that no capture is left with a dangling fork
@@ -1868,32 +1617,6 @@ size_t gd_bytes(const Dims& d) {
   return kv_fuses_diag(d.D) ? 0 : align256(size_t(d.BH()) * d.NB * size_t(kBT) * kBT * sizeof(float));
 }
 
-BwdSplit tc_bwd_split_plan(const Dims& d) {
-  BwdSplit sp;
-  if (!tc_supports(d.D) || d.D > 64 || d.NB < 4 || !bwd_split_enabled()) return sp;
-  // Both passes share the SMs (the q-pass on the forked stream); a kv tile step costs about 1.25 q tile steps, so
-  // the balanced finish is near 1.8 W / SMs kv steps for W = BH NB (NB + 1) / 2 tile steps per pass. A unit (the
-  // NB tiles of the first key tile or the last query tile at most) longer than that sets the finish instead:
-  // cut units into chunks of L tiles, so that the longest takes about the balanced time.
-  const double w = double(d.BH()) * d.NB * (d.NB + 1) / 2;
-  const double bound = 1.8 * w / sm_count();
-  if (d.NB <= 1.25 * bound) return sp;
-  const int nch = int(std::ceil(d.NB / std::max(bound, 1.0)));
-  const int L = std::max(2, (d.NB + nch - 1) / nch);
-  if (L >= d.NB) return sp;
-  sp.L = L;
-  sp.units_per_head = split_units_per_head(d.NB, L);
-  return sp;
-}
-
-size_t tc_bwd_split_bytes(const Dims& d) {
-  const BwdSplit sp = tc_bwd_split_plan(d);
-  if (sp.L == 0) return 0;
-  const size_t n = size_t(d.BH()) * sp.units_per_head;
-  return 3 * align256(n * kBT * d.D * sizeof(float)) + 3 * align256(n * kBT * sizeof(float)) +
-         align256(n * sizeof(float));
-}
-
 size_t tc_bwd_extra_bytes(const Dims& d) {
   const size_t bh = size_t(d.BH());
   return keycols_bytes(d) + gd_bytes(d) +
@@ -1901,8 +1624,8 @@ size_t tc_bwd_extra_bytes(const Dims& d) {
          2 * align256(bh * d.NB * sizeof(float));
 }
 
-int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, char* split_ws,
-           size_t split_avail, int* status, cudaStream_t s, int* launched, std::string* err) {
+int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, char* extra, int* status,
+           cudaStream_t s, int* launched, std::string* err) {
   *launched = 0;
   if (!tma_layout_ok(a.q, a.q_stride) || !tma_layout_ok(a.k, a.k_stride) || !tma_layout_ok(a.v, a.v_stride) ||
       !tma_layout_ok(a.dout, a.dout_stride)) {
@@ -1959,32 +1682,15 @@ int tc_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch
     *err = std::string("tensor-core backward prologue: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
   }
-  // The work-unit split when the caller's workspace has room for its partial results.
-  BwdSplitParams sp{0, 0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-  const BwdSplit plan = tc_bwd_split_plan(d);
-  if (plan.L > 0 && split_avail >= tc_bwd_split_bytes(d)) {
-    const size_t n = size_t(d.BH()) * plan.units_per_head;
-    const size_t big = align256(n * kBT * d.D * sizeof(float)), row = align256(n * kBT * sizeof(float));
-    sp.L = plan.L;
-    sp.UPH = plan.units_per_head;
-    sp.pdv = reinterpret_cast<float4*>(split_ws);
-    sp.pdk = reinterpret_cast<float4*>(split_ws + big);
-    sp.pdq = reinterpret_cast<float4*>(split_ws + 2 * big);
-    sp.pg = reinterpret_cast<float*>(split_ws + 3 * big);
-    sp.pw = reinterpret_cast<float*>(split_ws + 3 * big + row);
-    sp.pr = reinterpret_cast<float*>(split_ws + 3 * big + 2 * row);
-    sp.pdb = reinterpret_cast<float*>(split_ws + 3 * big + 3 * row);
-  }
   int rc;
   switch (d.D) {
-    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, sp, status, s, err); break;
-    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, sp, status, s, err); break;
-    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, sp, status, s, err); break;
-    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, sp, status, s, err); break;
+    case 16: rc = launch_bwd<16>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 32: rc = launch_bwd<32>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 64: rc = launch_bwd<64>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
+    case 128: rc = launch_bwd<128>(a, d, st, sc, cols, fact, gd, qv4, status + kSchedKv, status, s, err); break;
     default: *err = "unsupported head dimension for the tensor-core path"; return FPA_ERR_UNSUPPORTED;
   }
-  // stats, [delta, pack], kv, [kv combine], [diag], q, [q combine]
-  if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3) + (sp.L > 0 ? 2 : 0);
+  if (rc == FPA_OK) *launched = nprep + (kv_fuses_diag(d.D) ? 2 : 3);  // stats, [delta, pack], kv, [diag], q
   return rc;
 }
 

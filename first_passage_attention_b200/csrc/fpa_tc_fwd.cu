@@ -91,15 +91,30 @@ struct TcFwdParams {
 // Key-range split of the one-tile kernel (L = 0: none): chunk c of query tile i covers key tiles i - c L down to
 // max(0, i - c L - L + 1); a head's IPH chunks are numbered with i descending, c ascending. Query tiles with more
 // than one chunk leave their unnormalised output in po [z * IPH + chunk][D / 4][128] (float4 groups of columns,
-// rows innermost, so that a warp's stores and the combine kernel's loads are coalesced) with the row maximum pm
-// and row sum pl [z * IPH + chunk][128] for fwd_combine_kernel. A separate kernel argument, so that the two-tile
-// kernel's parameters stay as they are.
+// rows innermost, so that a warp's stores and loads are coalesced) with the row maximum pm and row sum pl
+// [z * IPH + chunk][128], and count themselves in cnt [z][i] (zeroed by the stats kernel); the chunk that counts
+// last joins them. A separate kernel argument, so that the two-tile kernel's parameters stay as they are.
 struct FwdSplitParams {
   int L, IPH;
   float4* po;
   float* pm;
   float* pl;
+  int* cnt;
 };
+
+// AND of v over the 256 softmax threads of the one-tile kernel (named barrier 1; all of them call it).
+__device__ __forceinline__ bool softmax_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v))
+      : "memory");
+  return r != 0;
+}
 
 // With kEmuEvery > 0, every kEmuEvery-th pair of columns takes its exponentials on the FMA pipe instead of the
 // MUFU unit (16 exp2 per clock per SM against 128 FMA lanes). Off by default: measured on B200 at configuration 2
@@ -858,21 +873,71 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     float l = lrow;
     if (ok) l += exchange(xmax + (nsteps & 1) * 2 * kBT, lrow, nsteps);
     if (ok) ok = mbar_wait(o_done, 0, p.status, 52);
-    if (ok && slot >= 0) {
-      // One chunk of several: the unnormalised output, row maximum and row sum for the combine kernel.
-      tc_fence_after();
-      float4* pcol = sp.po + size_t(slot) * (D / 4) * kBT + (half * (D / 8)) * kBT + r;
+    ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the TMEM loads below are warp-collective
+    if (slot >= 0) {
+      // One chunk of several: the unnormalised output, row maximum and row sum, made visible (fence) before the
+      // chunk counts itself; the chunk that counts last joins all chunks of query tile i in chunk order (the same
+      // order whichever chunk that is): M = max of the row maxima, l = sum of l_c 2^(m_c - M), O = sum of
+      // O_c 2^(m_c - M), then o = O / l and lse = M + log2 l as the unsplit kernel writes them. Every softmax
+      // thread reaches the barriers below (a timed-out wait leaves ok false but no thread behind).
+      if (ok) {
+        tc_fence_after();
+        float4* pcol = sp.po + size_t(slot) * (D / 4) * kBT + (half * (D / 8)) * kBT + r;
 #pragma unroll
-      for (int c = 0; c < D / 2; c += 8) {
-        float o[8];
-        tmem_ld8(tl + C::COL_O + half * (D / 2) + c, o);
-        tmem_ld_wait();
-        pcol[(c / 4) * kBT] = make_float4(o[0], o[1], o[2], o[3]);
-        pcol[(c / 4 + 1) * kBT] = make_float4(o[4], o[5], o[6], o[7]);
+        for (int c = 0; c < D / 2; c += 8) {
+          float o[8];
+          tmem_ld8(tl + C::COL_O + half * (D / 2) + c, o);
+          tmem_ld_wait();
+          pcol[(c / 4) * kBT] = make_float4(o[0], o[1], o[2], o[3]);
+          pcol[(c / 4 + 1) * kBT] = make_float4(o[4], o[5], o[6], o[7]);
+        }
+        if (half == 0) {
+          sp.pm[size_t(slot) * kBT + r] = mrow;
+          sp.pl[size_t(slot) * kBT + r] = l;
+        }
+        __threadfence();
       }
-      if (half == 0) {
-        sp.pm[size_t(slot) * kBT + r] = mrow;
-        sp.pl[size_t(slot) * kBT + r] = l;
+      const int nc = (i + sp.L) / sp.L;
+      uint32_t* join = tmem_slot + 1;
+      if (softmax_all(ok) && threadIdx.x == 0) join[0] = atomicAdd(sp.cnt + size_t(z) * p.NB + i, 1) == nc - 1;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (join[0] && ok) {
+        __threadfence();
+        int base = 0;  // chunks of the query tiles after i
+        for (int ii = p.NB - 1; ii > i; --ii) base += (ii + sp.L) / sp.L;
+        const size_t s0 = size_t(z) * sp.IPH + base;
+        float M = -kInf;
+        for (int c = 0; c < nc; ++c) M = fmaxf(M, __ldcg(sp.pm + (s0 + c) * kBT + r));
+        float lt = 0.f, acc[D / 2];
+#pragma unroll
+        for (int e = 0; e < D / 2; ++e) acc[e] = 0.f;
+        for (int c = 0; c < nc; ++c) {
+          const float w = ex2(__ldcg(sp.pm + (s0 + c) * kBT + r) - M);
+          lt = fmaf(__ldcg(sp.pl + (s0 + c) * kBT + r), w, lt);
+          const float4* src = sp.po + ((s0 + c) * (D / 4) + half * (D / 8)) * kBT + r;
+#pragma unroll
+          for (int e = 0; e < D / 8; ++e) {
+            const float4 v = __ldcg(src + e * kBT);
+            acc[4 * e] = fmaf(v.x, w, acc[4 * e]);
+            acc[4 * e + 1] = fmaf(v.y, w, acc[4 * e + 1]);
+            acc[4 * e + 2] = fmaf(v.z, w, acc[4 * e + 2]);
+            acc[4 * e + 3] = fmaf(v.w, w, acc[4 * e + 3]);
+          }
+        }
+        if (t < p.T) {
+          const float inv = 1.f / lt;
+          __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(t) * p.o_st + half * (D / 2);
+#pragma unroll
+          for (int e = 0; e < D / 2; e += 8) {
+            uint4 w0;
+            w0.x = pack_half2(acc[e] * inv, acc[e + 1] * inv);
+            w0.y = pack_half2(acc[e + 2] * inv, acc[e + 3] * inv);
+            w0.z = pack_half2(acc[e + 4] * inv, acc[e + 5] * inv);
+            w0.w = pack_half2(acc[e + 6] * inv, acc[e + 7] * inv);
+            reinterpret_cast<uint4*>(orow + e)[0] = w0;
+          }
+          if (half == 0) p.lse[size_t(z) * p.T + t] = M + lg2(lt);
+        }
       }
     } else if (ok) {
       tc_fence_after();
@@ -902,51 +967,6 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
-}
-
-// Joins the chunks of the query tiles that the one-tile kernel split (block = query tile L + blockIdx.x of head z,
-// thread = row), in chunk order: M = max of the chunks' row maxima, l = sum of l_c 2^(m_c - M), O = sum of
-// O_c 2^(m_c - M); then o = O / l and lse = M + log2 l, as the unsplit kernel writes them.
-template <int D>
-__global__ void __launch_bounds__(kBT) fwd_combine_kernel(const TcFwdParams p, const FwdSplitParams sp) {
-  const int i = sp.L + int(blockIdx.x), z = blockIdx.y, r = threadIdx.x;
-  const int nc = (i + sp.L) / sp.L;
-  const int t = i * kBT + r;
-  if (t >= p.T) return;
-  int base = 0;  // chunks of the query tiles after i (numbered first)
-  for (int ii = p.NB - 1; ii > i; --ii) base += (ii + sp.L) / sp.L;
-  const size_t s0 = size_t(z) * sp.IPH + base;
-  float M = -kInf;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, sp.pm[(s0 + c) * kBT + r]);
-  float l = 0.f, acc[D];
-#pragma unroll
-  for (int e = 0; e < D; ++e) acc[e] = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const float w = ex2(sp.pm[(s0 + c) * kBT + r] - M);
-    l = fmaf(sp.pl[(s0 + c) * kBT + r], w, l);
-    const float4* src = sp.po + (s0 + c) * (D / 4) * kBT + r;
-#pragma unroll
-    for (int e = 0; e < D / 4; ++e) {
-      const float4 v = src[e * kBT];
-      acc[4 * e] = fmaf(v.x, w, acc[4 * e]);
-      acc[4 * e + 1] = fmaf(v.y, w, acc[4 * e + 1]);
-      acc[4 * e + 2] = fmaf(v.z, w, acc[4 * e + 2]);
-      acc[4 * e + 3] = fmaf(v.w, w, acc[4 * e + 3]);
-    }
-  }
-  const float inv = 1.f / l;
-  const int b = z / p.H, h = z % p.H;
-  __half* orow = p.o + b * p.o_sb + h * p.o_sh + int64_t(t) * p.o_st;
-#pragma unroll
-  for (int e = 0; e < D; e += 8) {
-    uint4 w0;
-    w0.x = pack_half2(acc[e] * inv, acc[e + 1] * inv);
-    w0.y = pack_half2(acc[e + 2] * inv, acc[e + 3] * inv);
-    w0.z = pack_half2(acc[e + 4] * inv, acc[e + 5] * inv);
-    w0.w = pack_half2(acc[e + 6] * inv, acc[e + 7] * inv);
-    reinterpret_cast<uint4*>(orow + e)[0] = w0;
-  }
-  p.lse[size_t(z) * p.T + t] = M + lg2(l);
 }
 
 // Chunks per head with chunks of L key tiles: query tile i has ceil((i + 1) / L) of them.
@@ -980,7 +1000,7 @@ TcFwdParams fwd_params(const FpaFwdArgs& a, const Dims& d, const Stats& st, cons
   return p;
 }
 
-// One-tile forward; with sp.L > 0 its chunks and then the combine kernel. Sets *launched.
+// One-tile forward (with sp.L > 0, the chunks of the key-range split, joined in the kernel). Sets *launched.
 template <int D>
 int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, const FwdSplit& sp,
             char* split_ws, int* status, cudaStream_t s, int* launched, std::string* err) {
@@ -998,14 +1018,16 @@ int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& 
     return FPA_ERR_CUDA;
   }
   const TcFwdParams p = fwd_params(a, d, st, cols, status);
-  FwdSplitParams q{0, 0, nullptr, nullptr, nullptr};
+  FwdSplitParams q{0, 0, nullptr, nullptr, nullptr, nullptr};
   int grid = d.NB * d.BH();
   if (sp.L > 0) {
     const size_t n = size_t(d.BH()) * sp.items_per_head * kBT;
+    const size_t nc = align256(size_t(d.BH()) * d.NB * sizeof(int));
     q.L = sp.L;
     q.IPH = sp.items_per_head;
-    q.po = reinterpret_cast<float4*>(split_ws);
-    q.pm = reinterpret_cast<float*>(split_ws + align256(n * D * sizeof(float)));
+    q.cnt = reinterpret_cast<int*>(split_ws);
+    q.po = reinterpret_cast<float4*>(split_ws + nc);
+    q.pm = reinterpret_cast<float*>(split_ws + nc + align256(n * D * sizeof(float)));
     q.pl = q.pm + align256(n * sizeof(float)) / sizeof(float);
     grid = sp.items_per_head * d.BH();
   }
@@ -1016,15 +1038,6 @@ int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& 
     return FPA_ERR_CUDA;
   }
   *launched = 1;
-  if (sp.L > 0) {
-    fwd_combine_kernel<D><<<dim3(d.NB - sp.L, d.BH()), kBT, 0, s>>>(p, q);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) {
-      *err = std::string("forward combine launch: ") + cudaGetErrorString(e);
-      return FPA_ERR_CUDA;
-    }
-    *launched = 2;
-  }
   return FPA_OK;
 }
 
@@ -1091,7 +1104,13 @@ size_t tc_fwd_split_bytes(const Dims& d) {
   const FwdSplit sp = tc_fwd_split_plan(d);
   if (sp.L == 0) return 0;
   const size_t n = size_t(d.BH()) * sp.items_per_head * kBT;
-  return align256(n * d.D * sizeof(float)) + 2 * align256(n * sizeof(float));
+  return align256(size_t(d.BH()) * d.NB * sizeof(int)) + align256(n * d.D * sizeof(float)) +
+         2 * align256(n * sizeof(float));
+}
+
+int* tc_fwd_split_counters(const Dims& d, char* split_ws, size_t split_avail) {
+  if (!use_one_tile(d) || tc_fwd_split_plan(d).L == 0 || split_avail < tc_fwd_split_bytes(d)) return nullptr;
+  return reinterpret_cast<int*>(split_ws);
 }
 
 int tc_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& cols, char* split_ws,

@@ -62,22 +62,19 @@ def test_config2_batch_matches_the_oracle_on_sampled_heads(config2):
 
 
 def _unsplit(fn, *args):
-    """fn(*args) with the forward's key-range split and the backward's work-unit split turned off."""
+    """fn(*args) with the forward's key-range split turned off (FPA_B200_FWD_SPLIT=0)."""
     os.environ["FPA_B200_FWD_SPLIT"] = "0"
-    os.environ["FPA_B200_BWD_SPLIT"] = "0"
     try:
         return fn(*args)
     finally:
         os.environ.pop("FPA_B200_FWD_SPLIT", None)
-        os.environ.pop("FPA_B200_BWD_SPLIT", None)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_strong_split_shards_match_the_whole_batch_bit_for_bit(config2, world):
-    """With the small-grid splits off, a shard's heads come out bit for bit as inside the whole batch. With them on
-    (the default, taken when a shard's grid leaves SMs idle: the forward's at 12 and 6 heads per GPU here, the
-    backward's at 6), the kernels add the same terms in another order, so every output agrees with the whole
-    batch's to the fp16 tolerance."""
+    """With the forward's key-range split off, a shard's heads come out bit for bit as inside the whole batch. With
+    it on (the default, taken when a shard's grid leaves SMs idle: 12 and 6 heads per GPU here), the forward adds
+    the same terms in another order, so every output agrees with the whole batch's to the fp16 tolerance."""
     inp, out = config2
     B, H = 4, 12
     for rank in range(world):
