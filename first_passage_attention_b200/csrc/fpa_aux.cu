@@ -70,6 +70,8 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
                              const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv, int* tile_cnt,
                              int ncnt) {
   __shared__ float wmin[32], wlse[32], smin[1024], slse[1024];
+  pdl_wait();  // launched with launch_pdl: the previous kernel's writes are visible from here on
+  pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = BT >> 5;
   const int j = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (NB, H, B): z = b * H + h
   if (j == 0 && z == 0 && tid < 4 && status) status[tid] = 0;  // status word and the work-unit counters
@@ -215,10 +217,8 @@ cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, 
                          const Fact* fact, const QvIn* qv, int* tile_cnt, int ncnt) {
   const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   const QvIn q = qv ? *qv : QvIn{nullptr, Str4{0, 0, 0, 0}, nullptr, Str4{0, 0, 0, 0}, nullptr, nullptr, 0};
-  stats_kernel<<<dim3(d.NB, d.H, d.B), d.BT, 0, s>>>(phi, psi, d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols,
-                                                   cols_scaled, beta, d.H, f, status, q, tile_cnt,
-                                                   tile_cnt ? ncnt : 0);
-  return cudaGetLastError();
+  return launch_pdl(stats_kernel, dim3(d.NB, d.H, d.B), dim3(d.BT), 0, s, phi, psi, d.BH(), d.T, d.BT, d.NB,
+                    kLog2e / tau, st, cols, cols_scaled, beta, d.H, f, status, q, tile_cnt, tile_cnt ? ncnt : 0);
 }
 
 // delta_t = sum_d dO[t, d] * O[t, d] in float32 (kernel.py:166-174). One warp per row.

@@ -42,6 +42,16 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
+// Programmatic dependent launch (launch_pdl in fpa_internal.h). A kernel launched that way may start while the
+// kernel before it on the stream is still running, once every CTA of that kernel has called pdl_launch_dependents
+// (or exited): its CTAs run their prologue (shared-memory carving, barrier set-up, TMEM allocation), then
+// pdl_wait() blocks until the previous kernel has completed and its memory writes are visible. Every kernel
+// launched that way calls pdl_wait() before its first global-memory access, and pdl_launch_dependents() only after
+// it, so that no more than two kernels of a stream overlap. Both are no-ops for a kernel launched without the
+// attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // log2(2^a + 2^b), with -inf + -inf = -inf (the stable base-2 log-add-exp of kernel.py:73-75).
 __device__ __forceinline__ float lse2(float a, float b) {
   float m = fmaxf(a, b);

@@ -51,6 +51,23 @@ bool prof_on();  // per-kernel timing enabled (the library then launches everyth
 // (fpa_tma.cu). Thread-safe.
 cudaError_t allow_dynamic_smem(const void* fn, int bytes);
 
+// Launches `kernel` on `s` with programmatic stream serialization: it may start while the previous kernel of the
+// stream runs its last CTAs (see pdl_wait / pdl_launch_dependents in fpa_common.cuh, which the kernel must call).
+template <typename... P, typename... A>
+cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 // Records the message that fpa_last_error returns on the calling thread (fpa_capi.cu).
 void set_last_error(const std::string& msg);
 

@@ -347,6 +347,9 @@ tc_bwd_kv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched after the stats kernel with launch_pdl: the prologue above overlapped its last blocks.
+  pdl_wait();
+  pdl_launch_dependents();
   if (warp < kRowWarp0) regs_producer<D>();
 
   if (warp == kWarpProducer) {
@@ -1578,8 +1581,7 @@ int launch_bwd(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScr
     sq = f.aux;
   }
   prof_mark(s, "bwd_kv_tc");
-  kv<<<pgrid, kThreads, smem_kv, s>>>(mq, mk, mv, mdo, p);
-  e = cudaGetLastError();
+  e = launch_pdl(kv, dim3(pgrid), dim3(kThreads), smem_kv, s, mq, mk, mv, mdo, p);
   if (e == cudaSuccess && !CK::FUSEDIAG) {
     prof_mark(s, "diag_dphi");
     e = launch_diag_dphi(a.phi, gd, d, a.tau, sc.dphi4, s);

@@ -208,6 +208,9 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched after the stats kernel with launch_pdl: the prologue above overlapped its last blocks.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // Register split (per warpgroup): the launch gives 168 per thread; the producer/MMA group keeps C::REG_LO and
   // each softmax group takes C::REG_HI (128*40 + 256*232 = 128*24 + 256*240 = 384*168). With 224 the softmax
@@ -626,6 +629,9 @@ tc_fwd1_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched after the stats kernel with launch_pdl: the prologue above overlapped its last blocks.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // Register split: 80 per thread at launch (two CTAs per SM); the softmax warpgroups take 104, the third 32.
   if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 32;" ::: "memory");
@@ -1031,8 +1037,7 @@ int launch1(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& 
     q.pl = q.pm + align256(n * sizeof(float)) / sizeof(float);
     grid = sp.items_per_head * d.BH();
   }
-  fn<<<grid, kThreads1, C::SMEM, s>>>(mq, mk, mv, p, q);
-  e = cudaGetLastError();
+  e = launch_pdl(fn, dim3(grid), dim3(kThreads1), C::SMEM, s, mq, mk, mv, p, q);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
@@ -1059,8 +1064,7 @@ int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
   }
   TcFwdParams p = fwd_params(a, d, st, cols, status);
   p.NPAIR = (d.NB + 1) / 2;
-  fn<<<p.NPAIR * d.BH(), kThreads, C::SMEM, s>>>(mq, mk, mv, p);
-  e = cudaGetLastError();
+  e = launch_pdl(fn, dim3(p.NPAIR * d.BH()), dim3(kThreads), C::SMEM, s, mq, mk, mv, p);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core forward launch: ") + cudaGetErrorString(e);
     return FPA_ERR_CUDA;
