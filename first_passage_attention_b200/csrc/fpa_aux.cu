@@ -373,6 +373,8 @@ __device__ __forceinline__ void join_mv(float& m, float& v, float m2, float v2) 
 
 __global__ void dphi_part3_kernel(const float* __restrict__ bmin, int NB, int LV, float il2, BwdScratch sc) {
   extern __shared__ float rmq[];  // [LV][NB]: rmq[l][n] = max c over tiles n .. n + 2^l - 1
+  pdl_wait();  // launched with launch_pdl after the backward passes
+  pdl_launch_dependents();
   const int z = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nwarps = blockDim.x >> 5;
   for (int n = tid; n < NB; n += blockDim.x) rmq[n] = -bmin[size_t(z) * NB + n] * il2;
   __syncthreads();
@@ -450,6 +452,8 @@ __global__ void dphi_part3_kernel(const float* __restrict__ bmin, int NB, int LV
 __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restrict__ beta, int B, int H, int T,
                             int BT, int NB, float il2, Stats st, BwdScratch sc, float* __restrict__ dphi,
                             float* __restrict__ dbeta, int part3_ready) {
+  pdl_wait();  // launched with launch_pdl after the backward passes (and the join of the forked q-pass)
+  pdl_launch_dependents();
   extern __shared__ float sm[];
   float* cb = sm;           // [NB] max of a2 per tile
   float* A = cb + NB;       // [NB] A[j] = max cb over (j, U]
@@ -575,7 +579,9 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
       cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(dphi_part3_kernel), int(smem3));
       if (e != cudaSuccess) return e;
     }
-    dphi_part3_kernel<<<d.BH(), 1024, smem3, s>>>(st.bmin, d.NB, lv, kLog2e / tau, sc);
+    cudaError_t e = launch_pdl(dphi_part3_kernel, dim3(d.BH()), dim3(1024), smem3, s, st.bmin, d.NB, lv,
+                               kLog2e / tau, sc);
+    if (e != cudaSuccess) return e;
     *launched += 1;
   }
   int threads = d.BT < 32 ? 32 : d.BT;
@@ -584,10 +590,10 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
     cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(dphi_kernel), int(smem));
     if (e != cudaSuccess) return e;
   }
-  dphi_kernel<<<dim3(d.NB, d.H, d.B), threads, smem, s>>>(phi, beta, d.B, d.H, d.T, d.BT, d.NB, kLog2e / tau, st, sc,
-                                                        dphi, dbeta, quadratic ? 1 : 0);
-  *launched += 1;
-  return cudaGetLastError();
+  cudaError_t e = launch_pdl(dphi_kernel, dim3(d.NB, d.H, d.B), dim3(threads), smem, s, phi, beta, d.B, d.H, d.T,
+                             d.BT, d.NB, kLog2e / tau, st, sc, dphi, dbeta, quadratic ? 1 : 0);
+  if (e == cudaSuccess) *launched += 1;
+  return e;
 }
 
 // In-tile soft-min gradient of the diagonal tiles from their stored g (the tensor-core backward writes
@@ -606,6 +612,8 @@ diag_dphi_kernel(const float* __restrict__ phi, const float* __restrict__ gd, in
                  float* __restrict__ dphi4) {
   constexpr int BT = kDiagBT, LD = BT + 1;
   extern __shared__ float dsm[];
+  pdl_wait();  // launched with launch_pdl after the kv-pass, whose stored g it reads
+  pdl_launch_dependents();
   float* G = dsm;           // [BT][BT+1]
   float* a2 = G + BT * LD;  // [BT]
   const int j = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y, sl = threadIdx.x, wq = sl >> 5;  // grid (NB, H, B)
@@ -686,8 +694,8 @@ cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, f
   const int smem = (kDiagBT * (kDiagBT + 1) + kDiagBT) * int(sizeof(float));
   cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(diag_dphi_kernel), smem);
   if (e != cudaSuccess) return e;
-  diag_dphi_kernel<<<dim3(d.NB, d.H, d.B), kDiagBT, smem, s>>>(phi, gd, d.T, d.NB, kLog2e / tau, dphi4);
-  return cudaGetLastError();
+  return launch_pdl(diag_dphi_kernel, dim3(d.NB, d.H, d.B), dim3(kDiagBT), smem, s, phi, gd, d.T, d.NB, kLog2e / tau,
+                    dphi4);
 }
 
 
