@@ -65,6 +65,9 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // memory (kernel.py:84-100 computes the same per-tile statistics). It also clears the device status word of the
 // call's workspace (the first launch of every call), and, when `cols.a` is set, writes the per-key vectors of the
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
+// QV: the tensor-core backward's instantiation, which also forms delta and the per-query pairs (its eight rows of O
+// and dO in flight per lane cost registers that the forward's instantiation does not spend).
+template <bool QV>
 __global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
                              const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv, int* tile_cnt,
@@ -78,41 +81,55 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   if (tid < ncnt) tile_cnt[(size_t(z) * NB + j) * ncnt + tid] = 0;  // the split kernels' per-tile join counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
-  // Tensor-core backward: delta_t = sum_d dO[t, d] O[t, d] (kernel.py:166-174) in float32, read coalesced: each warp
-  // covers its 32 rows with groups of G = D/8 lanes, one 16-byte load of O and of dO per lane per row, a fixed
-  // shuffle tree over the group, and the row's owner thread picks the sum up from shared memory. The loads are
-  // issued before the scans below, so their latency passes meanwhile. Packed with -lse, PRE and prey at the end.
-  __shared__ float sdelta[1024];
+  // Every global load of the kernel is issued here, before any of them is used, so that one memory latency covers
+  // them all (the kernel is latency-bound at small sizes): phi, psi, lse and beta of this block's positions, and
+  // for the tensor-core backward the rows of O and dO for delta_t = sum_d dO[t, d] O[t, d] (kernel.py:166-174).
+  const bool need_psi = fact.kv4 != nullptr || cols.a != nullptr;
+  const float p = t < T ? phi[size_t(z) * T + t] : kInf;
+  const float y_psi = (need_psi && t < T) ? psi[size_t(z) * T + t] : 0.f;
+  const float beta_h = (cols.a && cols_scaled) ? beta[z % H] : 0.f;
   float delta = 0.f, nlse = -kInf;
-  if (qv.qv4) {
+  if (QV && t < T) nlse = -qv.lse[size_t(z) * T + t];
+  // delta in float32, read coalesced: each warp covers its 32 rows with groups of G = D/8 lanes, one 16-byte load
+  // of O and of dO per lane per row (eight rows' loads in flight at once), a fixed shuffle tree over the group, and
+  // the row's owner thread picks the sum up from shared memory. Packed with -lse, PRE and prey at the end.
+  __shared__ float sdelta[1024];
+  if constexpr (QV) {
     const int G = qv.D / 8, rpi = 32 / G, sub = lane / G, part = lane % G;
     const int b = z / H, h = z % H;
     const __half* ob = qv.o + b * qv.so.b + h * qv.so.h + part * 8;
     const __half* db = qv.dout + b * qv.sdo.b + h * qv.sdo.h + part * 8;
-#pragma unroll 4
-    for (int it = 0; it < G; ++it) {
-      const int rr = w * 32 + it * rpi + sub, tt = j * BT + rr;
-      float acc = 0.f;
-      if (tt < T) {
-        const uint4 x = *reinterpret_cast<const uint4*>(ob + int64_t(tt) * qv.so.t);
-        const uint4 y = *reinterpret_cast<const uint4*>(db + int64_t(tt) * qv.sdo.t);
-        const __half2* xh = reinterpret_cast<const __half2*>(&x);
-        const __half2* yh = reinterpret_cast<const __half2*>(&y);
+    for (int it0 = 0; it0 < G; it0 += 8) {
+      uint4 xo[8], xd[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int rr = w * 32 + (it0 + q) * rpi + sub, tt = j * BT + rr;
+        xo[q] = make_uint4(0u, 0u, 0u, 0u);
+        xd[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (it0 + q < G && tt < T) {
+          xo[q] = *reinterpret_cast<const uint4*>(ob + int64_t(tt) * qv.so.t);
+          xd[q] = *reinterpret_cast<const uint4*>(db + int64_t(tt) * qv.sdo.t);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (it0 + q >= G) break;
+        const __half2* xh = reinterpret_cast<const __half2*>(&xo[q]);
+        const __half2* yh = reinterpret_cast<const __half2*>(&xd[q]);
+        float acc = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 a2 = __half22float2(xh[e]), b2 = __half22float2(yh[e]);
           acc = fmaf(a2.x, b2.x, acc);
           acc = fmaf(a2.y, b2.y, acc);
         }
+        for (int o = G >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (part == 0) sdelta[w * 32 + (it0 + q) * rpi + sub] = acc;
       }
-      for (int o = G >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (part == 0) sdelta[rr] = acc;
     }
     __syncwarp();
     delta = sdelta[tid];  // this warp's rows only
-    if (t < T) nlse = -qv.lse[size_t(z) * T + t];
   }
-  const float p = t < T ? phi[size_t(z) * T + t] : kInf;
   const float a = t < T ? -p * il2 : -kInf;
   // inclusive prefix: PRE, PREL
   float pm = p, pl = a;
@@ -180,14 +197,14 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
     }
     if (fact.kv4) {
       // Pair layout: keys c, c+1 (c even) share kv4[c] and kv4[c + 1].
-      const float y = t < T ? psi[size_t(z) * T + t] : 0.f;
+      const float y = y_psi;
       float* kv = reinterpret_cast<float*>(fact.kv4 + base + (tid & ~1)) + (tid & 1);
       kv[0] = t < T ? suf - y : kInf;
       kv[2] = -y;
       kv[4] = ex2(sufl - sufl0);
       kv[6] = sufl;
     }
-    if (qv.qv4) {
+    if (QV) {
       // Pair layout: queries c, c+1 (c even) share qv4[c] = (-lse, -delta) and qv4[c + 1] = (PRE, prey).
       float* qa = reinterpret_cast<float*>(qv.qv4 + base + (tid & ~1)) + (tid & 1);
       qa[0] = nlse;  // -inf beyond T
@@ -198,9 +215,9 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   }
   if (cols.a) {
     const bool ok = t < T;
-    const float y = ok ? psi[size_t(z) * T + t] : 0.f;
+    const float y = y_psi;
     if (cols_scaled) {
-      const float bl = beta[z % H] * kLog2e;
+      const float bl = beta_h * kLog2e;
       cols.a[base + tid] = ok ? bl * fminf(suf - y, 0.f) : 0.f;
       cols.psi[base + tid] = ok ? -bl * y : 0.f;
       cols.phi[base + tid] = ok ? bl * p : 0.f;
@@ -217,8 +234,9 @@ cudaError_t launch_stats(const float* phi, const float* psi, const float* beta, 
                          const Fact* fact, const QvIn* qv, int* tile_cnt, int ncnt) {
   const Fact f = fact ? *fact : Fact{nullptr, nullptr, nullptr, nullptr, nullptr};
   const QvIn q = qv ? *qv : QvIn{nullptr, Str4{0, 0, 0, 0}, nullptr, Str4{0, 0, 0, 0}, nullptr, nullptr, 0};
-  return launch_pdl(stats_kernel, dim3(d.NB, d.H, d.B), dim3(d.BT), 0, s, phi, psi, d.BH(), d.T, d.BT, d.NB,
-                    kLog2e / tau, st, cols, cols_scaled, beta, d.H, f, status, q, tile_cnt, tile_cnt ? ncnt : 0);
+  return launch_pdl(qv ? stats_kernel<true> : stats_kernel<false>, dim3(d.NB, d.H, d.B), dim3(d.BT), 0, s, phi, psi,
+                    d.BH(), d.T, d.BT, d.NB, kLog2e / tau, st, cols, cols_scaled, beta, d.H, f, status, q, tile_cnt,
+                    tile_cnt ? ncnt : 0);
 }
 
 // delta_t = sum_d dO[t, d] * O[t, d] in float32 (kernel.py:166-174). One warp per row.
@@ -464,8 +482,15 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
   const int U = blockIdx.x, z = blockIdx.z * gridDim.y + blockIdx.y, h = z % H;  // grid (NB, H, B)
   const int tid = threadIdx.x;
   const size_t TP = size_t(NB) * BT;
-  for (int n = tid; n < NB; n += blockDim.x) cb[n] = -st.bmin[size_t(z) * NB + n] * il2;
   const int u = U * BT + tid;
+  // The per-position inputs of the final sum are loaded first, with the tile statistics below, so that their
+  // latency passes during the scans (the kernel is latency-bound at small sizes).
+  const bool own = tid < BT && u < T;
+  const size_t pu = size_t(z) * TP + u;
+  const float phi_u = own ? phi[size_t(z) * T + u] : 0.f;
+  const float d2 = own ? sc.dphi2[pu] : 0.f, d4 = own ? sc.dphi4[pu] : 0.f;
+  const float beta_h = beta[h];
+  for (int n = tid; n < NB; n += blockDim.x) cb[n] = -st.bmin[size_t(z) * NB + n] * il2;
   {
     float w = 0.f, c2 = -kInf;
     if (tid < BT) {
@@ -547,12 +572,11 @@ __global__ void dphi_kernel(const float* __restrict__ phi, const float* __restri
     ev = 0.f;
   }
   join(bm, bv, em, ev, em, ev);
-  if (tid < BT && u < T) {
-    float a2 = -phi[size_t(z) * T + u] * il2;
+  if (own) {
+    const float a2 = -phi_u * il2;
     const float part1 = em == -kInf ? 0.f : ev * ex2(em + a2);
-    float part3 = (U > 0 && U < NB - 1) ? ex2(a2 - cb[U]) * S : 0.f;
-    size_t p = size_t(z) * TP + u;
-    dphi[size_t(z) * T + u] = beta[h] * (part1 + sc.dphi2[p] + sc.dphi4[p] + part3);
+    const float part3 = (U > 0 && U < NB - 1) ? ex2(a2 - cb[U]) * S : 0.f;
+    dphi[size_t(z) * T + u] = beta_h * (part1 + d2 + d4 + part3);
   }
   // dbeta[h]: the kv-pass's parts summed over the batch and the key tiles, by the first warp of the blocks
   // (U = 0, b = 0), strided over the lanes and then a fixed shuffle tree (kernel.py:450: dbeta.sum((0, 2))).

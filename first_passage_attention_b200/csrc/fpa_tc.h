@@ -36,8 +36,9 @@ bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int 
 // Key-range split of the forward for grids too small to fill the SMs: each query tile's key tiles, from the
 // diagonal down, go in chunks of L tiles to separate CTAs (`items_per_head` CTAs per head), whose unnormalised
 // outputs the chunk that finishes last joins in chunk order. L = 0: no split. Depends on the current device's SM
-// count, and FPA_B200_FWD_SPLIT=0 in the environment turns it off (the results then do not depend on how many
-// heads a call holds: a head computes bit for bit the same alone or inside a larger batch).
+// count. FPA_B200_FWD_SPLIT=0 in the environment turns it off (the results then do not depend on how many heads a
+// call holds: a head computes bit for bit the same alone or inside a larger batch); FPA_B200_FWD_SPLIT=L (L >= 2)
+// sets the chunk length wherever the one-tile kernel runs.
 struct FwdSplit {
   int L = 0, items_per_head = 0;
 };

@@ -29,9 +29,12 @@
 //   o_done[x]           MMA commit -> softmax x (final O_x complete)
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
+#include <queue>
 #include <type_traits>
+#include <vector>
 
 #include "fpa_sm100.cuh"
 #include "fpa_tc.h"
@@ -1077,9 +1080,14 @@ int launch(const FpaFwdArgs& a, const Dims& d, const Stats& st, const KeyCols& c
 // they load, half the L2 traffic); below that the one-tile kernel (twice as many CTAs, two per SM).
 bool use_one_tile(const Dims& d) { return d.D <= 64 && int64_t((d.NB + 1) / 2) * d.BH() < sm_count(); }
 
-bool split_enabled() {
+// FPA_B200_FWD_SPLIT: unset (or any text that is not a number) for the planned split, 0 for none, L >= 2 for
+// chunks of L key tiles wherever the one-tile kernel runs (a tuning switch; L is capped below NB).
+int split_env() {
   const char* e = getenv("FPA_B200_FWD_SPLIT");
-  return !(e && e[0] == '0' && e[1] == 0);
+  if (e == nullptr || *e == 0) return -1;
+  char* end = nullptr;
+  const long v = strtol(e, &end, 10);
+  return (*end == 0 && v >= 0 && v < (1 << 20)) ? int(v) : -1;
 }
 
 }  // namespace
@@ -1088,17 +1096,44 @@ bool tc_supports(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
 FwdSplit tc_fwd_split_plan(const Dims& d) {
   FwdSplit sp;
-  if (!tc_supports(d.D) || !use_one_tile(d) || d.NB < 4 || !split_enabled()) return sp;
-  // The one-tile grid (NB CTAs per head, the longest NB key tiles) leaves some of the 2 x SMs CTA slots idle;
-  // cut each query tile's key range into chunks of L tiles, L as small as keeps every chunk in one wave of the
-  // slots, and only when that at least halves the longest chain of key tiles.
-  const int64_t slots = 2 * int64_t(sm_count());
-  for (int L = 2; 2 * L <= d.NB; ++L) {
-    const int iph = chunks_per_head(d.NB, L);
-    if (int64_t(iph) * d.BH() <= slots) {
+  const int forced = split_env();
+  if (!tc_supports(d.D) || !use_one_tile(d) || d.NB < 4 || forced == 0 || forced == 1) return sp;
+  if (forced > 1) {
+    if (forced < d.NB) {
+      sp.L = forced;
+      sp.items_per_head = chunks_per_head(d.NB, forced);
+    }
+    return sp;
+  }
+  // The one-tile grid (NB CTAs per head, the longest NB key tiles) leaves CTA slots (two per SM) idle. Pick the chunk
+  // length whose grid finishes first under a list schedule of its CTAs, in launch order, on the slots, each CTA
+  // costing its key tiles plus kChunkCost tiles for its prologue, pipeline fill and epilogue (fitted to chunk-length
+  // sweeps on B200 at 6 and 12 heads of T = 2048); ties keep the longer chunks (fewer partial outputs) or no split.
+  constexpr int kChunkCost = 2;
+  const int slots = 2 * sm_count();
+  auto finish = [&](int L) {  // L = NB: the unsplit grid
+    std::priority_queue<int, std::vector<int>, std::greater<int>> free_at;
+    for (int q = 0; q < slots; ++q) free_at.push(0);
+    int end = 0;
+    for (int i = d.NB - 1; i >= 0; --i)      // launch order: query tile descending, then chunk, then head
+      for (int c = 0; c * L <= i; ++c) {
+        const int len = std::min(L, i + 1 - c * L) + kChunkCost;
+        for (int z = 0; z < d.BH(); ++z) {
+          const int t = free_at.top() + len;
+          free_at.pop();
+          free_at.push(t);
+          end = std::max(end, t);
+        }
+      }
+    return end;
+  };
+  int best = finish(d.NB);
+  for (int L = d.NB - 1; L >= 2; --L) {
+    const int f = finish(L);
+    if (f < best) {
+      best = f;
       sp.L = L;
-      sp.items_per_head = iph;
-      return sp;
+      sp.items_per_head = chunks_per_head(d.NB, L);
     }
   }
   return sp;
