@@ -39,7 +39,7 @@ L2_FLUSH_BYTES = 256 << 20
 CONFIG4 = (1, 16, 16383, 128)
 # DRAM bytes (read + write) per launch of each tensor-core kernel at configuration 2 on one GPU, from an ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum); reported as roofline.traffic for the dominant kernel.
-NCU_TRAFFIC_C2 = {"bwd_kv_tc": (54.38 + 3.12) * 1e6, "bwd_q_tc": (54.85 + 1.50) * 1e6, "fwd_tc": (39.42 + 0.03) * 1e6}
+NCU_TRAFFIC_C2 = {"bwd_kv_tc": (54.38 + 2.17) * 1e6, "bwd_q_tc": (54.85 + 1.57) * 1e6, "fwd_tc": (39.42 + 0.09) * 1e6}
 
 
 def parse(argv=None):
