@@ -375,13 +375,46 @@ def reference_cpu_inputs(n_heads, T, D, seed=0):
     return q, k, v, phi, psi, beta, do
 
 
+_REF_MODULE = []
+
+
+def reference_module():
+    """The unmodified reference module (its kernel.py, installed under baseline/_ref), or None when it is not there
+    or does not import. Loaded once."""
+    if not _REF_MODULE:
+        import importlib.util
+        path = os.path.join(ROOT, "baseline", "_ref", "kernel.py")
+        mod = None
+        if os.path.exists(path):
+            try:
+                spec = importlib.util.spec_from_file_location("fpa_reference_module", path)
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+            except Exception as exc:  # reported by the callers' "kind"
+                print(f"# reference module under baseline/_ref does not import: {exc}", file=sys.stderr)
+                mod = None
+        _REF_MODULE.append(mod)
+    return _REF_MODULE[0]
+
+
+def reference_cpu_kind():
+    """"reference" when the CPU leg runs the unmodified reference's own impl="reference" path, else "port" (this
+    repository's restatement of the same definition, reference.py)."""
+    return "reference" if reference_module() is not None else "port"
+
+
 def reference_cpu_step(inputs):
     """One forward + backward of the reference's CPU path (the dense PyTorch definition, impl="reference"; fp32
-    arithmetic for fp16 inputs) on the host; returns the elapsed seconds."""
-    from first_passage_attention_b200 import first_passage_attention
+    arithmetic for fp16 inputs) on the host; returns the elapsed seconds. Runs the unmodified reference module when
+    it is installed under baseline/_ref, else this repository's restatement of it."""
+    mod = reference_module()
+    if mod is not None:
+        fpa = mod.first_passage_attention
+    else:
+        from first_passage_attention_b200 import first_passage_attention as fpa
     leaves = [t.clone().requires_grad_() for t in inputs[:6]]
     t0 = time.perf_counter()
-    o = first_passage_attention(*leaves, impl="reference")
+    o = fpa(*leaves, impl="reference")
     o.backward(inputs[6])
     return time.perf_counter() - t0
 
@@ -411,16 +444,18 @@ def reference_arm(args, B, H, T, D, rank, world):
     times = [reference_cpu_step(inputs) for _ in range(steps)]
     sec = statistics.median(times)
     val = flops(1, heads, T, D, "fwd_bwd") / sec / 1e12
+    src = ("the unmodified reference kernel.py under baseline/_ref" if reference_cpu_kind() == "reference"
+           else "this repository's restatement of it")
     sample = (f"{heads} of the {B * H} heads of B{B} H{H} T{T} D{D} per step (heads are independent; full T), "
-              f"forward + backward of the dense PyTorch definition (impl='reference'), fp16 inputs computed in fp32, "
-              f"median of {steps} steps")
+              f"forward + backward of the dense PyTorch definition (impl='reference', {src}), fp16 inputs computed "
+              f"in fp32, median of {steps} steps")
     line = {"impl": "reference", "metric": metric_for(B, H, T, D), "value": val, "unit": "TFLOP/s",
             "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": 1e3 * sec, "higher_is_better": True,
             "scaling": args.scaling, "vs_baseline": None, "dtype": "f32 (fp16 inputs)", "data": "synthetic",
             "config": {"workload": f"{shape_label(B, H, T, D)} (B{B} H{H} T{T} D{D} fp16) fwd+bwd, sampled heads",
                        "B": B, "H": H, "T": T, "D": D, "heads_per_step": heads, "same_config": True},
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                             "kind": reference_cpu_kind(), "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -429,14 +464,10 @@ def triton_reference(inputs, flush):
     """The reference's own GPU path (its Triton kernels, impl="triton", from the unmodified reference module installed
     under baseline/_ref) timed with the reference benchmark's protocol (3 warm-up, median of 15, its bench.py:11-23,
     46-52) on the same inputs, when that module imports here; otherwise the reason it is unavailable."""
-    import importlib.util
-    path = os.path.join(ROOT, "baseline", "_ref", "kernel.py")
-    if not os.path.exists(path):
-        return {"unavailable": "the reference module is not installed under baseline/_ref"}
+    mod = reference_module()
+    if mod is None:
+        return {"unavailable": "the reference module is not installed (or does not import) under baseline/_ref"}
     try:
-        spec = importlib.util.spec_from_file_location("fpa_reference_module", path)
-        mod = importlib.util.module_from_spec(spec)
-        spec.loader.exec_module(mod)
         q, k, v, phi, psi, beta, do = inputs
         args = (q, k, v, phi, psi, beta)
 
@@ -760,10 +791,12 @@ def main(argv=None):
         torch.set_num_threads(cpu_threads())
         heads, _ = reference_cpu_heads(T, D, 15.0, B * H)
         sec = reference_cpu_step(reference_cpu_inputs(heads, T, D, seed=0))
+        src = ("the unmodified reference kernel.py under baseline/_ref" if reference_cpu_kind() == "reference"
+               else "this repository's restatement of it")
         cpu = {"value": flops(1, heads, T, D, "fwd_bwd") / sec / 1e12, "unit": "TFLOP/s",
-               "cores": torch.get_num_threads(), "kind": "port",
+               "cores": torch.get_num_threads(), "kind": reference_cpu_kind(),
                "sample": f"{heads} of the {B * H} heads at T={T} D={D} in one call, forward + backward of the dense "
-                         f"PyTorch definition (impl='reference'), fp16 inputs computed in fp32, {sec:.1f} s"}
+                         f"PyTorch definition (impl='reference', {src}), fp16 inputs computed in fp32, {sec:.1f} s"}
 
     if rank == 0:
         wl_ = f"B{Bs} H{Hs}" if args.scaling == "strong" else f"B{B} H{H}"
