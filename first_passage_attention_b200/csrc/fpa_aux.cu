@@ -65,10 +65,11 @@ KeyCols carve_keycols(char* base, const Dims& d) {
 // memory (kernel.py:84-100 computes the same per-tile statistics). It also clears the device status word of the
 // call's workspace (the first launch of every call), and, when `cols.a` is set, writes the per-key vectors of the
 // tensor-core forward. Positions >= T take phi = +inf (a2 = -inf) and do not enter any statistic.
-// QV: the tensor-core backward's instantiation, which also forms delta and the per-query pairs (its eight rows of O
-// and dO in flight per lane cost registers that the forward's instantiation does not spend).
+// QV: the tensor-core backward's instantiation, which also forms delta and the per-query pairs (its rows of O and
+// dO in flight cost registers that the forward's instantiation does not spend). Eight 128-thread blocks per SM: at
+// configuration 2 (768 blocks) the whole grid is resident at once.
 template <bool QV>
-__global__ void stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
+__global__ void __launch_bounds__(128, 8) stats_kernel(const float* __restrict__ phi, const float* __restrict__ psi, int BH, int T, int BT,
                              int NB, float il2, Stats st, KeyCols cols, int cols_scaled,
                              const float* __restrict__ beta, int H, Fact fact, int* status, QvIn qv, int* tile_cnt,
                              int ncnt) {
@@ -81,7 +82,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   if (tid < ncnt) tile_cnt[(size_t(z) * NB + j) * ncnt + tid] = 0;  // the split kernels' per-tile join counters
   const int t = j * BT + tid;
   const size_t base = (size_t(z) * NB + j) * BT;
-  // Every global load of the kernel is issued here, before any of them is used, so that one memory latency covers
+  // The global loads of the kernel are issued here, before any of them is used, so that few memory latencies cover
   // them all (the kernel is latency-bound at small sizes): phi, psi, lse and beta of this block's positions, and
   // for the tensor-core backward the rows of O and dO for delta_t = sum_d dO[t, d] O[t, d] (kernel.py:166-174).
   const bool need_psi = fact.kv4 != nullptr || cols.a != nullptr;
@@ -91,7 +92,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
   float delta = 0.f, nlse = -kInf;
   if (QV && t < T) nlse = -qv.lse[size_t(z) * T + t];
   // delta in float32, read coalesced: each warp covers its 32 rows with groups of G = D/8 lanes, one 16-byte load
-  // of O and of dO per lane per row (eight rows' loads in flight at once), a fixed shuffle tree over the group, and
+  // of O and of dO per lane per row (four rows' loads in flight at once), a fixed shuffle tree over the group, and
   // the row's owner thread picks the sum up from shared memory. Packed with -lse, PRE and prey at the end.
   __shared__ float sdelta[1024];
   if constexpr (QV) {
@@ -99,10 +100,10 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
     const int b = z / H, h = z % H;
     const __half* ob = qv.o + b * qv.so.b + h * qv.so.h + part * 8;
     const __half* db = qv.dout + b * qv.sdo.b + h * qv.sdo.h + part * 8;
-    for (int it0 = 0; it0 < G; it0 += 8) {
-      uint4 xo[8], xd[8];
+    for (int it0 = 0; it0 < G; it0 += 4) {
+      uint4 xo[4], xd[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         const int rr = w * 32 + (it0 + q) * rpi + sub, tt = j * BT + rr;
         xo[q] = make_uint4(0u, 0u, 0u, 0u);
         xd[q] = make_uint4(0u, 0u, 0u, 0u);
@@ -112,7 +113,7 @@ __global__ void stats_kernel(const float* __restrict__ phi, const float* __restr
         }
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         if (it0 + q >= G) break;
         const __half2* xh = reinterpret_cast<const __half2*>(&xo[q]);
         const __half2* yh = reinterpret_cast<const __half2*>(&xd[q]);
