@@ -5,6 +5,7 @@ the CUDA path either runs the native kernels or fails with the reason.
 """
 import ctypes
 import os
+import struct
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -64,6 +65,28 @@ class FpaFieldArgs(ctypes.Structure):
                 ("dphi", ctypes.c_void_p), ("dpsi", ctypes.c_void_p),
                 ("dproj", ctypes.c_void_p), ("dproj_stride", ctypes.c_int64 * 3)]
 
+
+def _packer(cls):
+    """A struct.Struct with the byte layout of the ctypes Structure `cls` (the compiler's padding included), so that
+    one pack_into call fills an argument block: much cheaper per call than the keyword constructor."""
+    codes = {ctypes.c_int32: "i", ctypes.c_float: "f", ctypes.c_void_p: "Q", ctypes.c_size_t: "Q"}
+    fmt, pos = "<", 0
+    for name, ct in cls._fields_:
+        f = getattr(cls, name)
+        if f.offset > pos:
+            fmt += f"{f.offset - pos}x"
+        fmt += codes.get(ct) or f"{ct._length_}q"
+        pos = f.offset + f.size
+    if ctypes.sizeof(cls) > pos:
+        fmt += f"{ctypes.sizeof(cls) - pos}x"
+    packer = struct.Struct(fmt)
+    assert packer.size == ctypes.sizeof(cls), (cls.__name__, packer.size, ctypes.sizeof(cls))
+    return packer
+
+
+# Field order of the packers = the order of _fields_ (pointers as integers, each stride array as four integers).
+FWD_PACKER = _packer(FpaFwdArgs)
+BWD_PACKER = _packer(FpaBwdArgs)
 
 _lock = threading.Lock()
 _lib = None

@@ -1094,6 +1094,19 @@ int split_env() {
 
 bool tc_supports(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
+namespace {
+
+// Plans already made, by (NB, heads, SM slots): the list-schedule model below costs the host far more than a launch,
+// and a call asks for its plan several times (workspace size, join counters, launch).
+struct PlanEntry {
+  int NB, BH, slots;
+  FwdSplit sp;
+};
+std::mutex g_plan_mu;
+std::vector<PlanEntry> g_plans;
+
+}  // namespace
+
 FwdSplit tc_fwd_split_plan(const Dims& d) {
   FwdSplit sp;
   const int forced = split_env();
@@ -1111,6 +1124,11 @@ FwdSplit tc_fwd_split_plan(const Dims& d) {
   // sweeps on B200 at 6 and 12 heads of T = 2048); ties keep the longer chunks (fewer partial outputs) or no split.
   constexpr int kChunkCost = 2;
   const int slots = 2 * sm_count();
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mu);
+    for (const PlanEntry& e : g_plans)
+      if (e.NB == d.NB && e.BH == d.BH() && e.slots == slots) return e.sp;
+  }
   auto finish = [&](int L) {  // L = NB: the unsplit grid
     std::priority_queue<int, std::vector<int>, std::greater<int>> free_at;
     for (int q = 0; q < slots; ++q) free_at.push(0);
@@ -1136,6 +1154,9 @@ FwdSplit tc_fwd_split_plan(const Dims& d) {
       sp.items_per_head = chunks_per_head(d.NB, L);
     }
   }
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  if (g_plans.size() >= 256) g_plans.clear();  // bounded: shapes seldom vary that much
+  g_plans.push_back(PlanEntry{d.NB, d.BH(), slots, sp});
   return sp;
 }
 

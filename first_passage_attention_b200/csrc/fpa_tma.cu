@@ -72,7 +72,37 @@ bool tma_layout_ok(const void* p, const int64_t st[4]) {
   return true;
 }
 
+namespace {
+
+// The last tensor maps made, keyed by everything the encoding depends on (a map is a pure function of its base,
+// sizes and strides): a training loop passes the same buffers call after call, and each encoding costs the host
+// about as much as a kernel launch.
+struct MapKey {
+  const void* base;
+  int64_t s0, s1, s2;
+  int B, H, T, D;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && s0 == o.s0 && s1 == o.s1 && s2 == o.s2 && B == o.B && H == o.H && T == o.T && D == o.D;
+  }
+};
+constexpr int kMapCache = 32;
+std::mutex g_map_mu;
+MapKey g_map_key[kMapCache];
+CUtensorMap g_map_val[kMapCache];
+int g_map_n = 0, g_map_next = 0;
+
+}  // namespace
+
 bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int T, int D) {
+  const MapKey key{base, st[0], st[1], st[2], B, H, T, D};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    for (int i = 0; i < g_map_n; ++i)
+      if (g_map_key[i] == key) {
+        *map = g_map_val[i];
+        return true;
+      }
+  }
   auto fn = encode_fn();
   if (!fn) return false;
   const int boxc = D >= 64 ? 64 : D;
@@ -86,7 +116,13 @@ bool make_tile_map(CUtensorMap* map, const void* base, const int64_t st[4], int 
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  g_map_key[g_map_next] = key;
+  g_map_val[g_map_next] = *map;
+  g_map_next = (g_map_next + 1) % kMapCache;
+  if (g_map_n < kMapCache) ++g_map_n;
+  return true;
 }
 
 }  // namespace fpa

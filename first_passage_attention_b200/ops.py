@@ -6,6 +6,7 @@ for its GPU path) runs the native sm_100a kernels of libfpa_b200 through its C A
 the dense PyTorch definition. ``impl=None`` picks the CUDA kernels for CUDA tensors and the definition otherwise
 (kernel.py:463-464). There is no silent fallback: a CUDA request that the library cannot serve raises.
 """
+import contextlib
 import ctypes
 import math
 import os
@@ -29,16 +30,21 @@ def _path_from_env():
     return {"auto": _lib.PATH_AUTO, "simt": _lib.PATH_SIMT, "tensor": _lib.PATH_TENSOR}[p]
 
 
-def _strides(t):
-    return (ctypes.c_int64 * 4)(*t.stride())
-
-
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
 def _stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+_NO_SWITCH = contextlib.nullcontext()
+
+
+def _on_device(device):
+    """Make `device` the current CUDA device for the library call (the context manager costs a few microseconds,
+    so it is skipped when the device is current already)."""
+    return _NO_SWITCH if device.index == torch.cuda.current_device() else torch.cuda.device(device)
 
 
 def _tma_ready(t):
@@ -52,10 +58,12 @@ def _tma_ready(t):
 
 
 def _prep_qkv(x, path):
-    # The FFMA kernels take any strides; the tensor-core kernels need a TMA-describable layout.
-    if path != _lib.PATH_SIMT and x.dtype == torch.float16 and not _tma_ready(x):
-        return x.contiguous()
-    return x
+    # The FFMA kernels take any strides; the tensor-core kernels need a TMA-describable layout. A contiguous tensor
+    # with a 16-byte aligned base is one (D is a power of two >= 16), which saves the stride checks on the common path.
+    if path == _lib.PATH_SIMT or x.dtype != torch.float16 or (
+            x.is_contiguous() and x.data_ptr() % 16 == 0 and 0 not in x.stride()):
+        return x
+    return x if _tma_ready(x) else x.contiguous()
 
 
 class LaunchStats:
@@ -89,11 +97,11 @@ def fpa_forward(q, k, v, phi, psi, beta, tau, path=None):
     if nbytes == 0:
         _lib.check(_lib.ERR_UNSUPPORTED if path == _lib.PATH_TENSOR else _lib.ERR_INVALID)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-    a = _lib.FpaFwdArgs(dtype=dt, path=path, B=B, H=H, T=T, D=D, tau=float(tau),
-                        q=_ptr(q), q_stride=_strides(q), k=_ptr(k), k_stride=_strides(k),
-                        v=_ptr(v), v_stride=_strides(v), phi=_ptr(phi), psi=_ptr(psi), beta=_ptr(beta),
-                        o=_ptr(o), o_stride=_strides(o), lse=_ptr(lse),
-                        workspace=_ptr(ws), workspace_bytes=nbytes)
+    a = _lib.FpaFwdArgs()  # filled in one pack_into, in the field order of FpaFwdArgs
+    _lib.FWD_PACKER.pack_into(a, 0, dt, path, B, H, T, D, float(tau),
+                              q.data_ptr(), *q.stride(), k.data_ptr(), *k.stride(), v.data_ptr(), *v.stride(),
+                              phi.data_ptr(), psi.data_ptr(), beta.data_ptr(), o.data_ptr(), *o.stride(),
+                              lse.data_ptr(), ws.data_ptr(), nbytes, 0, 0)
     _lib.check(lib.fpa_fwd(ctypes.byref(a), _stream(q.device)))
     LaunchStats.fwd_calls += 1
     LaunchStats.kernels += a.kernels_launched
@@ -121,14 +129,13 @@ def fpa_backward(q, k, v, o, lse, phi, psi, beta, do, tau, path=None):
     if nbytes == 0:
         _lib.check(_lib.ERR_UNSUPPORTED if path == _lib.PATH_TENSOR else _lib.ERR_INVALID)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-    a = _lib.FpaBwdArgs(dtype=dt, path=path, B=B, H=H, T=T, D=D, tau=float(tau),
-                        q=_ptr(q), q_stride=_strides(q), k=_ptr(k), k_stride=_strides(k),
-                        v=_ptr(v), v_stride=_strides(v), o=_ptr(o), o_stride=_strides(o),
-                        dout=_ptr(do), dout_stride=_strides(do), lse=_ptr(lse),
-                        phi=_ptr(phi), psi=_ptr(psi), beta=_ptr(beta),
-                        dq=_ptr(dq), dq_stride=_strides(dq), dk=_ptr(dk), dk_stride=_strides(dk),
-                        dv=_ptr(dv), dv_stride=_strides(dv), dphi=_ptr(dphi), dpsi=_ptr(dpsi), dbeta=_ptr(dbeta),
-                        workspace=_ptr(ws), workspace_bytes=nbytes)
+    a = _lib.FpaBwdArgs()  # filled in one pack_into, in the field order of FpaBwdArgs
+    _lib.BWD_PACKER.pack_into(a, 0, dt, path, B, H, T, D, float(tau),
+                              q.data_ptr(), *q.stride(), k.data_ptr(), *k.stride(), v.data_ptr(), *v.stride(),
+                              o.data_ptr(), *o.stride(), do.data_ptr(), *do.stride(), lse.data_ptr(),
+                              phi.data_ptr(), psi.data_ptr(), beta.data_ptr(), dq.data_ptr(), *dq.stride(),
+                              dk.data_ptr(), *dk.stride(), dv.data_ptr(), *dv.stride(), dphi.data_ptr(),
+                              dpsi.data_ptr(), dbeta.data_ptr(), ws.data_ptr(), nbytes, 0, 0)
     _lib.check(lib.fpa_bwd(ctypes.byref(a), _stream(q.device)))
     LaunchStats.bwd_calls += 1
     LaunchStats.kernels += a.kernels_launched
@@ -145,7 +152,7 @@ class _FirstPassageAttention(torch.autograd.Function):
         phif = phi.float().contiguous()
         psif = psi.float().contiguous()
         betaf = beta.float().contiguous()
-        with torch.cuda.device(q.device):
+        with _on_device(q.device):
             o, lse = fpa_forward(q, k, v, phif, psif, betaf, tau, path)
         ctx.save_for_backward(q, k, v, o, lse, phif, psif, betaf)
         ctx.tau, ctx.path = tau, path
@@ -154,7 +161,7 @@ class _FirstPassageAttention(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, lse, phif, psif, betaf = ctx.saved_tensors
-        with torch.cuda.device(q.device):
+        with _on_device(q.device):
             dq, dk, dv, dphi, dpsi, dbeta = fpa_backward(q, k, v, o, lse, phif, psif, betaf, do.to(q.dtype),
                                                          ctx.tau, ctx.path)
         return dq, dk, dv, dphi, dpsi, dbeta, None, None
