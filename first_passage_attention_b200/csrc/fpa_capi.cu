@@ -146,7 +146,7 @@ int fpa_fwd(FpaFwdArgs* a, void* stream) {
     if (rc) return rc;
   } else {
     fpa::prof_mark(s, "fwd_simt");
-    e = fpa::simt_fwd(*a, d, st, s);
+    e = fpa::simt_fwd_tiled(*a, d, st, s);
     if (e != cudaSuccess) return cuda_fail(e, "forward kernel");
     a->kernels_launched += 1;
   }

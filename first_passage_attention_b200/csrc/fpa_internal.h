@@ -105,7 +105,8 @@ cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, floa
 
 // fpa_simt.cu (FFMA kernels, tiles of 64 positions, any supported D, fp16 or fp32 inputs)
 constexpr int kSimtBT = 64;
-cudaError_t simt_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s);
+// fpa_simt_fwd.cu: the register-tiled FFMA forward (tiles of 64 positions, any supported D, fp16 or fp32 inputs).
+cudaError_t simt_fwd_tiled(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s);
 cudaError_t simt_bwd_kv(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
 cudaError_t simt_bwd_q(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
 

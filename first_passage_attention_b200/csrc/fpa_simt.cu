@@ -1,10 +1,11 @@
-// FFMA (SIMT) kernels of the FPA operator: the fp32 path, and the path for any head dimension the tensor-core
-// kernels do not cover. Tiles of 64 positions; a group of TPR consecutive threads owns one query row (forward,
-// q-pass) or one key (kv-pass) and splits the head dimension between its lanes.
+// FFMA (SIMT) backward kernels of the FPA operator: the fp32 path, and the path for any head dimension the
+// tensor-core kernels do not cover (the forward of that path is fpa_simt_fwd.cu). Tiles of 64 positions; a group of
+// TPR consecutive threads owns one query row (q-pass) or one key (kv-pass) and splits the head dimension between
+// its lanes.
 //
-// The math follows the reference's tiled decomposition (kernel.py:104-162 forward, 178-265 kv-pass,
-// 287-340 q-pass): for query t in tile i and key s in tile j < i the range (s, t] splits into (s, end of j],
-// the tiles strictly between, and [start of i, t], so
+// The math follows the reference's tiled decomposition (kernel.py:178-265 kv-pass, 287-340 q-pass): for query t in
+// tile i and key s in tile j < i the range (s, t] splits into (s, end of j], the tiles strictly between, and
+// [start of i, t], so
 //     min_{s<u<=t} phi_u = min(SUF_s, mid_ij, PRE_t),   Z_{s,t} = 2^{SUFL_s} + 2^{MIDL_ij} + 2^{PREL_t}.
 // Inside the diagonal tile the range minimum is carried as a running minimum along the row.
 #include "fpa_internal.h"
@@ -32,124 +33,6 @@ __device__ __forceinline__ void load_tile(float* dst, const TIn* base, Str4 st, 
   for (int e = threadIdx.x; e < BT * D; e += THREADS) {
     int r = e / D, c = e % D, t = j * BT + r;
     dst[e] = t < T ? to_f32(base[int64_t(t) * st.t + int64_t(c) * st.d]) : 0.f;
-  }
-}
-
-// ------------------------------------------------------------------------------------------------ forward ----
-template <typename TIn, int D>
-__global__ void __launch_bounds__(SimtShape<D>::THREADS)
-simt_fwd_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k, Str4 sk, const TIn* __restrict__ v,
-                Str4 sv, const float* __restrict__ phi, const float* __restrict__ psi,
-                const float* __restrict__ beta, Stats st, TIn* __restrict__ o, Str4 so, float* __restrict__ lse,
-                int H, int T, int NB, float scale2) {
-  using S = SimtShape<D>;
-  constexpr int BT = S::BT, TPR = S::TPR, CPT = S::CPT, CH = 8;
-  extern __shared__ float smem[];
-  float* Ks = smem;
-  float* Vs = Ks + BT * D;
-  float* psis = Vs + BT * D;
-  float* phis = psis + BT;
-  float* sufs = phis + BT;
-
-  const int i = NB - 1 - blockIdx.x;  // longest query tiles first (kernel.py:108)
-  const int z = blockIdx.z * gridDim.y + blockIdx.y, b = z / H, h = z % H;  // grid (NB, H, B)
-  const int tl = threadIdx.x / TPR, sub = threadIdx.x % TPR, c0 = sub * CPT;
-  const int t = i * BT + tl;
-  const size_t TP = size_t(NB) * BT;
-  const float betal = beta[h] * kLog2e;
-
-  float qr[CPT];
-  load_row(qr, q + b * sq.b + h * sq.h + int64_t(t < T ? t : T - 1) * sq.t, sq.d, c0, CPT, true);
-#pragma unroll
-  for (int c = 0; c < CPT; ++c) qr[c] *= scale2;
-  const float pre_t = st.pre[size_t(z) * TP + t];
-
-  float m = -kInf, l = 0.f, acc[CPT];
-#pragma unroll
-  for (int c = 0; c < CPT; ++c) acc[c] = 0.f;
-
-  auto update = [&](const float* sc, int s0) {
-    float mx = m;
-#pragma unroll
-    for (int e = 0; e < CH; ++e) mx = fmaxf(mx, sc[e]);
-    if (mx == -kInf) return;
-    float corr = ex2(m - mx);
-    l *= corr;
-#pragma unroll
-    for (int c = 0; c < CPT; ++c) acc[c] *= corr;
-#pragma unroll
-    for (int e = 0; e < CH; ++e) {
-      float p = ex2(sc[e] - mx);
-      l += p;
-      const float* vr = Vs + (s0 + e) * D + c0;
-#pragma unroll
-      for (int c = 0; c < CPT; ++c) acc[c] = fmaf(p, vr[c], acc[c]);
-    }
-    m = mx;
-  };
-  auto tile_in = [&](int j) {
-    const size_t zb = size_t(z) * T;
-    load_tile<TIn, D, S::THREADS>(Ks, k + b * sk.b + h * sk.h, sk, j, T);
-    load_tile<TIn, D, S::THREADS>(Vs, v + b * sv.b + h * sv.h, sv, j, T);
-    for (int r = threadIdx.x; r < BT; r += S::THREADS) {
-      int s = j * BT + r;
-      psis[r] = s < T ? psi[zb + s] : 0.f;
-      phis[r] = s < T ? phi[zb + s] : kInf;
-      sufs[r] = st.suf[size_t(z) * TP + s];
-    }
-  };
-
-  // Diagonal tile: keys in descending order carry r = min_{s<u<=t} phi_u (kernel.py:130-132).
-  tile_in(i);
-  __syncthreads();
-  float r = kInf;
-  for (int s0 = BT - CH; s0 >= 0; s0 -= CH) {
-    float sc[CH];
-#pragma unroll
-    for (int e = CH - 1; e >= 0; --e) {
-      const int sl = s0 + e;
-      const float* kr = Ks + sl * D + c0;
-      float dot = 0.f;
-#pragma unroll
-      for (int c = 0; c < CPT; ++c) dot = fmaf(qr[c], kr[c], dot);
-      dot = group_sum<TPR>(dot);
-      const bool ok = (sl <= tl) && (i * BT + sl < T);
-      const float x = r - psis[sl];
-      sc[e] = ok ? dot + betal * fminf(x, 0.f) : -kInf;
-      if (sl <= tl) r = fminf(r, phis[sl]);
-    }
-    update(sc, s0);
-  }
-  // Earlier key tiles, walking back from the diagonal with mid = min phi over the tiles passed (kernel.py:143-159).
-  float mid = kInf;
-  for (int j = i - 1; j >= 0; --j) {
-    __syncthreads();
-    tile_in(j);
-    __syncthreads();
-    const float cap = fminf(mid, pre_t);
-    for (int s0 = 0; s0 < BT; s0 += CH) {
-      float sc[CH];
-#pragma unroll
-      for (int e = 0; e < CH; ++e) {
-        const int sl = s0 + e;
-        const float* kr = Ks + sl * D + c0;
-        float dot = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) dot = fmaf(qr[c], kr[c], dot);
-        dot = group_sum<TPR>(dot);
-        const float x = fminf(sufs[sl], cap) - psis[sl];
-        sc[e] = dot + betal * fminf(x, 0.f);
-      }
-      update(sc, s0);
-    }
-    mid = fminf(mid, st.bmin[size_t(z) * NB + j]);
-  }
-  if (t < T) {
-    const float inv = 1.f / l;
-    TIn* orow = o + b * so.b + h * so.h + int64_t(t) * so.t;
-#pragma unroll
-    for (int c = 0; c < CPT; ++c) orow[int64_t(c0 + c) * so.d] = from_f32<TIn>(acc[c] * inv);
-    if (sub == 0) lse[size_t(z) * T + t] = m + lg2(l);
   }
 }
 
@@ -481,8 +364,6 @@ simt_bwd_q_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict__ k,
 
 // ------------------------------------------------------------------------------------------------ launchers --
 template <int D>
-static size_t fwd_smem() { return (2 * size_t(kSimtBT) * D + 3 * kSimtBT) * sizeof(float); }
-template <int D>
 static size_t kv_smem() {
   return (2 * size_t(kSimtBT) * D + 5 * kSimtBT + 2 * size_t(kSimtBT) * (kSimtBT + 1) + 32) * sizeof(float);
 }
@@ -493,19 +374,6 @@ template <typename F>
 static cudaError_t allow_smem(F* fn, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   return allow_dynamic_smem(reinterpret_cast<const void*>(fn), int(bytes));
-}
-
-template <typename TIn, int D>
-static cudaError_t simt_fwd_t(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s) {
-  auto fn = simt_fwd_kernel<TIn, D>;
-  size_t smem = fwd_smem<D>();
-  cudaError_t e = allow_smem(fn, smem);
-  if (e != cudaSuccess) return e;
-  fn<<<dim3(d.NB, d.H, d.B), SimtShape<D>::THREADS, smem, s>>>(
-      (const TIn*)a.q, str4(a.q_stride), (const TIn*)a.k, str4(a.k_stride), (const TIn*)a.v, str4(a.v_stride),
-      a.phi, a.psi, a.beta, st, (TIn*)a.o, str4(a.o_stride), a.lse, d.H, d.T, d.NB,
-      float(1.0 / sqrt(double(D))) * kLog2e);
-  return cudaGetLastError();
 }
 
 template <typename TIn, int D>
@@ -547,14 +415,6 @@ static cudaError_t simt_q_t(const FpaBwdArgs& a, const Dims& d, const Stats& st,
   }
 
 template <int D>
-static cudaError_t fwd_f16(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s) {
-  return simt_fwd_t<__half, D>(a, d, st, s);
-}
-template <int D>
-static cudaError_t fwd_f32(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s) {
-  return simt_fwd_t<float, D>(a, d, st, s);
-}
-template <int D>
 static cudaError_t kv_f16(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc,
                           cudaStream_t s) {
   return simt_kv_t<__half, D>(a, d, st, sc, s);
@@ -571,13 +431,6 @@ static cudaError_t q_f16(const FpaBwdArgs& a, const Dims& d, const Stats& st, co
 template <int D>
 static cudaError_t q_f32(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s) {
   return simt_q_t<float, D>(a, d, st, sc, s);
-}
-
-cudaError_t simt_fwd(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s) {
-  if (a.dtype == FPA_DTYPE_F16) {
-    FPA_DISPATCH_D(d.D, fwd_f16, a, d, st, s);
-  }
-  FPA_DISPATCH_D(d.D, fwd_f32, a, d, st, s);
 }
 
 cudaError_t simt_bwd_kv(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s) {
