@@ -768,10 +768,11 @@ def main(argv=None):
 
     # Algorithmic FLOPs per launch (causal FlashAttention convention, unit G = B*H*T^2*D): the forward kernel does
     # the forward's 2G; the kv-pass does 4 of the backward's 5 G-sized products (S^T, dP^T, dV, dK); the q-pass does
-    # dQ (its S and dP are the recomputation the convention does not count).
+    # dQ (its S and dP are the recomputation the convention does not count); the FFMA backward for D <= 128 runs
+    # both passes in one launch (5G).
     G = float(Bs) * Hs * T * T * D
     algo = {"fwd_tc": 2 * G, "fwd_simt": 2 * G, "bwd_kv_tc": 4 * G, "bwd_kv_simt": 4 * G, "bwd_q_tc": G,
-            "bwd_q_simt": G}
+            "bwd_q_simt": G, "bwd_simt": 5 * G}
     per_launch_us = {k_: 1e3 * ms / n for k_, (n, ms) in kernels.items()}
     dom = max(kernels, key=lambda k_: kernels[k_][1]) if kernels else None
     if dom in algo:

@@ -1,7 +1,7 @@
-// FFMA (SIMT) backward kernels of the FPA operator: the fp32 path, and the path for any head dimension the
-// tensor-core kernels do not cover (the forward of that path is fpa_simt_fwd.cu). Tiles of 64 positions; a group of
-// TPR consecutive threads owns one query row (q-pass) or one key (kv-pass) and splits the head dimension between
-// its lanes.
+// Row-per-thread-group FFMA backward kernels of the FPA operator, for D = 256, where the register-tiled backward
+// (fpa_simt_bwd.cu) does not fit its four transposed tiles in shared memory: the fp32 path and fp16 at D = 256 (the
+// forward of that path is fpa_simt_fwd.cu). Tiles of 64 positions; a group of TPR consecutive threads owns one query
+// row (q-pass) or one key (kv-pass) and splits the head dimension between its lanes.
 //
 // The math follows the reference's tiled decomposition (kernel.py:178-265 kv-pass, 287-340 q-pass): for query t in
 // tile i and key s in tile j < i the range (s, t] splits into (s, end of j], the tiles strictly between, and
@@ -404,16 +404,6 @@ static cudaError_t simt_q_t(const FpaBwdArgs& a, const Dims& d, const Stats& st,
   return cudaGetLastError();
 }
 
-#define FPA_DISPATCH_D(D_, FN, ...)                       \
-  switch (D_) {                                           \
-    case 16: return FN<16>(__VA_ARGS__);                  \
-    case 32: return FN<32>(__VA_ARGS__);                  \
-    case 64: return FN<64>(__VA_ARGS__);                  \
-    case 128: return FN<128>(__VA_ARGS__);                \
-    case 256: return FN<256>(__VA_ARGS__);                \
-    default: return cudaErrorInvalidValue;                \
-  }
-
 template <int D>
 static cudaError_t kv_f16(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc,
                           cudaStream_t s) {
@@ -434,17 +424,13 @@ static cudaError_t q_f32(const FpaBwdArgs& a, const Dims& d, const Stats& st, co
 }
 
 cudaError_t simt_bwd_kv(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s) {
-  if (a.dtype == FPA_DTYPE_F16) {
-    FPA_DISPATCH_D(d.D, kv_f16, a, d, st, sc, s);
-  }
-  FPA_DISPATCH_D(d.D, kv_f32, a, d, st, sc, s);
+  if (d.D != 256) return cudaErrorInvalidValue;
+  return a.dtype == FPA_DTYPE_F16 ? kv_f16<256>(a, d, st, sc, s) : kv_f32<256>(a, d, st, sc, s);
 }
 
 cudaError_t simt_bwd_q(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s) {
-  if (a.dtype == FPA_DTYPE_F16) {
-    FPA_DISPATCH_D(d.D, q_f16, a, d, st, sc, s);
-  }
-  FPA_DISPATCH_D(d.D, q_f32, a, d, st, sc, s);
+  if (d.D != 256) return cudaErrorInvalidValue;
+  return a.dtype == FPA_DTYPE_F16 ? q_f16<256>(a, d, st, sc, s) : q_f32<256>(a, d, st, sc, s);
 }
 
 }  // namespace fpa
