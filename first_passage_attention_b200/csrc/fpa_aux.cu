@@ -39,7 +39,7 @@ BwdScratch carve_bwd(char* base, const Dims& d, int tb_parts) {
   size_t bh = size_t(d.BH());
   BwdScratch s;
   s.tb_parts = tb_parts;
-  s.tb_sum = tb_parts == 2 ? 1 : tb_parts;  // the FFMA kv-pass writes one total per pair into a 2-float slot
+  s.tb_sum = tb_parts;
   s.delta = take(base, bh * d.TP);
   s.w = take(base, bh * d.TP);
   s.dphi2 = take(base, bh * d.TP);

@@ -52,13 +52,9 @@ int pick_path(int requested, int dtype, int D) {
 
 int tile_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcBT : fpa::kSimtBT; }
 
-// Floats per tile pair of the TB array: the tensor-core and the register-tiled FFMA kv-passes write 8 per-warp
-// partial sums, the row-per-thread-group FFMA one (D = 256) a single total into a slot of 2 (the O(NB^2) part-3
-// passes of the dphi combination reuse two floats per pair).
-int tb_parts_of(int path, int D) {
-  if (path == FPA_PATH_TENSOR) return fpa::kTcTbParts;
-  return fpa::simt_bwd_tiled_supports(D) ? fpa::kSimtTbParts : 2;
-}
+// Floats per tile pair of the TB array: both kv-passes write 8 per-warp partial sums (the O(NB^2) part-3 passes of
+// the dphi combination reuse two of them).
+int tb_parts_of(int path) { return path == FPA_PATH_TENSOR ? fpa::kTcTbParts : fpa::kSimtTbParts; }
 
 // The backward follows the same choice as the forward: tensor cores for fp16 with a supported D, FFMA otherwise.
 int bwd_path(int requested, int dtype, int D) { return pick_path(requested, dtype, D); }
@@ -78,7 +74,7 @@ size_t fwd_ws(int dtype, int B, int H, int T, int D, int path) {
 
 size_t bwd_ws(int dtype, int B, int H, int T, int D, int path) {
   fpa::Dims d = fpa::make_dims(B, H, T, D, tile_of(path));
-  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, tb_parts_of(path, D)) +
+  return fpa::kStatusBytes + fpa::stats_bytes(d) + fpa::bwd_scratch_bytes(d, tb_parts_of(path)) +
          (path == FPA_PATH_TENSOR ? fpa::tc_bwd_extra_bytes(d) : 0);
 }
 
@@ -176,7 +172,7 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
   int* status = static_cast<int*>(a->workspace);
   char* ws = static_cast<char*>(a->workspace) + fpa::kStatusBytes;
   fpa::Stats st = fpa::carve_stats(ws, d);
-  fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d, tb_parts_of(path, a->D));
+  fpa::BwdScratch sc = fpa::carve_bwd(ws + fpa::stats_bytes(d), d, tb_parts_of(path));
   int n = 0;
   cudaError_t e;
   if (path == FPA_PATH_TENSOR) {
@@ -199,21 +195,10 @@ int fpa_bwd(FpaBwdArgs* a, void* stream) {
                           nullptr, nullptr, s);
     if (e != cudaSuccess) return cuda_fail(e, "delta kernel");
     ++n;
-    if (fpa::simt_bwd_tiled_supports(a->D)) {
-      fpa::prof_mark(s, "bwd_simt");
-      e = fpa::simt_bwd_tiled(*a, d, st, sc, s);
-      if (e != cudaSuccess) return cuda_fail(e, "backward kernel");
-      ++n;
-    } else {
-      fpa::prof_mark(s, "bwd_kv_simt");
-      e = fpa::simt_bwd_kv(*a, d, st, sc, s);
-      if (e != cudaSuccess) return cuda_fail(e, "kv-pass kernel");
-      ++n;
-      fpa::prof_mark(s, "bwd_q_simt");
-      e = fpa::simt_bwd_q(*a, d, st, sc, s);
-      if (e != cudaSuccess) return cuda_fail(e, "q-pass kernel");
-      ++n;
-    }
+    fpa::prof_mark(s, "bwd_simt");
+    e = fpa::simt_bwd_tiled(*a, d, st, sc, s);
+    if (e != cudaSuccess) return cuda_fail(e, "backward kernel");
+    ++n;
   }
   fpa::prof_mark(s, "dphi");
   int nd = 0;

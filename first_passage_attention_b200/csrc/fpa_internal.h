@@ -103,17 +103,13 @@ cudaError_t launch_diag_dphi(const float* phi, const float* gd, const Dims& d, f
 cudaError_t launch_dphi(const float* phi, const float* beta, const Dims& d, float tau, const Stats& st,
                         const BwdScratch& sc, float* dphi, float* dbeta, cudaStream_t s, int* launched);
 
-// fpa_simt.cu (FFMA kernels, tiles of 64 positions, any supported D, fp16 or fp32 inputs)
+// The FFMA path (fp32, fp16 with D = 256, or path=SIMT): tiles of 64 positions, any supported D, fp16 or fp32.
 constexpr int kSimtBT = 64;
-// fpa_simt_fwd.cu: the register-tiled FFMA forward (tiles of 64 positions, any supported D, fp16 or fp32 inputs).
+// fpa_simt_fwd.cu: the register-tiled FFMA forward.
 cudaError_t simt_fwd_tiled(const FpaFwdArgs& a, const Dims& d, const Stats& st, cudaStream_t s);
-// fpa_simt_bwd.cu: the register-tiled FFMA backward (kv-pass and q-pass in one launch) for D <= 128; its kv-pass
-// writes kSimtTbParts per-warp partial sums per tile pair into the TB array.
+// fpa_simt_bwd.cu: the register-tiled FFMA backward (kv-pass and q-pass in one launch); its kv-pass writes
+// kSimtTbParts per-warp partial sums per tile pair into the TB array.
 constexpr int kSimtTbParts = 8;
-bool simt_bwd_tiled_supports(int D);
 cudaError_t simt_bwd_tiled(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
-// fpa_simt.cu: the row-per-thread-group FFMA backward passes (D = 256).
-cudaError_t simt_bwd_kv(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
-cudaError_t simt_bwd_q(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc, cudaStream_t s);
 
 }  // namespace fpa

@@ -1,16 +1,21 @@
-// Register-tiled FFMA backward of the FPA operator for D <= 128: the fp32 path, and fp16 wherever the FFMA path is
-// asked for. One launch runs both passes of the reference's backward (kernel.py:178-265 kv-pass, 287-340 q-pass) as
-// interleaved CTAs: even blockIdx.x is the kv-pass of key tile x / 2, odd blockIdx.x the q-pass of query tile
-// NB - 1 - x / 2, so both start with their longest tiles and their tails overlap.
+// Register-tiled FFMA backward of the FPA operator: the fp32 path, fp16 with D = 256 (which the tensor-core kernels
+// do not cover) and fp16 wherever the FFMA path is asked for. One launch runs both passes of the reference's backward
+// (kernel.py:178-265 kv-pass, 287-340 q-pass) as interleaved CTAs: even blockIdx.x are kv-pass CTAs of key tiles
+// 0, 1, ..., odd ones q-pass CTAs of query tiles NB - 1, NB - 2, ..., so both start with their longest tiles and
+// their tails overlap.
 //
 // Work split (256 threads as 16 x 16, tiles of 64 positions): thread (ty, tx) owns
 //   * of the score tiles (S^T, dP^T in the kv-pass, S, dP in the q-pass) the 4 x 4 block of rows 4 ty .. 4 ty + 3
 //     and columns 4 tx .. 4 tx + 3: an outer product per head-dimension index from the transposed tiles in shared
 //     memory (four 16-byte loads for 32 FMAs);
-//   * of the gradient accumulators (dK and dV of its four keys, or dQ of its four queries) the columns tx + 16 g,
-//     g < D / 16: per four positions, one 16-byte load of each score row and one of the transposed operand's row
-//     per column.
-// The field math is the one of the row-per-thread-group kernels: off the diagonal tile the bias uses
+//   * of the gradient accumulators (dK and dV of its four keys, or dQ of its four queries) the columns tx + 16 g:
+//     per four positions, one 16-byte load of each score row and one of the transposed operand's row per column.
+// The CTA's own tile pair (K, V in the kv-pass; Q, dO in the q-pass) stays in shared memory, transposed; the other
+// pair streams through it. For D <= 128 the streamed pair is one stage of all D columns. For D = 256 (four
+// transposed 64 x 256 fp32 tiles would need 278 KB) it streams in stages of 64 columns, and two CTAs share each tile
+// and pass: both compute the score tiles, each keeps the accumulators of one half of the columns (128 registers of
+// dK and dV per thread otherwise), and the first also writes the per-key or per-query results.
+// The field math is the one of the reference's tiled decomposition: off the diagonal tile the bias uses
 // min(SUF_s, mid, PRE_t) and the soft-min sums Z = 2^SUFL + 2^MIDL + 2^PREL; inside it the range minimum over (s, t]
 // comes from a table built once per CTA, and the kv-pass runs the in-tile soft-min recurrence (kernel.py:269-283)
 // on the g values it leaves in shared memory.
@@ -28,12 +33,19 @@ using tile::vec_ok;
 
 template <int D>
 struct BwdTile {
-  static constexpr int CPT = D / 16;  // accumulator columns per thread (tx + 16 g)
-  // kv-pass: Kt, Vt, Qt, Dt [D][kPitch]; Ps, Ds [kFT][kPitch]; per query lse, delta, PRE, PREL, phi; per key psi;
-  // eight per-warp partial sums.
-  static constexpr size_t KV_FLOATS = 4 * size_t(D) * kPitch + 2 * size_t(kFT) * kPitch + 6 * kFT + 8;
-  // q-pass: Qt, Dt, Kt, Vt [D][kPitch]; Ss [kFT][kPitch]; per key psi, phi, SUF, SUFL; per query r, c2, phi.
-  static constexpr size_t Q_FLOATS = 4 * size_t(D) * kPitch + size_t(kFT) * kPitch + 7 * kFT;
+  static constexpr int NH = D <= 128 ? 1 : 2;   // CTAs per tile and pass (column halves of the accumulators)
+  static constexpr int NC = D / NH;             // accumulator columns of a CTA
+  static constexpr int CPT = NC / 16;           // accumulator columns per thread (tx + 16 g)
+  static constexpr int DC = D <= 128 ? D : 64;  // columns of the streamed tile pair per shared-memory stage
+  static constexpr int NCH = D / DC;            // stages of the score contraction
+  // kv-pass: Kt, Vt [D][kPitch]; Qt, Dt [DC][kPitch]; Ps, Ds [kFT][kPitch]; per query lse, delta, PRE, PREL, phi;
+  // per key psi; eight per-warp partial sums.
+  static constexpr size_t KV_FLOATS =
+      2 * size_t(D) * kPitch + 2 * size_t(DC) * kPitch + 2 * size_t(kFT) * kPitch + 6 * kFT + 8;
+  // q-pass: Qt, Dt [D][kPitch]; Kt, Vt [DC][kPitch]; Ss [kFT][kPitch]; per key psi, phi, SUF, SUFL; per query r,
+  // c2, phi.
+  static constexpr size_t Q_FLOATS =
+      2 * size_t(D) * kPitch + 2 * size_t(DC) * kPitch + size_t(kFT) * kPitch + 7 * kFT;
   static constexpr size_t SMEM = (KV_FLOATS > Q_FLOATS ? KV_FLOATS : Q_FLOATS) * 4;
 };
 
@@ -57,17 +69,13 @@ __device__ __forceinline__ float row16_sum(float x) {
   return x;
 }
 
-// The 4 x 4 blocks A = X Y^T and B = U W^T over the head dimension, X, U rows 4 ty .., Y, W rows 4 tx .., all four
-// operands transposed ([D][kPitch]) in shared memory.
-template <int D>
+// Adds to the 4 x 4 blocks A = X Y^T and B = U W^T the contraction over DC head-dimension indices; X, U rows
+// 4 ty .., Y, W rows 4 tx .., all four operands transposed ([DC][kPitch]) in shared memory.
+template <int DC>
 __device__ __forceinline__ void score_blocks(float (&A)[4][4], float (&Bm)[4][4], const float* Xt, const float* Yt,
                                              const float* Ut, const float* Wt, int ty, int tx) {
-#pragma unroll
-  for (int a = 0; a < 4; ++a)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) A[a][c] = Bm[a][c] = 0.f;
 #pragma unroll 4
-  for (int d = 0; d < D; ++d) {
+  for (int d = 0; d < DC; ++d) {
     const float4 x = lds4(Xt + d * kPitch + ty * 4), y = lds4(Yt + d * kPitch + tx * 4);
     const float4 u = lds4(Ut + d * kPitch + ty * 4), w = lds4(Wt + d * kPitch + tx * 4);
     const float xv[4] = {x.x, x.y, x.z, x.w}, yv[4] = {y.x, y.y, y.z, y.w};
@@ -84,16 +92,18 @@ __device__ __forceinline__ void score_blocks(float (&A)[4][4], float (&Bm)[4][4]
 
 // ------------------------------------------------------------------------------------------------ kv-pass ----
 // Key tile j: dK, dV, dpsi, the dbeta partial, the soft-min sums W (u in the key's tile) and TB (u strictly between
-// the tiles, one partial per warp), and the in-tile soft-min gradient DPHI4 of the diagonal tile.
+// the tiles, one partial per warp), and the in-tile soft-min gradient DPHI4 of the diagonal tile; the columns
+// half * NC .. of dK and dV (the per-key results from half 0 only).
 template <typename TIn, int D, bool VEC>
 __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, const BwdScratch& sc, float* smem,
-                                        int j, int z) {
-  constexpr int CPT = BwdTile<D>::CPT;
+                                        int j, int z, int half) {
+  using BT = BwdTile<D>;
+  constexpr int CPT = BT::CPT, DC = BT::DC, NCH = BT::NCH;
   float* Kt = smem;
   float* Vt = Kt + D * kPitch;
-  float* Qt = Vt + D * kPitch;
-  float* Dt = Qt + D * kPitch;
-  float* Ps = Dt + D * kPitch;  // P^T [key][query]; the range-minimum table before, log2 Z of the recurrence after
+  float* Qt = Vt + D * kPitch;  // one stage of DC columns of the query tile's Q and dO
+  float* Dt = Qt + DC * kPitch;
+  float* Ps = Dt + DC * kPitch;  // P^T [key][query]; the range-minimum table before, log2 Z of the recurrence after
   float* Ds = Ps + kFT * kPitch;  // dS^T [key][query]; g and then the recurrence's contributions on the diagonal
   float* lses = Ds + kFT * kPitch;
   float* dels = lses + kFT;
@@ -135,35 +145,50 @@ __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, 
 #pragma unroll
     for (int g = 0; g < CPT; ++g) dka[a][g] = dva[a][g] = 0.f;
 
+  // Stages of Q and dO in the order (first + 1, ..., first): the score contraction ends on the stage holding the
+  // first DC of this CTA's accumulator columns, which the dK / dV update then starts from without a reload.
+  const int first = half * (NCH / BT::NH);
+  auto load_stage = [&](int i, int c) {
+    load_rows<TIn, DC, true, VEC>(Qt, q + int64_t(c) * DC * A.sq.d, A.sq, i, T, 1.f);
+    load_rows<TIn, DC, true, VEC>(Dt, dout + int64_t(c) * DC * A.sdo.d, A.sdo, i, T, 1.f);
+  };
+
   for (int i = j; i < NB; ++i) {
     const bool diag = i == j;
-    __syncthreads();  // the previous query tile's Qt, Dt, Ps and Ds are read
-    load_rows<TIn, D, true, VEC>(Qt, q, A.sq, i, T, 1.f);
-    load_rows<TIn, D, true, VEC>(Dt, dout, A.sdo, i, T, 1.f);
-    if (tid < kFT) {
-      const int t = i * kFT + tid;
-      const bool ok = t < T;
-      lses[tid] = ok ? A.lse[zt + t] : 0.f;
-      dels[tid] = ok ? sc.delta[zp + t] : 0.f;
-      pres[tid] = st.pre[zp + t];
-      prels[tid] = st.prel[zp + t];
-      phis[tid] = ok ? A.phi[zt + t] : kInf;
-    }
-    __syncthreads();
-    if (diag) {
-      // Range-minimum table of the diagonal tile: Ps[s][t] = min phi over (s, t] for t > s, one thread per key.
-      if (tid < kFT) {
-        float x = kInf;
-        float* row = Ps + tid * kPitch;
-        for (int t = tid + 1; t < kFT; ++t) {
-          x = fminf(x, phis[t]);
-          row[t] = x;
-        }
+    float sS[4][4], sP[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sS[a][c] = sP[a][c] = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (first + 1 + k) % NCH;
+      __syncthreads();  // the previous stage (and, at k = 0, the previous query tile's Ps and Ds) are read
+      load_stage(i, c);
+      if (k == 0 && tid < kFT) {
+        const int t = i * kFT + tid;
+        const bool ok = t < T;
+        lses[tid] = ok ? A.lse[zt + t] : 0.f;
+        dels[tid] = ok ? sc.delta[zp + t] : 0.f;
+        pres[tid] = st.pre[zp + t];
+        prels[tid] = st.prel[zp + t];
+        phis[tid] = ok ? A.phi[zt + t] : kInf;
       }
       __syncthreads();
+      if (k == 0 && diag) {
+        // Range-minimum table of the diagonal tile: Ps[s][t] = min phi over (s, t] for t > s, one thread per key.
+        if (tid < kFT) {
+          float x = kInf;
+          float* row = Ps + tid * kPitch;
+          for (int t = tid + 1; t < kFT; ++t) {
+            x = fminf(x, phis[t]);
+            row[t] = x;
+          }
+        }
+        __syncthreads();
+      }
+      score_blocks<DC>(sS, sP, Kt + c * DC * kPitch, Qt, Vt + c * DC * kPitch, Dt, ty, tx);
     }
-    float sS[4][4], sP[4][4];
-    score_blocks<D>(sS, sP, Kt, Qt, Vt, Dt, ty, tx);
 
     // Per-key constants of this query tile (off the diagonal): rs normalises the soft-min sums.
     const float cmid2 = mid < kInf ? -mid * il2 : -kInf;
@@ -217,27 +242,36 @@ __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, 
       *reinterpret_cast<float4*>(Ds + sl * kPitch + tx * 4) = make_float4(sP[a][0], sP[a][1], sP[a][2], sP[a][3]);
     }
     __syncthreads();
-    // dV += P^T dO and dK += dS^T Q over the tile's 64 queries.
-#pragma unroll 2
-    for (int t0 = 0; t0 < kFT; t0 += 4) {
-      float pr[4][4], dr[4][4];
+    // dV += P^T dO and dK += dS^T Q over the tile's 64 queries, one stage of DC columns at a time.
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        ld_vec<4>(pr[a], Ps + (ty * 4 + a) * kPitch + t0);
-        ld_vec<4>(dr[a], Ds + (ty * 4 + a) * kPitch + t0);
+    for (int cc = 0; cc < CPT / (DC / 16); ++cc) {
+      if (cc > 0) {
+        __syncthreads();
+        load_stage(i, first + cc);
+        __syncthreads();
       }
+#pragma unroll 2
+      for (int t0 = 0; t0 < kFT; t0 += 4) {
+        float pr[4][4], dr[4][4];
 #pragma unroll
-      for (int g = 0; g < CPT; ++g) {
-        float dov[4], qv[4];
-        ld_vec<4>(dov, Dt + (tx + 16 * g) * kPitch + t0);
-        ld_vec<4>(qv, Qt + (tx + 16 * g) * kPitch + t0);
+        for (int a = 0; a < 4; ++a) {
+          ld_vec<4>(pr[a], Ps + (ty * 4 + a) * kPitch + t0);
+          ld_vec<4>(dr[a], Ds + (ty * 4 + a) * kPitch + t0);
+        }
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int gl = 0; gl < DC / 16; ++gl) {
+          const int g = cc * (DC / 16) + gl;
+          float dov[4], qv[4];
+          ld_vec<4>(dov, Dt + (tx + 16 * gl) * kPitch + t0);
+          ld_vec<4>(qv, Qt + (tx + 16 * gl) * kPitch + t0);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            dva[a][g] = fmaf(pr[a][c], dov[c], dva[a][g]);
-            dka[a][g] = fmaf(dr[a][c], qv[c], dka[a][g]);
-          }
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              dva[a][g] = fmaf(pr[a][c], dov[c], dva[a][g]);
+              dka[a][g] = fmaf(dr[a][c], qv[c], dka[a][g]);
+            }
+        }
       }
     }
     if (!diag) {
@@ -248,14 +282,14 @@ __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, 
           wsum[a] += ex2(c2_s[a] - rs[a]) * fsum[a];
           tp += ex2(cmid2 - rs[a]) * fsum[a];
         }
-      if (i > j + 1) {
+      if (i > j + 1 && half == 0) {
         // Tile-pair total: one partial per warp, summed in a fixed order by the dphi kernel.
         tp = group_sum<32>(tp);
         if ((tid & 31) == 0) sc.tb[((size_t(z) * NB + i) * NB + j) * sc.tb_parts + warp] = tp;
       }
       mid = fminf(mid, st.bmin[size_t(z) * NB + i]);
       midl = lse2(midl, st.bl[size_t(z) * NB + i]);
-    } else {
+    } else if (half == 0) {
       // In-tile soft-min gradient of the diagonal tile, one thread per key s: with Z_{s,t} = sum over s < u <= t
       // of 2^{a2_u} carried as L = log2 Z, H(t) = g_st + (Z_{s,t} / Z_{s,t+1}) H(t + 1) and the contribution to
       // u = t is (2^{a2_t} / Z_{s,t}) H(t); DPHI4_t sums the contributions over the keys s < t.
@@ -297,14 +331,16 @@ __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, 
     if (!s_ok[a]) continue;
 #pragma unroll
     for (int g = 0; g < CPT; ++g) {
-      dk[int64_t(s) * A.sdk.t + int64_t(tx + 16 * g) * A.sdk.d] = from_f32<TIn>(dka[a][g] * A.scale);
-      dv[int64_t(s) * A.sdv.t + int64_t(tx + 16 * g) * A.sdv.d] = from_f32<TIn>(dva[a][g]);
+      const int64_t col = half * BT::NC + tx + 16 * g;
+      dk[int64_t(s) * A.sdk.t + col * A.sdk.d] = from_f32<TIn>(dka[a][g] * A.scale);
+      dv[int64_t(s) * A.sdv.t + col * A.sdv.d] = from_f32<TIn>(dva[a][g]);
     }
-    if (tx == 0) {
+    if (tx == 0 && half == 0) {
       A.dpsi[zt + s] = -bh * gs;
       sc.w[zp + s] = ws;
     }
   }
+  if (half != 0) return;
   // dbeta partial of this key tile, reduced in a fixed order.
   dbsum = group_sum<32>(dbsum);
   if ((tid & 31) == 0) red[warp] = dbsum;
@@ -319,15 +355,17 @@ __device__ __forceinline__ void kv_pass(const BwdTiledArgs& A, const Stats& st, 
 // ------------------------------------------------------------------------------------------------- q-pass ----
 // Query tile i: dQ and the soft-min contribution of u in the query's own tile (DPHI2), from
 //   r_t = sum_{s in earlier tiles} g_ts 2^{c_t} / Z_{s,t},  DPHI2_u = sum_{t >= u in tile} 2^{a2_u - c_t} r_t.
+// The columns half * NC .. of dQ (DPHI2 from half 0 only).
 template <typename TIn, int D, bool VEC>
 __device__ __forceinline__ void q_pass(const BwdTiledArgs& A, const Stats& st, const BwdScratch& sc, float* smem,
-                                       int i, int z) {
-  constexpr int CPT = BwdTile<D>::CPT;
+                                       int i, int z, int half) {
+  using BT = BwdTile<D>;
+  constexpr int CPT = BT::CPT, DC = BT::DC, NCH = BT::NCH;
   float* Qt = smem;
   float* Dt = Qt + D * kPitch;
-  float* Kt = Dt + D * kPitch;
-  float* Vt = Kt + D * kPitch;
-  float* Ss = Vt + D * kPitch;  // dS [query][key]; the range-minimum table of the diagonal tile before
+  float* Kt = Dt + D * kPitch;  // one stage of DC columns of the key tile's K and V
+  float* Vt = Kt + DC * kPitch;
+  float* Ss = Vt + DC * kPitch;  // dS [query][key]; the range-minimum table of the diagonal tile before
   float* psis = Ss + kFT * kPitch;
   float* phis = psis + kFT;
   float* sufs = phis + kFT;
@@ -368,34 +406,48 @@ __device__ __forceinline__ void q_pass(const BwdTiledArgs& A, const Stats& st, c
     for (int g = 0; g < CPT; ++g) dqa[a][g] = 0.f;
   float mid = kInf, midl = -kInf;
 
+  // Stages of K and V in the order (first + 1, ..., first), as in the kv-pass.
+  const int first = half * (NCH / BT::NH);
+  auto load_stage = [&](int j, int c) {
+    load_rows<TIn, DC, true, VEC>(Kt, k + int64_t(c) * DC * A.sk.d, A.sk, j, T, 1.f);
+    load_rows<TIn, DC, true, VEC>(Vt, v + int64_t(c) * DC * A.sv.d, A.sv, j, T, 1.f);
+  };
+
   // The diagonal tile first, then the earlier key tiles walking back with mid = min phi over the tiles passed.
   for (int j = i; j >= 0; --j) {
     const bool diag = j == i;
-    __syncthreads();  // the previous key tile's Kt, Vt and Ss are read
-    load_rows<TIn, D, true, VEC>(Kt, k, A.sk, j, T, 1.f);
-    load_rows<TIn, D, true, VEC>(Vt, v, A.sv, j, T, 1.f);
-    if (tid < kFT) {
-      const int s = j * kFT + tid;
-      psis[tid] = s < T ? A.psi[zt + s] : 0.f;
-      phis[tid] = s < T ? A.phi[zt + s] : kInf;
-      sufs[tid] = st.suf[zp + s];
-      sufls[tid] = st.sufl[zp + s];
-    }
-    __syncthreads();
-    if (diag) {
-      // Range-minimum table: Ss[t][s] = min phi over (s, t] for s < t, one thread per query walking its keys down.
-      if (tid < kFT) {
-        float x = kInf;
-        float* row = Ss + tid * kPitch;
-        for (int s = tid - 1; s >= 0; --s) {
-          x = fminf(x, phis[s + 1]);
-          row[s] = x;
-        }
+    float sS[4][4], sP[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sS[a][c] = sP[a][c] = 0.f;
+#pragma unroll 1
+    for (int kk = 0; kk < NCH; ++kk) {
+      const int c = (first + 1 + kk) % NCH;
+      __syncthreads();  // the previous stage (and, at kk = 0, the previous key tile's Ss) are read
+      load_stage(j, c);
+      if (kk == 0 && tid < kFT) {
+        const int s = j * kFT + tid;
+        psis[tid] = s < T ? A.psi[zt + s] : 0.f;
+        phis[tid] = s < T ? A.phi[zt + s] : kInf;
+        sufs[tid] = st.suf[zp + s];
+        sufls[tid] = st.sufl[zp + s];
       }
       __syncthreads();
+      if (kk == 0 && diag) {
+        // Range-minimum table: Ss[t][s] = min phi over (s, t] for s < t, one thread per query walking its keys down.
+        if (tid < kFT) {
+          float x = kInf;
+          float* row = Ss + tid * kPitch;
+          for (int s = tid - 1; s >= 0; --s) {
+            x = fminf(x, phis[s + 1]);
+            row[s] = x;
+          }
+        }
+        __syncthreads();
+      }
+      score_blocks<DC>(sS, sP, Qt + c * DC * kPitch, Kt, Dt + c * DC * kPitch, Vt, ty, tx);
     }
-    float sS[4][4], sP[4][4];
-    score_blocks<D>(sS, sP, Qt, Kt, Dt, Vt, ty, tx);
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
       const int tl = ty * 4 + a;
@@ -430,20 +482,29 @@ __device__ __forceinline__ void q_pass(const BwdTiledArgs& A, const Stats& st, c
       *reinterpret_cast<float4*>(Ss + (ty * 4 + a) * kPitch + tx * 4) =
           make_float4(sP[a][0], sP[a][1], sP[a][2], sP[a][3]);
     __syncthreads();
-    // dQ += dS K over the tile's 64 keys.
+    // dQ += dS K over the tile's 64 keys, one stage of DC columns at a time.
+#pragma unroll
+    for (int cc = 0; cc < CPT / (DC / 16); ++cc) {
+      if (cc > 0) {
+        __syncthreads();
+        load_stage(j, first + cc);
+        __syncthreads();
+      }
 #pragma unroll 2
-    for (int s0 = 0; s0 < kFT; s0 += 4) {
-      float dr[4][4];
+      for (int s0 = 0; s0 < kFT; s0 += 4) {
+        float dr[4][4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) ld_vec<4>(dr[a], Ss + (ty * 4 + a) * kPitch + s0);
+        for (int a = 0; a < 4; ++a) ld_vec<4>(dr[a], Ss + (ty * 4 + a) * kPitch + s0);
 #pragma unroll
-      for (int g = 0; g < CPT; ++g) {
-        float kv[4];
-        ld_vec<4>(kv, Kt + (tx + 16 * g) * kPitch + s0);
+        for (int gl = 0; gl < DC / 16; ++gl) {
+          const int g = cc * (DC / 16) + gl;
+          float kv[4];
+          ld_vec<4>(kv, Kt + (tx + 16 * gl) * kPitch + s0);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+          for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) dqa[a][g] = fmaf(dr[a][c], kv[c], dqa[a][g]);
+            for (int c = 0; c < 4; ++c) dqa[a][g] = fmaf(dr[a][c], kv[c], dqa[a][g]);
+        }
       }
     }
     if (!diag) {
@@ -460,8 +521,9 @@ __device__ __forceinline__ void q_pass(const BwdTiledArgs& A, const Stats& st, c
     if (!t_ok[a]) continue;
 #pragma unroll
     for (int g = 0; g < CPT; ++g)
-      dq[int64_t(t) * A.sdq.t + int64_t(tx + 16 * g) * A.sdq.d] = from_f32<TIn>(dqa[a][g] * A.scale);
+      dq[int64_t(t) * A.sdq.t + int64_t(half * BT::NC + tx + 16 * g) * A.sdq.d] = from_f32<TIn>(dqa[a][g] * A.scale);
   }
+  if (half != 0) return;
   if (tx == 0)
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
@@ -485,12 +547,13 @@ template <typename TIn, int D, bool VEC>
 __global__ void __launch_bounds__(kFThreads, D <= 64 ? 2 : 1)
 simt_bwd_tiled_kernel(const BwdTiledArgs A, const Stats st, const BwdScratch sc) {
   extern __shared__ __align__(16) float smem[];
-  const int z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (2 NB, H, B)
-  const int x = blockIdx.x >> 1;
+  constexpr int NH = BwdTile<D>::NH;
+  const int z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (2 NH NB, H, B)
+  const int half = (blockIdx.x >> 1) % NH, x = blockIdx.x / (2 * NH);
   if (blockIdx.x & 1)
-    q_pass<TIn, D, VEC>(A, st, sc, smem, A.NB - 1 - x, z);
+    q_pass<TIn, D, VEC>(A, st, sc, smem, A.NB - 1 - x, z, half);
   else
-    kv_pass<TIn, D, VEC>(A, st, sc, smem, x, z);
+    kv_pass<TIn, D, VEC>(A, st, sc, smem, x, z, half);
 }
 
 template <typename TIn, int D>
@@ -513,7 +576,7 @@ cudaError_t launch(const FpaBwdArgs& a, const Dims& d, const Stats& st, const Bw
   A.H = d.H, A.T = d.T, A.NB = d.NB;
   A.scale = float(1.0 / sqrt(double(d.D)));
   A.il2 = kLog2e / a.tau;
-  fn<<<dim3(2 * d.NB, d.H, d.B), kFThreads, smem, s>>>(A, st, sc);
+  fn<<<dim3(2 * BwdTile<D>::NH * d.NB, d.H, d.B), kFThreads, smem, s>>>(A, st, sc);
   return cudaGetLastError();
 }
 
@@ -524,13 +587,12 @@ cudaError_t launch_d(const FpaBwdArgs& a, const Dims& d, const Stats& st, const 
     case 32: return launch<TIn, 32>(a, d, st, sc, s);
     case 64: return launch<TIn, 64>(a, d, st, sc, s);
     case 128: return launch<TIn, 128>(a, d, st, sc, s);
+    case 256: return launch<TIn, 256>(a, d, st, sc, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
-
-bool simt_bwd_tiled_supports(int D) { return D <= 128; }
 
 cudaError_t simt_bwd_tiled(const FpaBwdArgs& a, const Dims& d, const Stats& st, const BwdScratch& sc,
                            cudaStream_t s) {

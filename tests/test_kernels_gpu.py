@@ -274,6 +274,22 @@ def test_strided_qkv_views():
     check(run_kernel(q, k, v, phi, psi, beta, do), run_oracle(q, k, v, phi, psi, beta, do), torch.float16)
 
 
+@pytest.mark.parametrize("D", [64, 256])
+def test_ffma_path_reads_strided_operands(D):
+    """fp32 q, k, v and dO stored [B, H, D, T] and passed as transposed views (column stride T, so every tile load
+    takes the scalar path; at D = 256 the streamed tiles start at column offsets 64, 128, 192): the same result as
+    the oracle and, bit for bit, as contiguous copies."""
+    need_gpu()
+    B, H, T = 1, 2, 300
+    q, k, v, phi, psi, beta, do = make_inputs(B, H, T, D, seed=70 + D, dtype=torch.float32)
+    tq, tk, tv, tdo = (x.transpose(-1, -2).contiguous().transpose(-1, -2) for x in (q, k, v, do))
+    assert tq.stride()[-1] == T
+    kern = run_kernel(tq, tk, tv, phi, psi, beta, tdo)
+    check(kern, run_oracle(q, k, v, phi, psi, beta, do), torch.float32)
+    dense = run_kernel(q, k, v, phi, psi, beta, do)
+    assert all(torch.equal(x, y) for x, y in zip(kern, dense))
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_keys_and_values_shared_across_heads(dtype):
     """k and v given as one head broadcast over all heads (expand, head stride 0): the result equals the oracle's on
