@@ -38,7 +38,8 @@ extern "C" {
  * dpsi and dbeta are always float32. */
 enum FpaDtype { FPA_DTYPE_F16 = 0, FPA_DTYPE_F32 = 1 };
 
-/* Which kernels to run. AUTO picks the tensor-core (tcgen05) kernels for fp16 and the FFMA kernels for fp32. */
+/* Which kernels to run. AUTO picks the tensor-core (tcgen05) kernels for fp16 with D <= 128 and the FFMA kernels
+   for fp32 and for D = 256. */
 enum FpaPath { FPA_PATH_AUTO = 0, FPA_PATH_SIMT = 1, FPA_PATH_TENSOR = 2 };
 
 enum FpaStatus {
