@@ -1,8 +1,8 @@
 // Register-tiled FFMA backward of the FPA operator: the fp32 path, fp16 with D = 256 (which the tensor-core kernels
 // do not cover) and fp16 wherever the FFMA path is asked for. One launch runs both passes of the reference's backward
-// (kernel.py:178-265 kv-pass, 287-340 q-pass) as interleaved CTAs: even blockIdx.x are kv-pass CTAs of key tiles
-// 0, 1, ..., odd ones q-pass CTAs of query tiles NB - 1, NB - 2, ..., so both start with their longest tiles and
-// their tails overlap.
+// (kernel.py:178-265 kv-pass, 287-340 q-pass) as interleaved CTAs of a 1-D grid, tile rank major over all heads: kv-pass
+// CTAs of key tiles 0, 1, ... alternate with q-pass CTAs of query tiles NB - 1, NB - 2, ..., so that the hardware's
+// in-order dispatch starts the longest tiles of every head first and the tails of the two passes overlap.
 //
 // Work split (256 threads as 16 x 16, tiles of 64 positions): thread (ty, tx) owns
 //   * of the score tiles (S^T, dP^T in the kv-pass, S, dP in the q-pass) the 4 x 4 block of rows 4 ty .. 4 ty + 3
@@ -548,9 +548,10 @@ __global__ void __launch_bounds__(kFThreads, D <= 64 ? 2 : 1)
 simt_bwd_tiled_kernel(const BwdTiledArgs A, const Stats st, const BwdScratch sc) {
   extern __shared__ __align__(16) float smem[];
   constexpr int NH = BwdTile<D>::NH;
-  const int z = blockIdx.z * gridDim.y + blockIdx.y;  // grid (2 NH NB, H, B)
-  const int half = (blockIdx.x >> 1) % NH, x = blockIdx.x / (2 * NH);
-  if (blockIdx.x & 1)
+  const int BH = int(gridDim.x) / (2 * NH * A.NB);  // grid: 2 NH NB units (rank major) x B H heads
+  const int u = int(blockIdx.x) / BH, z = int(blockIdx.x) % BH;
+  const int half = (u >> 1) % NH, x = u / (2 * NH);
+  if (u & 1)
     q_pass<TIn, D, VEC>(A, st, sc, smem, A.NB - 1 - x, z, half);
   else
     kv_pass<TIn, D, VEC>(A, st, sc, smem, x, z, half);
@@ -576,7 +577,7 @@ cudaError_t launch(const FpaBwdArgs& a, const Dims& d, const Stats& st, const Bw
   A.H = d.H, A.T = d.T, A.NB = d.NB;
   A.scale = float(1.0 / sqrt(double(d.D)));
   A.il2 = kLog2e / a.tau;
-  fn<<<dim3(2 * BwdTile<D>::NH * d.NB, d.H, d.B), kFThreads, smem, s>>>(A, st, sc);
+  fn<<<dim3(2 * BwdTile<D>::NH * d.NB * d.B * d.H), kFThreads, smem, s>>>(A, st, sc);
   return cudaGetLastError();
 }
 

@@ -52,8 +52,11 @@ simt_fwd_tiled_kernel(const TIn* __restrict__ q, Str4 sq, const TIn* __restrict_
   float* sufs = psis + kFT;
   float* phis = sufs + kFT;
 
-  const int i = NB - 1 - int(blockIdx.x);  // longest query tiles first (kernel.py:108)
-  const int z = blockIdx.z * gridDim.y + blockIdx.y, b = z / H, h = z % H;  // grid (NB, H, B)
+  // 1-D grid of NB * B * H CTAs, tile rank major: the longest query tiles of every head first (kernel.py:108 orders
+  // a head's tiles the same way), so that the hardware's in-order dispatch approximates longest-first scheduling.
+  const int BH = int(gridDim.x) / NB;
+  const int i = NB - 1 - int(blockIdx.x) / BH;
+  const int z = int(blockIdx.x) % BH, b = z / H, h = z % H;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const size_t TP = size_t(NB) * kFT, zt = size_t(z) * T, zp = size_t(z) * TP;
   const float betal = beta[h] * kLog2e;
@@ -225,7 +228,7 @@ cudaError_t launch_tiled(const FpaFwdArgs& a, const Dims& d, const Stats& st, cu
     const cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(fn), int(smem));
     if (e != cudaSuccess) return e;
   }
-  fn<<<dim3(d.NB, d.H, d.B), kFThreads, smem, s>>>(
+  fn<<<dim3(d.NB * d.B * d.H), kFThreads, smem, s>>>(
       (const TIn*)a.q, str4(a.q_stride), (const TIn*)a.k, str4(a.k_stride), (const TIn*)a.v, str4(a.v_stride),
       a.phi, a.psi, a.beta, st, (TIn*)a.o, str4(a.o_stride), a.lse, d.H, d.T, d.NB,
       float(1.0 / sqrt(double(D))) * kLog2e);
