@@ -52,8 +52,10 @@ __device__ __forceinline__ void load4(float (&x)[4], const TIn* base, Str4 st, i
 // TRANS, transposed to [D][kPitch] (thread -> (row, four columns), consecutive threads on consecutive rows, so the
 // scalar stores hit consecutive banks); otherwise row-major [64][D] (consecutive threads on consecutive columns).
 // Every load of a batch is issued before the first store, so one memory latency covers the batch.
+// `tid` is the thread's index among the kFThreads threads that share the load.
 template <typename TIn, int D, bool TRANS, bool VEC>
-__device__ __forceinline__ void load_rows(float* dst, const TIn* base, Str4 st, int j, int T, float scale) {
+__device__ __forceinline__ void load_rows(float* dst, const TIn* base, Str4 st, int j, int T, float scale,
+                                          int tid = threadIdx.x) {
   constexpr int NCH = kFT * D / 4 / kFThreads;  // chunks of four per thread (D / 16)
   constexpr int BATCH = NCH < 8 ? NCH : 8;
 #pragma unroll
@@ -61,13 +63,13 @@ __device__ __forceinline__ void load_rows(float* dst, const TIn* base, Str4 st, 
     float x[BATCH][4];
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
-      const int e = threadIdx.x + (c0 + q) * kFThreads;
+      const int e = tid + (c0 + q) * kFThreads;
       const int r = TRANS ? e % kFT : e / (D / 4), d0 = TRANS ? (e / kFT) * 4 : (e % (D / 4)) * 4;
       load4<TIn, VEC>(x[q], base, st, j * kFT + r, d0, j * kFT + r < T);
     }
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
-      const int e = threadIdx.x + (c0 + q) * kFThreads;
+      const int e = tid + (c0 + q) * kFThreads;
       const int r = TRANS ? e % kFT : e / (D / 4), d0 = TRANS ? (e / kFT) * 4 : (e % (D / 4)) * 4;
       if (TRANS) {
 #pragma unroll
