@@ -52,6 +52,8 @@ def parse(argv=None):
     ap.add_argument("--shape", default="4,12,2048,64", help="B,H,T,D in total (strong) or per rank (weak)")
     ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU reference sample")
+    ap.add_argument("--e2e-pieces", type=int, default=4,
+                    help="at least this many pieces in the pipelined end-to-end step (several sequences per GPU)")
     ap.add_argument("--no-config4", action="store_true", help="skip the configuration-4 measurement")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's own Triton kernels (installed under baseline/_ref)")
@@ -490,11 +492,15 @@ def triton_reference(inputs, flush):
 
 
 # ------------------------------------------------------------------------------------------------ native ----
-def e2e_chunks(Bs, Hs):
-    """Pieces of a [Bs, Hs] shard the end-to-end step pipelines: each sequence when there are several, else up to
-    four groups of heads of the one sequence. Returns [(b, h0, h1)]."""
+def e2e_chunks(Bs, Hs, want=4):
+    """Pieces of a [Bs, Hs] shard the end-to-end step pipelines. Several sequences: each sequence, cut into equal
+    groups of heads until there are at least `want` pieces; one sequence: up to four groups of heads (a piece of one
+    or two heads is latency-bound on the GPU). At configuration 2, 4 and 8 pieces measured the same within the
+    run-to-run spread of the host copies (1.57-1.76 ms per step on one B200). Returns [(b, h0, h1)]."""
     if Bs > 1:
-        return [(b, 0, Hs) for b in range(Bs)]
+        g = next((c for c in range(1, Hs + 1) if Hs % c == 0 and Bs * c >= want), Hs)
+        per = Hs // g
+        return [(b, c * per, (c + 1) * per) for b in range(Bs) for c in range(g)]
     n = max(c for c in range(1, 5) if Hs % c == 0)
     per = Hs // n
     return [(0, c * per, (c + 1) * per) for c in range(n)]
@@ -625,7 +631,7 @@ def main(argv=None):
     # copy-in stream, two compute streams and a copy-out stream, so the copies of one piece overlap the compute of
     # the others (PCIe is full duplex). Captured in a CUDA graph like the device step (the pipelined step is
     # host-bound when enqueued eagerly).
-    chunks = e2e_chunks(Bs, Hs)
+    chunks = e2e_chunks(Bs, Hs, args.e2e_pieces)
     esz = q.element_size()
     host_pack, layouts = [], []
     for (bi, h0, h1) in chunks:
@@ -687,13 +693,10 @@ def main(argv=None):
                     hst[bi:bi + 1, h0:h1].copy_(d, non_blocking=True)
         for cs in s_comp:
             main_s.wait_stream(cs)
-        # dbeta of the shard: a sum over the sequences' parts, or the groups of heads side by side.
-        if Bs > 1:
-            dbeta_dev = dbetas[0][2]
-            for _, _, g_ in dbetas[1:]:
-                dbeta_dev = dbeta_dev + g_
-        else:
-            dbeta_dev = torch.cat([g_ for _, _, g_ in dbetas])
+        # dbeta of the shard: each group of heads summed over the sequences, in piece order.
+        dbeta_dev = torch.zeros(Hs, dtype=torch.float32, device=device)
+        for h0, h1, g_ in dbetas:
+            dbeta_dev[h0:h1] += g_
         ev_b = torch.cuda.Event()
         ev_b.record(main_s)
         with torch.cuda.stream(s_out):
@@ -708,6 +711,14 @@ def main(argv=None):
                                                          args.warmup, flush)))
     e2e_graphed = e2e_graph is not None
     del e2e_graph
+    # The pipelined pieces compute what the device step does: their gradients read back to the host against the
+    # device step's (fp16 rounding of a different key-range split and summation order at most).
+    torch.cuda.synchronize(device)
+
+    def rel_diff(host_t, dev_t):
+        ref = dev_t.detach().float().cpu()
+        return float((host_t.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    e2e_check = max(rel_diff(h_, l_.grad) for h_, l_ in zip(host_out[1:] + [host_dbeta], leaves))
     sync_all()
 
     # 5. Configuration 4 (B1 H16 T16383 D128 fp16), its heads split the same way.
@@ -828,7 +839,8 @@ def main(argv=None):
                     "result_read_back": "o and all six gradients (dq, dk, dv, dphi, dpsi, dbeta) into pinned host "
                                         "buffers",
                     "pipeline": f"{len(chunks)} pieces, one packed pinned block each; copy-in / 2 compute / copy-out "
-                                "streams"},
+                                "streams",
+                    "grads_rel_diff_vs_device_step": e2e_check},
             "weak_scaling": weak,
             "config4": cfg4,
             "triton_reference": triton_ref,
