@@ -33,6 +33,22 @@ def test_library_exports_every_declared_symbol():
     assert lib.fpa_struct_size(1) == ctypes.sizeof(_lib.FpaBwdArgs)
 
 
+def test_ffma_backward_workspace_holds_eight_tb_partials_per_tile_pair():
+    """The FFMA path's backward workspace (tiles of 64): the status block, the field statistics, delta, W, DPHI2,
+    DPHI4, the TB array with eight per-warp partial sums per tile pair (the register-tiled kv-pass writes one per
+    warp), dbeta partials and the part-3 scratch, every array 256-byte aligned."""
+    lib = _lib.load()
+    a256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    for B, H, T, D in [(2, 8, 1000, 64), (1, 3, 65, 256), (1, 1, 1, 16), (4, 2, 4096, 128)]:
+        NB = (T + 63) // 64
+        TP, BH = NB * 64, B * H
+        stats = 4 * a256(BH * TP * 4) + 2 * a256(BH * NB * 4)
+        scratch = 4 * a256(BH * TP * 4) + a256(BH * NB * NB * 8 * 4) + 2 * a256(BH * NB * 4)
+        want = 256 + stats + scratch
+        assert lib.fpa_bwd_workspace_bytes(_lib.DTYPE_F32, B, H, T, D, _lib.PATH_AUTO) == want, (B, H, T, D)
+        assert lib.fpa_bwd_workspace_bytes(_lib.DTYPE_F16, B, H, T, D, _lib.PATH_SIMT) == want, (B, H, T, D)
+
+
 def test_workspace_queries_and_argument_errors():
     lib = _lib.load()
     assert lib.fpa_fwd_workspace_bytes(_lib.DTYPE_F16, 4, 12, 2048, 64, 0) > 0

@@ -38,3 +38,17 @@ def test_reference_arm_other_ranks_print_nothing():
     r = _run({"RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_e2e_pieces_cover_every_head_once():
+    """The pipelined end-to-end step's pieces: every (sequence, head) of the shard in exactly one piece, equal groups
+    of heads, at least the asked-for number of pieces when there are several sequences."""
+    sys.path.insert(0, ROOT)
+    import bench
+    for Bs, Hs, want in [(4, 12, 4), (4, 12, 8), (2, 12, 4), (1, 12, 4), (1, 6, 4), (1, 7, 4), (8, 12, 4), (3, 5, 8)]:
+        pieces = bench.e2e_chunks(Bs, Hs, want)
+        seen = [(b, h) for b, h0, h1 in pieces for h in range(h0, h1)]
+        assert sorted(seen) == [(b, h) for b in range(Bs) for h in range(Hs)], (Bs, Hs, want)
+        assert len({h1 - h0 for _, h0, h1 in pieces}) == 1
+        if Bs > 1:
+            assert len(pieces) >= min(want, Bs * Hs)
